@@ -1,0 +1,166 @@
+/*
+ * kea_lowbit.h - C ABI of the B200 (sm_100a) low-bit GEMM library `libkea_lowbit.so`.
+ *
+ * The library multiplies INT8 activation parts by 1-bit (sign) or 2-bit (ternary) packed weights on the
+ * tcgen05 tensor cores (kind::i8, INT32 accumulators in tensor memory) and applies the kea-kernels FP32
+ * epilogue. Every entry point takes plain device pointers, sizes and a CUDA stream passed as `void *`
+ * (a `cudaStream_t`; NULL is the legacy default stream). Nothing here allocates device memory or
+ * synchronizes the host, except `kea_lowbit_read_error`, which says so.
+ *
+ * Reference interfaces replaced (paths inside the kea-kernels project):
+ *   - the NVRTC launch path `_nvrtc.load(...).launch(...)` (src/kea_kernels/_nvrtc.py:116-137), which the
+ *     Python layer called with 16 typed kernel arguments (src/kea_kernels/binary/layer.py:196-201);
+ *   - the Triton launches of `_quantize` / `_int8_dot` / `_finish` (src/kea_kernels/ternary/fused_kernels.py:
+ *     139-160; src/kea_kernels/ternary/encoder4.py:120-148).
+ * All status codes are `int`; 0 is success.
+ */
+#ifndef KEA_LOWBIT_H
+#define KEA_LOWBIT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KEA_LOWBIT_VERSION 1
+
+/* Status codes. The Python layer maps 1-4 to ValueError and 5-8 to RuntimeError, as the reference raises
+ * ValueError for argument errors (src/kea_kernels/binary/layer.py:66-78,188-189) and RuntimeError for a failed
+ * launch (src/kea_kernels/_nvrtc.py:123-124). */
+enum {
+    KEA_OK = 0,
+    KEA_ERR_INVALID_VALUE = 1,   /* a NULL pointer, a non-positive size, an unknown enum value */
+    KEA_ERR_ALIGNMENT = 2,       /* a pointer or stride that is not 16-byte aligned where TMA needs it */
+    KEA_ERR_UNSUPPORTED = 3,     /* a valid request outside what the kernels implement (e.g. parts = 4) */
+    KEA_ERR_INVALID_CODES = 4,   /* prepare: nonzero tail bits, or the unused ternary pattern 0b11 */
+    KEA_ERR_CUDA = 5,            /* a CUDA runtime / driver call failed (launch, attribute, tensor map) */
+    KEA_ERR_NO_DEVICE = 6,       /* the current device is not an sm_100 (B200-class) GPU */
+    KEA_ERR_DEVICE_TIMEOUT = 7,  /* a kernel's bounded wait expired and the kernel returned early */
+    KEA_ERR_CAPTURE = 8          /* first use of a device inside a CUDA-graph capture (one-time set-up needed) */
+};
+
+/* Output element type of y. FP32 is the reference's output (src/kea_kernels/binary/kernels.py:315-325);
+ * FP16 is round-to-nearest-even of the same FP32 value. */
+enum { KEA_OUT_F32 = 0, KEA_OUT_F16 = 1 };
+
+/* kea_lowbit_gemm flags. SILU and ORDER1 are the reference's `flags` bits 0 and 1
+ * (src/kea_kernels/binary/kernels.py:73-84: bit 0 SiLU epilogue, bit 1 the other P = 2 contraction order). */
+enum {
+    KEA_FLAG_SILU = 1,
+    KEA_FLAG_ORDER1 = 2,
+    KEA_FLAG_PDL = 4            /* launch with programmatic dependent launch (overlap with the previous kernel) */
+};
+
+/* Device error word bits (written by kernels into `error_word`, or into the library's own device word). */
+enum {
+    KEA_DEVERR_TIMEOUT = 1,      /* an mbarrier wait exceeded its bound */
+    KEA_DEVERR_TAIL_BITS = 2,    /* prepare: nonzero padding bits past K */
+    KEA_DEVERR_TERNARY_11 = 4    /* prepare: a 2-bit field holds the unused pattern 0b11 */
+};
+
+/*
+ * One low-bit GEMM:
+ *   acc_c[m, n] = sum_k q_c[m, k] * w[n, k]            (exact INT32; w in {-1,+1} or {-1,0,+1})
+ *   r           = comb_P(acc, qs)                       (P = parts; see below)
+ *   y[m, n]     = bias ? fma(r, alpha[n], bias[n]) : r * alpha[n],   then SiLU if KEA_FLAG_SILU
+ * comb_1 = RN(float(acc_0) * s_0); comb_2 = fma(acc_0, s_0, RN(acc_1 * s_1)) (ORDER1: fma(acc_1, s_1,
+ * RN(acc_0 * s_0))); comb_3 = fma(acc_2, s_2, comb_2). Every operation is one IEEE FP32 rounding, as in
+ * the reference's comb<P> / epilogue_p (src/kea_kernels/binary/kernels_parts.py:30-45).
+ *
+ * Replaces Int8MmaLayer.dot / dot_parts -> b1_dot (src/kea_kernels/binary/layer.py:182-209;
+ * src/kea_kernels/binary/layer_parts.py:112-130; src/kea_kernels/binary/kernels.py:556-564) and the ternary
+ * _int8_dot + _finish launches (src/kea_kernels/ternary/fused_kernels.py:53-120,139-160).
+ */
+typedef struct KeaGemmDesc {
+    const int8_t *q;          /* int8 [parts][m][ldq]; k columns are read, columns >= k are ignored */
+    int64_t q_part_stride;    /* elements between parts (multiple of 16 when parts > 1) */
+    int32_t ldq;              /* row stride in elements, multiple of 16 (q must be 16-byte aligned) */
+    int32_t parts;            /* 1, 2 or 3 residual INT8 parts */
+    const float *qs;          /* FP32 [parts][m] per-token part scales */
+    int64_t qs_part_stride;   /* elements between parts of qs */
+    const uint8_t *panels;    /* weights prepared by kea_lowbit_prepare */
+    int32_t wbits;            /* 1 (signs) or 2 (ternary) */
+    int32_t n, k;             /* output channels, reduction length */
+    const float *alpha;       /* FP32 [n] per-channel weight scale */
+    const float *bias;        /* FP32 [n] or NULL */
+    void *y;                  /* [m][ldy] FP32 or FP16 */
+    int64_t ldy;              /* row stride of y in elements */
+    int32_t y_dtype;          /* KEA_OUT_F32 or KEA_OUT_F16 */
+    int32_t *acc;             /* optional INT32 [parts][m][ld_acc] accumulators, or NULL */
+    int64_t ld_acc;           /* row stride of acc in elements */
+    int64_t acc_part_stride;  /* elements between parts of acc */
+    int32_t m;                /* tokens (rows of q and y); 0 is a no-op */
+    int32_t flags;            /* KEA_FLAG_* */
+    int32_t token_tile;       /* 0: dispatch table; else tokens per CTA (multiple of 16, <= 256) */
+    int32_t splits;           /* 0: dispatch table; else split-K ways = cluster size (1..16) */
+    int32_t stages;           /* 0: dispatch table; else pipeline stages (2..8) */
+    uint32_t *error_word;     /* device word OR-ed with KEA_DEVERR_* bits, or NULL for the library's own */
+} KeaGemmDesc;
+
+/* Tile configuration picked for a shape (the M-bucketed split-K dispatch table). */
+typedef struct KeaGemmConfig {
+    int32_t token_tile;       /* tokens per CTA (tcgen05 N dimension) */
+    int32_t splits;           /* K split across a thread-block cluster of this size */
+    int32_t stages;           /* smem pipeline depth (k128 blocks in flight) */
+    int32_t smem_bytes;       /* dynamic shared memory per CTA */
+} KeaGemmConfig;
+
+int kea_lowbit_gemm(const KeaGemmDesc *desc, void *stream);
+
+/* The configuration kea_lowbit_gemm uses when token_tile / splits / stages are 0.
+ * Replaces configs.choose (src/kea_kernels/binary/configs.py:53-58). */
+int kea_lowbit_choose_config(int32_t m, int32_t n, int32_t k, int32_t wbits, int32_t parts, KeaGemmConfig *out);
+
+/* Bytes of the prepared panel layout: ceil(n/128) * ceil(k/128) * wbits * 2048.
+ * Replaces kernels.fragment_bytes (src/kea_kernels/binary/kernels.py:726-727). */
+size_t kea_lowbit_panel_bytes(int32_t wbits, int32_t n, int32_t k);
+
+/* Re-lays export codes (uint8 [n][ceil(k*wbits/8)] on the device; parakeet-binary-v1 LSB-first signs or
+ * parakeet-ternary-v1 2-bit fields) into panels of kea_lowbit_panel_bytes bytes, and checks the codes:
+ * nonzero tail bits or a 0b11 field set KEA_DEVERR_* bits in error_word (NULL: the library's own word).
+ * Replaces relayout(unpack_bits(codes)) in Int8MmaLayer.prepare (src/kea_kernels/binary/kernels.py:730-742;
+ * src/kea_kernels/binary/layer.py:37-56) and PackedLinear's word re-layout (src/kea_kernels/ternary/runtime.py:
+ * 33-35). */
+int kea_lowbit_prepare(const uint8_t *codes, int32_t wbits, int32_t n, int32_t k, uint8_t *panels,
+                       uint32_t *error_word, void *stream);
+
+/* Residual INT8 quantizer:
+ *   x[m, kk] at x + (m / t) * xb + (m % t) * xt + kk * xk (elements);
+ *   optional LayerNorm over k (norm_weight / norm_bias FP32 [k]), optional input SiLU;
+ *   for each part c: s_c = max(amax / 127, 1e-30), q = rint(x / s_c), x -= q * s_c.
+ * Division is IEEE round-to-nearest (the CPU oracle reproduces it bit for bit).
+ * Replaces b1_quantize (src/kea_kernels/binary/kernels.py:567-617; layer.py:154-165) and the Triton
+ * _quantize (src/kea_kernels/ternary/fused_kernels.py:31-50). */
+typedef struct KeaQuantizeDesc {
+    const float *x;
+    int64_t xb, xt, xk;       /* strides in elements (see above) */
+    int32_t t;                /* rows per batch entry (>= 1) */
+    int32_t m, k, parts;
+    int8_t *q;                /* int8 [parts][m][ldq], columns k..ldq-1 written as 0 */
+    int64_t q_part_stride;
+    int32_t ldq;
+    float *qs;                /* FP32 [parts][m] */
+    int64_t qs_part_stride;
+    const float *norm_weight; /* NULL: no LayerNorm */
+    const float *norm_bias;
+    float eps;
+    int32_t flags;            /* KEA_QUANT_INPUT_SILU */
+} KeaQuantizeDesc;
+
+enum { KEA_QUANT_INPUT_SILU = 1 };
+
+int kea_lowbit_quantize(const KeaQuantizeDesc *desc, void *stream);
+
+/* Reads and clears the library's own device error word on the current device. Synchronizes the device. */
+int kea_lowbit_read_error(uint32_t *out);
+
+const char *kea_lowbit_status_string(int status);
+int kea_lowbit_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KEA_LOWBIT_H */

@@ -1,0 +1,152 @@
+// ptx.cuh - inline-PTX helpers for sm_100a: mbarriers, TMA / bulk copies, tcgen05 (TMEM, MMA), clusters.
+// Written against the public PTX ISA (sm_100a). Every wait on an mbarrier is bounded by a clock budget so a
+// kernel can report a timeout instead of hanging the GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+
+namespace kea {
+
+#define KEA_DEVI __device__ __forceinline__
+
+KEA_DEVI uint32_t smem_u32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+// ---- mbarrier ------------------------------------------------------------------------------------------
+KEA_DEVI void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+KEA_DEVI void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+KEA_DEVI void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+KEA_DEVI bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// Waits for phase `parity` of the barrier; false when `budget` SM clocks pass first.
+KEA_DEVI bool mbar_wait(uint32_t bar, uint32_t parity, long long budget) {
+    if (mbar_test(bar, parity)) return true;
+    const long long start = clock64();
+    while (!mbar_test(bar, parity)) {
+        if (clock64() - start > budget) return false;
+    }
+    return true;
+}
+KEA_DEVI void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA / tcgen05) accesses.
+KEA_DEVI void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---- copies into shared memory ----------------------------------------------------------------------------
+// 3-D tiled TMA load (no multicast) completing on an mbarrier of this CTA.
+KEA_DEVI void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(dst), "l"(map), "r"(bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
+KEA_DEVI void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+KEA_DEVI void prefetch_tensormap(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// ---- tcgen05: tensor memory and the 5th-generation MMA -------------------------------------------------------
+KEA_DEVI void tmem_alloc(uint32_t slot, uint32_t cols) {  // whole warp
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(cols) : "memory");
+}
+KEA_DEVI void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+KEA_DEVI void tmem_dealloc(uint32_t taddr, uint32_t cols) {  // whole warp
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+KEA_DEVI void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+KEA_DEVI void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, signed INT8 inputs, INT32 accumulators.
+KEA_DEVI void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives once on `bar` when every tcgen05.mma this thread issued before it has completed.
+KEA_DEVI void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// 32 lanes x 16 consecutive 32-bit columns: thread i of the warp gets lane (base lane + i).
+KEA_DEVI void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+KEA_DEVI void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major operand stored in the 128-byte swizzle layout:
+// rows of 128 bytes, 8-row (1024 B) swizzle atoms stacked along M/N (stride 1024 B), atom base 1024-aligned.
+// Fields: start address >> 4 [0,14), leading byte offset >> 4 [16,30) (unused for this layout: 1),
+// stride byte offset >> 4 [32,46), version 1 [46,48), layout type 2 = 128-byte swizzle [61,64).
+KEA_DEVI uint64_t sw128_kmajor_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::i8: D = S32 [4,6), A = B = signed 8-bit [7,10) / [10,13), both K-major,
+// N >> 3 at [17,23), M >> 4 at [24,29).
+__host__ __device__ constexpr uint32_t idesc_i8(uint32_t m, uint32_t n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// ---- clusters ----------------------------------------------------------------------------------------------
+KEA_DEVI uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+KEA_DEVI void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+KEA_DEVI uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+KEA_DEVI int ld_cluster_s32(uint32_t addr) {
+    int v;
+    asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+// ---- programmatic dependent launch --------------------------------------------------------------------------
+KEA_DEVI void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+KEA_DEVI void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- exact FP32 epilogue pieces ------------------------------------------------------------------------------
+// SiLU as y / (2^(-y * log2(e)) + 1) with the hardware ex2.approx and div.full instructions, the instruction
+// sequence the kea-kernels epilogue uses for its activation.
+KEA_DEVI float silu_approx(float y) {
+    float e, r;
+    const float t = __fmul_rn(-y, 1.4426950408889634f);
+    asm("ex2.approx.f32 %0, %1;" : "=f"(e) : "f"(t));
+    const float d = __fadd_rn(e, 1.0f);
+    asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(y), "f"(d));
+    return r;
+}
+
+}  // namespace kea

@@ -1,0 +1,122 @@
+"""ctypes binding of libkea_lowbit.so, the sm_100a C-ABI library (include/kea_lowbit.h).
+
+This module replaces the reference's NVRTC launch runtime (src/kea_kernels/_nvrtc.py:50-149): there is no run-time
+compilation; the library is built ahead of time by kea-kernels_b200/build.py and loaded here. Status codes map to
+ValueError (argument errors) and RuntimeError (CUDA failures), as the reference's launcher raised RuntimeError for a
+nonzero CUresult (_nvrtc.py:123-124). There is no CPU fallback: without the library every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(os.environ.get("KEA_LOWBIT_LIB", Path(__file__).resolve().parent / "libkea_lowbit.so"))
+
+OK, INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES, CUDA, NO_DEVICE, DEVICE_TIMEOUT, CAPTURE = range(9)
+OUT_F32, OUT_F16 = 0, 1
+FLAG_SILU, FLAG_ORDER1, FLAG_PDL = 1, 2, 4
+QUANT_INPUT_SILU = 1
+DEVERR_TIMEOUT, DEVERR_TAIL_BITS, DEVERR_TERNARY_11 = 1, 2, 4
+
+# Every symbol include/kea_lowbit.h declares.
+EXPORTS = ("kea_lowbit_gemm", "kea_lowbit_choose_config", "kea_lowbit_panel_bytes", "kea_lowbit_prepare",
+           "kea_lowbit_quantize", "kea_lowbit_read_error", "kea_lowbit_status_string", "kea_lowbit_version")
+
+
+class GemmDesc(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("q_part_stride", ctypes.c_int64), ("ldq", ctypes.c_int32), ("parts", ctypes.c_int32),
+        ("qs", ctypes.c_void_p), ("qs_part_stride", ctypes.c_int64),
+        ("panels", ctypes.c_void_p), ("wbits", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
+        ("alpha", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+        ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64), ("y_dtype", ctypes.c_int32),
+        ("acc", ctypes.c_void_p), ("ld_acc", ctypes.c_int64), ("acc_part_stride", ctypes.c_int64),
+        ("m", ctypes.c_int32), ("flags", ctypes.c_int32),
+        ("token_tile", ctypes.c_int32), ("splits", ctypes.c_int32), ("stages", ctypes.c_int32),
+        ("error_word", ctypes.c_void_p),
+    ]
+
+
+class GemmConfig(ctypes.Structure):
+    _fields_ = [("token_tile", ctypes.c_int32), ("splits", ctypes.c_int32), ("stages", ctypes.c_int32),
+                ("smem_bytes", ctypes.c_int32)]
+
+
+class QuantizeDesc(ctypes.Structure):
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("xb", ctypes.c_int64), ("xt", ctypes.c_int64), ("xk", ctypes.c_int64),
+        ("t", ctypes.c_int32), ("m", ctypes.c_int32), ("k", ctypes.c_int32), ("parts", ctypes.c_int32),
+        ("q", ctypes.c_void_p), ("q_part_stride", ctypes.c_int64), ("ldq", ctypes.c_int32),
+        ("qs", ctypes.c_void_p), ("qs_part_stride", ctypes.c_int64),
+        ("norm_weight", ctypes.c_void_p), ("norm_bias", ctypes.c_void_p), ("eps", ctypes.c_float),
+        ("flags", ctypes.c_int32),
+    ]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises RuntimeError (never falls back) when it is missing."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python kea-kernels_b200/build.py` "
+                               "(kea_kernels has no CPU fallback)")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        handle.kea_lowbit_gemm.argtypes = [ctypes.POINTER(GemmDesc), ctypes.c_void_p]
+        handle.kea_lowbit_gemm.restype = ctypes.c_int
+        handle.kea_lowbit_choose_config.argtypes = [ctypes.c_int32] * 5 + [ctypes.POINTER(GemmConfig)]
+        handle.kea_lowbit_choose_config.restype = ctypes.c_int
+        handle.kea_lowbit_panel_bytes.argtypes = [ctypes.c_int32] * 3
+        handle.kea_lowbit_panel_bytes.restype = ctypes.c_size_t
+        handle.kea_lowbit_prepare.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        handle.kea_lowbit_prepare.restype = ctypes.c_int
+        handle.kea_lowbit_quantize.argtypes = [ctypes.POINTER(QuantizeDesc), ctypes.c_void_p]
+        handle.kea_lowbit_quantize.restype = ctypes.c_int
+        handle.kea_lowbit_read_error.argtypes = [ctypes.POINTER(ctypes.c_uint32)]
+        handle.kea_lowbit_read_error.restype = ctypes.c_int
+        handle.kea_lowbit_status_string.argtypes = [ctypes.c_int]
+        handle.kea_lowbit_status_string.restype = ctypes.c_char_p
+        handle.kea_lowbit_version.argtypes = []
+        handle.kea_lowbit_version.restype = ctypes.c_int
+        _lib = handle
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status == OK:
+        return
+    text = lib().kea_lowbit_status_string(status).decode()
+    if status in (INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES):
+        raise ValueError(f"{what}: {text}")
+    raise RuntimeError(f"{what}: {text} (status {status})")
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def panel_bytes(wbits: int, n: int, k: int) -> int:
+    return int(lib().kea_lowbit_panel_bytes(wbits, n, k))
+
+
+def choose_config(m: int, n: int, k: int, wbits: int, parts: int) -> GemmConfig:
+    out = GemmConfig()
+    check(lib().kea_lowbit_choose_config(m, n, k, wbits, parts, ctypes.byref(out)), "choose_config")
+    return out
+
+
+def read_device_error() -> int:
+    """Reads and clears the library's own device error word (synchronizes the current device)."""
+    v = ctypes.c_uint32(0)
+    check(lib().kea_lowbit_read_error(ctypes.byref(v)), "read_error")
+    return int(v.value)

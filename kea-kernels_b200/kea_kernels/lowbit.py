@@ -1,0 +1,123 @@
+"""The three device operations every layer object here is built from, each one C-ABI call on the current stream:
+
+  * prepare_panels - export codes (1- or 2-bit) -> the B200 panel layout, with the code checks on the device;
+  * quantize       - FP32 rows -> P residual INT8 parts + per-row part scales (optional LayerNorm / input SiLU);
+  * gemm           - INT8 parts x packed weights -> exact INT32 accumulators -> the FP32 epilogue -> FP32 / FP16.
+
+They replace the reference's per-kernel NVRTC launches (src/kea_kernels/binary/layer.py:154-209,
+src/kea_kernels/binary/layer_parts.py:112-130) and Triton launches (src/kea_kernels/ternary/fused_kernels.py:139-160).
+No call allocates on the launch path except where a function returns new tensors (quantize, prepare_panels); gemm
+writes caller-owned outputs, so it can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+from torch import Tensor
+
+from kea_kernels import _lib
+
+
+def _round_up(v: int, m: int) -> int:
+    return -(-v // m) * m
+
+
+def _require_cuda(t: Tensor, name: str) -> None:
+    if not isinstance(t, Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+
+
+def prepare_panels(codes: Tensor, wbits: int, n: int, k: int) -> Tensor:
+    """codes uint8 [n, ceil(k * wbits / 8)] on a CUDA device -> panels uint8 [panel_bytes] on that device.
+    Raises ValueError for nonzero tail bits or (2-bit) a 0b11 field. Synchronizes (like the reference's checks)."""
+    _require_cuda(codes, "codes")
+    width = -(-k * wbits // 8)
+    if codes.dtype != torch.uint8 or codes.dim() != 2 or tuple(codes.shape) != (n, width):
+        raise ValueError(f"codes must be uint8 [{n}, {width}], got {codes.dtype} {tuple(codes.shape)}")
+    codes = codes.contiguous()
+    panels = torch.empty(_lib.panel_bytes(wbits, n, k), dtype=torch.uint8, device=codes.device)
+    err = torch.zeros(1, dtype=torch.int32, device=codes.device)
+    with torch.cuda.device(codes.device):
+        _lib.check(_lib.lib().kea_lowbit_prepare(codes.data_ptr(), wbits, n, k, panels.data_ptr(), err.data_ptr(),
+                                                 _lib.stream_handle(codes.device)), "prepare")
+    bad = int(err.item())
+    if bad:
+        raise ValueError("invalid packed codes" + (": nonzero tail padding" if bad & _lib.DEVERR_TAIL_BITS else ""))
+    return panels
+
+
+def quantize(x: Tensor, rows: tuple[int, int, int, int], m: int, k: int, parts: int, *, ldq: int | None = None,
+             norm=None, input_silu: bool = False) -> tuple[Tensor, Tensor, int]:
+    """x[m', kk] at x + (m' // T) * XB + (m' % T) * XT + kk * XK for rows = (XB, XT, XK, T) ->
+    (q int8 [parts, m, ldq] zero-padded past k, qs FP32 [parts, m], ldq)."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.float32:
+        raise ValueError(f"expected FP32 input, got {x.dtype}")
+    xb, xt, xk, t = rows
+    ldq = _round_up(k, 16) if ldq is None else ldq
+    q = torch.empty(parts, m, ldq, device=x.device, dtype=torch.int8)
+    qs = torch.empty(parts, m, device=x.device, dtype=torch.float32)
+    if m == 0:
+        return q, qs, ldq
+    d = _lib.QuantizeDesc()
+    d.x, d.xb, d.xt, d.xk, d.t = x.data_ptr(), xb, xt, xk, max(t, 1)
+    d.m, d.k, d.parts = m, k, parts
+    d.q, d.q_part_stride, d.ldq = q.data_ptr(), m * ldq, ldq
+    d.qs, d.qs_part_stride = qs.data_ptr(), m
+    if norm is not None:
+        d.norm_weight = norm.weight.data_ptr()
+        d.norm_bias = None if norm.bias is None else norm.bias.data_ptr()
+        d.eps = float(norm.eps)
+    d.flags = _lib.QUANT_INPUT_SILU if input_silu else 0
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().kea_lowbit_quantize(ctypes.byref(d), _lib.stream_handle(x.device)), "quantize")
+    return q, qs, ldq
+
+
+def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n: int, k: int, alpha: Tensor,
+         bias: Tensor | None, y: Tensor, *, parts: int, silu: bool = False, order: int = 0, acc: Tensor | None = None,
+         config=None, pdl: bool = False, error_word: Tensor | None = None) -> None:
+    """y[:m] (row stride y.stride(0); FP32 or FP16) from q int8 [parts, m, ldq] and qs FP32 [parts, m].
+    acc, when given, receives the exact INT32 accumulators as int32 [parts, m, n] (any row / part strides)."""
+    if m == 0:
+        return
+    if parts not in (1, 2, 3):
+        raise ValueError(f"parts must be 1, 2 or 3, got {parts!r}")
+    if order not in (0, 1):
+        raise ValueError("order must be 0 or 1")
+    for t, name in ((q, "q"), (qs, "qs"), (y, "y")):
+        _require_cuda(t, name)
+    if q.dtype != torch.int8 or q.dim() != 3 or q.shape[0] < parts or q.shape[1] < m:
+        raise ValueError(f"q must be int8 [{parts}, {m}, ldq]")
+    if ldq % 16 or q.stride(1) != ldq or q.stride(2) != 1 or q.data_ptr() % 16 or ldq < k:
+        raise ValueError("fast path needs 16-byte aligned rows of q")
+    if parts > 1 and q.stride(0) % 16:
+        raise ValueError("fast path needs 16-byte aligned parts of q")
+    if qs.dtype != torch.float32 or qs.dim() != 2 or qs.shape[0] < parts or qs.shape[1] < m or qs.stride(1) != 1:
+        raise ValueError(f"qs must be FP32 [{parts}, {m}] with unit column stride")
+    if y.dtype not in (torch.float32, torch.float16) or y.dim() != 2 or y.shape[0] < m or y.shape[1] < n \
+            or y.stride(1) != 1:
+        raise ValueError(f"y must be FP32 / FP16 [{m}, {n}] with unit column stride")
+    if not (q.device == qs.device == y.device == panels.device):
+        raise ValueError("q, qs, y and the layer must be on one device")
+    if acc is not None and (acc.dtype != torch.int32 or acc.dim() != 3 or acc.shape[0] < parts
+                            or acc.shape[1] < m or acc.shape[2] < n or acc.stride(2) != 1 or acc.device != y.device):
+        raise ValueError(f"acc must be int32 [{parts}, {m}, {n}] with unit column stride")
+    d = _lib.GemmDesc()
+    d.q, d.q_part_stride, d.ldq, d.parts = q.data_ptr(), q.stride(0), ldq, parts
+    d.qs, d.qs_part_stride = qs.data_ptr(), qs.stride(0)
+    d.panels, d.wbits, d.n, d.k = panels.data_ptr(), wbits, n, k
+    d.alpha, d.bias = alpha.data_ptr(), (None if bias is None else bias.data_ptr())
+    d.y, d.ldy = y.data_ptr(), y.stride(0)
+    d.y_dtype = _lib.OUT_F16 if y.dtype == torch.float16 else _lib.OUT_F32
+    if acc is not None:
+        d.acc, d.ld_acc, d.acc_part_stride = acc.data_ptr(), acc.stride(1), acc.stride(0)
+    d.m = m
+    d.flags = (_lib.FLAG_SILU if silu else 0) | (_lib.FLAG_ORDER1 if order else 0) | (_lib.FLAG_PDL if pdl else 0)
+    if config is not None:
+        d.token_tile, d.splits, d.stages = config.token_tile, config.splits, config.stages
+    if error_word is not None:
+        d.error_word = error_word.data_ptr()
+    with torch.cuda.device(y.device):
+        _lib.check(_lib.lib().kea_lowbit_gemm(ctypes.byref(d), _lib.stream_handle(y.device)), "gemm")

@@ -1,0 +1,368 @@
+"""GPU parity: the sm_100a library (called through its C ABI) against the CPU oracle and the reference's fixtures.
+
+Bar: INT32 accumulators bit-exact; FP32 outputs bit-exact without SiLU (every epilogue operation is one IEEE
+rounding on both sides); FP16 outputs bit-exact without SiLU (round-to-nearest-even of the same FP32 value); with
+SiLU (hardware ex2.approx / div.full on the GPU) FP32 within rtol 2e-6 / atol 1e-6 - the reference's own GPU-test
+tolerance (tests/test_kernels_gpu.py:44) - and FP16 within 1e-3 relative.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import kea_oracle as oracle
+from conftest import golden_cases
+from kea_kernels import _lib, formats, lowbit
+from kea_kernels.binary import bits, configs
+from kea_kernels.binary import layer as L
+from kea_kernels.binary import layer_parts
+from kea_kernels.ternary.runtime import PackedLinear, PackedPointwiseConv1d
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _codes(wbits: int, n: int, k: int, seed: int) -> tuple[np.ndarray, np.ndarray]:
+    """(export codes, dense int8 weights) drawn like the reference's tests / BASELINE configs 0-1."""
+    g = torch.Generator().manual_seed(seed)
+    if wbits == 1:
+        w = torch.where(torch.rand(n, k, generator=g) < 0.5, -1, 1).to(torch.int8)
+        return bits.pack_signs(w).numpy(), w.numpy()
+    u = torch.rand(n, k, generator=g)
+    w = torch.where(u < 0.3, -1, torch.where(u < 0.7, 0, 1)).to(torch.int8)
+    return formats.pack_ternary(w).numpy(), w.numpy()
+
+
+def _activations(parts: int, m: int, k: int, seed: int, ldq: int | None = None):
+    g = torch.Generator().manual_seed(seed + 17)
+    ldq = -(-k // 16) * 16 if ldq is None else ldq
+    q = torch.zeros(parts, m, ldq, dtype=torch.int8)
+    q[:, :, :k] = torch.randint(-127, 128, (parts, m, k), generator=g, dtype=torch.int8)
+    qs = (torch.rand(parts, m, generator=g) * 0.015 + 0.005).float()
+    return q.numpy(), qs.numpy()
+
+
+def _channel(n: int, seed: int, bias: bool):
+    g = torch.Generator().manual_seed(seed + 29)
+    alpha = (torch.rand(n, generator=g) * 0.04 + 0.01).half().float().numpy()
+    b = (torch.randn(n, generator=g) * 0.1).float().numpy() if bias else None
+    return alpha, b
+
+
+def _run(codes, wbits, n, k, q, qs, alpha, bias, *, flags=0, out=torch.float32, config=None, pdl=False):
+    parts, m, ldq = q.shape
+    panels = lowbit.prepare_panels(torch.from_numpy(codes).to(DEV), wbits, n, k)
+    qd, qsd = torch.from_numpy(q).to(DEV), torch.from_numpy(qs).to(DEV)
+    ad = torch.from_numpy(alpha).to(DEV)
+    bd = None if bias is None else torch.from_numpy(bias).to(DEV)
+    y = torch.full((m, n), float("nan"), device=DEV, dtype=out)
+    acc = torch.full((parts, m, n), -7, device=DEV, dtype=torch.int32)
+    lowbit.gemm(qd, qsd, ldq, m, panels, wbits, n, k, ad, bd, y, parts=parts, silu=bool(flags & 1),
+                order=(flags >> 1) & 1, acc=acc, config=config, pdl=pdl)
+    torch.cuda.synchronize()
+    assert _lib.read_device_error() == 0
+    return y.cpu(), acc.cpu().numpy()
+
+
+def _check(y, acc, want_y, want_acc, flags):
+    assert np.array_equal(acc, want_acc), f"{(acc != want_acc).sum()} accumulators differ"
+    if y.dtype == torch.float16:
+        want16 = oracle.to_f16(want_y)
+        if flags & 1:
+            np.testing.assert_allclose(y.float().numpy(), want16.astype(np.float32), rtol=1e-3, atol=1e-5)
+        else:
+            assert np.array_equal(y.numpy().view(np.uint16), want16.view(np.uint16))
+    else:
+        if flags & 1:
+            np.testing.assert_allclose(y.numpy(), want_y, rtol=2e-6, atol=1e-6)
+        else:
+            assert np.array_equal(y.numpy().view(np.uint32), want_y.view(np.uint32)), \
+                f"{(y.numpy() != want_y).sum()} outputs differ"
+
+
+# ---- panels ---------------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("n,k", [(4096, 1024), (1024, 4096), (5, 300), (200, 21), (130, 136)])
+def test_device_panels_equal_the_oracle_layout(wbits, n, k):
+    codes, _ = _codes(wbits, n, k, seed=n + k)
+    panels = lowbit.prepare_panels(torch.from_numpy(codes).to(DEV), wbits, n, k)
+    assert panels.numel() == _lib.panel_bytes(wbits, n, k)
+    assert np.array_equal(panels.cpu().numpy(), oracle.panels(codes, wbits, n, k))
+
+
+def test_device_prepare_rejects_invalid_codes():
+    bad = torch.zeros(2, 2, dtype=torch.uint8)
+    bad[0, 1] = 0x80  # bit 15 set for K = 12
+    with pytest.raises(ValueError, match="tail"):
+        lowbit.prepare_panels(bad.to(DEV), 1, 2, 12)
+    t = torch.zeros(3, 1, dtype=torch.uint8)
+    t[1, 0] = 0b11 << 2
+    with pytest.raises(ValueError):
+        lowbit.prepare_panels(t.to(DEV), 2, 3, 4)
+    with pytest.raises(ValueError, match="tail"):
+        L.Int8MmaLayer.prepare(bad, torch.ones(2), None, 12, DEV)
+
+
+# ---- the reference's fixtures ------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("index", range(8))
+@pytest.mark.parametrize("out", [torch.float32, torch.float16])
+def test_gemm_equals_golden_fixtures(golden, index, out):
+    case = golden_cases(golden)[index]
+    k, n = case["k"], case["n"]
+    ldq = -(-k // 16) * 16
+    q = np.zeros((case["parts"], case["m"], ldq), dtype=np.int8)
+    q[:, :, :k] = case["q"]
+    y, acc = _run(case["codes"], case["wbits"], n, k, q, case["qs"], case["alpha"], case["bias"], out=out)
+    assert np.array_equal(acc, case["acc"])                       # the reference's int64 accumulators
+    w = oracle.unpack(case["codes"], case["wbits"], k)
+    want, _ = oracle.reference(q, case["qs"], w, case["alpha"], case["bias"])
+    _check(y, acc, want, case["acc"], 0)
+    if out == torch.float32:                                      # the reference test's own tolerance vs FP64
+        np.testing.assert_allclose(y.double().numpy(), case["y64"], rtol=2e-6, atol=1e-6)
+
+
+# ---- shape sweep (config-1 M sweep and the Parakeet encoder shapes) ----------------------------------------------
+
+SHAPES = [(4096, 1024), (1024, 4096), (3072, 1024), (2048, 1024), (1024, 1024)]
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("n,k", SHAPES)
+@pytest.mark.parametrize("m", [1, 16, 38, 125, 300, 512])
+def test_gemm_x1_fp16_sweep(wbits, n, k, m):
+    seed = wbits * 7919 + n + k + m
+    codes, w = _codes(wbits, n, k, seed)
+    q, qs = _activations(1, m, k, seed)
+    alpha, _ = _channel(n, seed, False)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, None, out=torch.float16)
+    want, want_acc = oracle.reference(q, qs, w, alpha)
+    _check(y, acc, want, want_acc, 0)
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("parts", [2, 3])
+@pytest.mark.parametrize("n,k,m", [(4096, 1024, 125), (1024, 4096, 38), (3072, 1024, 300), (2048, 1024, 77)])
+@pytest.mark.parametrize("flags", [0, 2])
+def test_gemm_parts_and_order(wbits, parts, n, k, m, flags):
+    seed = wbits * 131 + parts * 17 + n + k + m + flags
+    codes, w = _codes(wbits, n, k, seed)
+    q, qs = _activations(parts, m, k, seed)
+    alpha, bias = _channel(n, seed, True)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags)
+    want, want_acc = oracle.reference(q, qs, w, alpha, bias, flags)
+    _check(y, acc, want, want_acc, flags)
+
+
+@pytest.mark.parametrize("out", [torch.float32, torch.float16])
+@pytest.mark.parametrize("parts", [1, 3])
+def test_gemm_silu_epilogue(out, parts):
+    n, k, m = 1024, 1024, 125
+    codes, w = _codes(1, n, k, 5)
+    q, qs = _activations(parts, m, k, 5)
+    alpha, bias = _channel(n, 5, True)
+    y, acc = _run(codes, 1, n, k, q, qs, alpha, bias, flags=1, out=out)
+    want, want_acc = oracle.reference(q, qs, w, alpha, bias, 1)
+    _check(y, acc, want, want_acc, 1)
+
+
+@pytest.mark.parametrize("config", [(16, 1, 1), (32, 2, 2), (64, 4, 1), (128, 8, 1), (128, 1, 4), (256, 1, 2),
+                                    (128, 16, 1), (128, 3, 2), (48, 5, 3), (256, 2, 2), (160, 1, 3), (128, 1, 8)])
+@pytest.mark.parametrize("wbits", [1, 2])
+def test_forced_tile_configs(config, wbits):
+    """Every token tile / cluster split / pipeline depth gives the same bits."""
+    n, k, m = 512, 2048, 200
+    codes, w = _codes(wbits, n, k, 11)
+    q, qs = _activations(1, m, k, 11)
+    alpha, _ = _channel(n, 11, False)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, None, config=configs.DotConfig(*config))
+    want, want_acc = oracle.reference(q, qs, w, alpha)
+    _check(y, acc, want, want_acc, 0)
+
+
+@pytest.mark.parametrize("n,k,m", [(5, 300, 3), (200, 21, 7), (130, 4097, 1), (1, 128, 257), (129, 129, 129)])
+@pytest.mark.parametrize("wbits", [1, 2])
+def test_ragged_edges(n, k, m, wbits):
+    codes, w = _codes(wbits, n, k, n * k + m)
+    q, qs = _activations(2, m, k, n + m)
+    alpha, bias = _channel(n, k, True)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias)
+    want, want_acc = oracle.reference(q, qs, w, alpha, bias)
+    _check(y, acc, want, want_acc, 0)
+
+
+def test_zero_rows_is_a_no_op():
+    layer = L.Int8MmaLayer.prepare(*_binary_layer(256, 128), None, 128, DEV)
+    y = torch.full((4, 256), 3.0, device=DEV)
+    q = torch.zeros(3, 4, 128, dtype=torch.int8, device=DEV)
+    qs = torch.ones(3, 4, device=DEV)
+    layer.dot(q, qs, 128, 0, y)
+    torch.cuda.synchronize()
+    assert bool((y == 3.0).all())
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+def test_full_size_m8192_rows_sampled(wbits):
+    """Config-1's largest M at full size: the accumulators of 96 sampled rows and a checksum of every row."""
+    n, k, m = 4096, 1024, 8192
+    codes, w = _codes(wbits, n, k, 8192 + wbits)
+    q, qs = _activations(1, m, k, 99)
+    alpha, _ = _channel(n, 3, False)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, None, out=torch.float16)
+    rows = np.random.default_rng(0).choice(m, size=96, replace=False)
+    want, want_acc = oracle.reference(q[:, rows], qs[:, rows], w, alpha)
+    _check(y[rows], acc[:, rows], want, want_acc, 0)
+    # checksum of checksums: sum_n acc[m, n] = q[m] . (sum_n w[n]) exactly, for every row
+    colsum = w.astype(np.int64).sum(axis=0)
+    assert np.array_equal(acc[0].astype(np.int64).sum(axis=1), q[0, :, :k].astype(np.int64) @ colsum)
+
+
+def test_pdl_launch_chain_matches():
+    n, k, m = 1024, 1024, 125
+    codes, w = _codes(1, n, k, 3)
+    q, qs = _activations(1, m, k, 3)
+    alpha, _ = _channel(n, 3, False)
+    y, acc = _run(codes, 1, n, k, q, qs, alpha, None, pdl=True)
+    want, want_acc = oracle.reference(q, qs, w, alpha)
+    _check(y, acc, want, want_acc, 0)
+
+
+# ---- the quantizer ---------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("m,k", [(125, 1024), (38, 4096), (7, 300), (1, 21)])
+@pytest.mark.parametrize("parts", [1, 2, 3])
+def test_quantizer_equals_oracle_bitwise(m, k, parts):
+    g = torch.Generator().manual_seed(m + k)
+    x = torch.randn(m, k, generator=g) * torch.rand(m, 1, generator=g) * 5
+    x[0, :] = 0.0
+    q, qs, ldq = lowbit.quantize(x.to(DEV), (0, x.stride(0), x.stride(1), m), m, k, parts)
+    torch.cuda.synchronize()
+    want_q, want_qs = oracle.quantize(x.numpy(), parts, ldq)
+    assert np.array_equal(q.cpu().numpy(), want_q)
+    assert np.array_equal(qs.cpu().numpy().view(np.uint32), want_qs.view(np.uint32))
+
+
+def test_quantizer_strided_conv_input():
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(2, 300, 19, generator=g)          # [B, K, T]: the conv layout, read through strides
+    xd = x.to(DEV)
+    q, qs, ldq = lowbit.quantize(xd, (xd.stride(0), xd.stride(2), xd.stride(1), 19), 38, 300, 3)
+    want_q, want_qs = oracle.quantize(x.transpose(1, 2).reshape(38, 300).numpy(), 3, ldq)
+    assert np.array_equal(q.cpu().numpy(), want_q) and np.array_equal(qs.cpu().numpy(), want_qs)
+
+
+def test_quantizer_fused_norm_and_silu_match_torch():
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(3, 41, 1024, generator=g)
+    norm = torch.nn.LayerNorm(1024)
+    with torch.no_grad():
+        norm.weight.copy_(torch.rand(1024, generator=g) + 0.5)
+        norm.bias.copy_(torch.randn(1024, generator=g) * 0.1)
+    z = torch.nn.functional.silu(norm(x)).detach()
+    normd = norm.to(DEV)
+    xd = x.to(DEV)
+    q, qs = layer_parts.m1_quantize_parts(xd, 3, normd, "silu")
+    deq = (q.float()[:, :, :1024] * qs[:, :, None]).sum(0).cpu().view(3, 41, 1024)
+    assert (deq - z).abs().max() < 1e-5 * z.abs().max()
+
+
+# ---- the layer API (the reference's GPU contract tests, tests/test_kernels_gpu.py:30-105) ------------------------
+
+def _binary_layer(n, k, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    signs = torch.where(torch.rand(n, k, generator=g) < 0.5, -1, 1).to(torch.int8)
+    scale = torch.rand(n, generator=g) * 0.02 + 0.001
+    return bits.pack_signs(signs), scale.float()
+
+
+@pytest.mark.parametrize("parts", [1, 2, 3])
+@pytest.mark.parametrize("n,k", [(1024, 1024), (4096, 1024), (1024, 4096), (3072, 1024)])
+@pytest.mark.parametrize("m", [38, 126, 300])
+@torch.inference_mode()
+def test_b1_dot_equals_exact_integer_reference(parts, n, k, m):
+    codes, scale = _binary_layer(n, k, seed=n + k + m)
+    layer = layer_parts.LAYERS[parts].prepare(codes, scale, None, k, DEV)
+    assert layer.fast
+    x = torch.randn(m, k, device=DEV)
+    q, qs, ldq = L.quantize(x, (0, x.stride(0), x.stride(1), m), m, k)
+    y = torch.empty(m, n, device=DEV)
+    layer.dot(q[:parts], qs[:parts], ldq, m, y, parts=parts)
+    torch.cuda.synchronize()
+    signs = bits.unpack_signs(codes, k).to(torch.int64)
+    acc = [q[c, :, :k].cpu().to(torch.int64) @ signs.t() for c in range(parts)]
+    ref = sum(a.double() * qs[c].cpu().double()[:, None] for c, a in enumerate(acc)) * scale.double()[None, :]
+    torch.testing.assert_close(y.cpu().double(), ref, rtol=2e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("parts,tol", [(1, 2e-2), (2, 1e-4), (3, 1e-6)])
+@torch.inference_mode()
+def test_linear_matches_dense_fp64_within_activation_precision(parts, tol):
+    n, k, m = 1024, 4096, 126
+    codes, scale = _binary_layer(n, k, seed=7)
+    layer = layer_parts.LAYERS[parts].prepare(codes, scale, None, k, DEV)
+    x = torch.randn(2, m // 2, k, device=DEV)
+    y = layer.linear(x).cpu().double()
+    ref = x.cpu().double() @ bits.dense_weight(codes, scale, k).t()
+    assert (y - ref).norm() / ref.norm() < tol
+
+
+@torch.inference_mode()
+def test_conv_and_project_paths():
+    n, k = 2048, 1024
+    codes, scale = _binary_layer(n, k, seed=9)
+    bias = torch.randn(n) * 0.1
+    layer = layer_parts.LAYERS[3].prepare(codes, scale, bias, k, DEV)
+    dense = bits.dense_weight(codes, scale, k)
+    x = torch.randn(2, k, 33, device=DEV)
+    y = layer.conv(x)
+    assert y.shape == (2, n, 33)
+    ref = torch.einsum("bkt,nk->bnt", x.cpu().double(), dense) + bias.double()[None, :, None]
+    assert (y.cpu().double() - ref).norm() / ref.norm() < 1e-6
+    xt = torch.randn(2, 33, k, device=DEV)
+    yp = layer.project(xt, components=3, activation="silu")
+    refp = torch.nn.functional.silu(xt.cpu().double() @ dense.t() + bias.double())
+    assert (yp.cpu().double() - refp).norm() / refp.norm() < 1e-5
+    yc = layer.project(x, conv=True, components=2)
+    refc = ref
+    assert yc.shape == (2, n, 33) and (yc.cpu().double() - refc).norm() / refc.norm() < 1e-4
+
+
+@torch.inference_mode()
+def test_ternary_packed_linear_matches_dense_fp64():
+    n, k, m = 1024, 1024, 64
+    g = torch.Generator().manual_seed(3)
+    codes = torch.randint(-1, 2, (n, k), generator=g, dtype=torch.int8)
+    scale = torch.rand(n, generator=g) * 0.02 + 0.001
+    module = PackedLinear(formats.pack_ternary(codes), scale.float(), k).cuda()
+    x = torch.randn(m, k, device=DEV)
+    y = module(x).cpu().double()
+    ref = x.cpu().double() @ (codes.double() * scale.double()[:, None]).t()
+    assert (y - ref).norm() / ref.norm() < 1e-5
+    conv = PackedPointwiseConv1d(formats.pack_ternary(codes), scale.float(), k, device=DEV)
+    xc = torch.randn(1, k, 40, device=DEV)
+    yc = conv(xc).cpu().double()
+    refc = torch.einsum("bkt,nk->bnt", xc.cpu().double(), codes.double() * scale.double()[:, None])
+    assert (yc - refc).norm() / refc.norm() < 1e-5
+
+
+@torch.inference_mode()
+def test_graph_capture_replays_bitwise():
+    n, k, m = 4096, 1024, 125
+    codes, scale = _binary_layer(n, k, seed=12)
+    layer = layer_parts.LAYERS[1].prepare(codes, scale, None, k, DEV)
+    q = torch.randint(-127, 128, (1, m, k), dtype=torch.int8, device=DEV)
+    qs = torch.rand(1, m, device=DEV) * 0.01 + 0.005
+    y = torch.empty(m, n, device=DEV, dtype=torch.float16)
+    layer.dot(q, qs, k, m, y, parts=1)       # first call on the device: one-time set-up outside capture
+    torch.cuda.synchronize()
+    first = y.clone()
+    graph = torch.cuda.CUDAGraph()
+    y.zero_()
+    with torch.cuda.graph(graph):
+        layer.dot(q, qs, k, m, y, parts=1)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, first)

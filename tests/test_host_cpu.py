@@ -1,0 +1,195 @@
+"""CPU: the C-ABI library loads and exports what include/kea_lowbit.h declares; host-side logic (dispatch table,
+argument checks, layer / provider plumbing, export-code checks) behaves like the reference's (no GPU work here)."""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+import torch
+
+from conftest import ROOT
+from kea_kernels import _lib, formats, lowbit
+from kea_kernels.binary import bits, configs
+from kea_kernels.binary import layer as L
+from kea_kernels.binary.provider import BinaryLinear, BinaryProjection, PartCount, Table, handle
+
+
+def test_library_exports_every_declared_symbol():
+    header = (ROOT / "include" / "kea_lowbit.h").read_text()
+    declared = set(re.findall(r"^\s*(?:int|size_t|const char \*)\s*(kea_lowbit_\w+)\s*\(", header, re.M))
+    assert declared == set(_lib.EXPORTS)
+    lib = _lib.lib()
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert lib.kea_lowbit_version() == 1
+    assert lib.kea_lowbit_status_string(0) == b"success"
+    assert lib.kea_lowbit_status_string(4) == b"invalid packed codes"
+
+
+def test_panel_bytes():
+    assert _lib.panel_bytes(1, 4096, 1024) == 4096 * 1024 // 8           # no padding at Parakeet shapes
+    assert _lib.panel_bytes(2, 4096, 1024) == 4096 * 1024 // 4
+    assert _lib.panel_bytes(1, 5, 300) == 1 * 3 * 2048
+    assert _lib.panel_bytes(2, 129, 129) == 2 * 2 * 2 * 2048
+    assert _lib.panel_bytes(3, 8, 8) == 0 and _lib.panel_bytes(1, 0, 8) == 0
+
+
+PARAKEET = [(1024, 1024), (1024, 4096), (2048, 1024), (3072, 1024), (4096, 1024)]
+
+
+@pytest.mark.parametrize("n,k", PARAKEET)
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("parts", [1, 2, 3])
+def test_every_shape_has_a_valid_config(n, k, wbits, parts):
+    kb = -(-k // 128)
+    for m in (1, 16, 38, 125, 126, 249, 256, 368, 400, 512, 1500, 2048, 8192, 32000):
+        c = _lib.choose_config(m, n, k, wbits, parts)
+        assert 16 <= c.token_tile <= 256 and c.token_tile % 16 == 0
+        assert parts * c.token_tile <= 512
+        assert 1 <= c.splits <= min(kb, 16) and 1 <= c.stages <= 8
+        assert c.smem_bytes <= 227 * 1024
+        if c.splits > 1:
+            assert parts * c.token_tile * 128 * 4 <= c.smem_bytes
+        cfg = configs.choose(m, n, k, wbits, parts)
+        cfg.validate(parts)
+        gx, gy, gz = cfg.grid(m, n)
+        assert gx * gy * gz >= min(74, gx * gy)   # small grids are split along K to cover the SMs
+
+
+def test_small_m_splits_k_and_large_m_does_not():
+    c = _lib.choose_config(125, 4096, 1024, 1, 1)
+    assert c.token_tile == 128 and c.splits > 1
+    c = _lib.choose_config(8192, 4096, 1024, 1, 1)
+    assert c.splits == 1
+
+
+def _desc(**kw):
+    d = _lib.GemmDesc()
+    d.q, d.ldq, d.parts, d.qs, d.panels, d.wbits, d.n, d.k = 16, 1024, 1, 16, 16, 1, 4096, 1024
+    d.alpha, d.y, d.ldy, d.y_dtype, d.m = 16, 16, 4096, 0, 125
+    for key, value in kw.items():
+        setattr(d, key, value)
+    return d
+
+
+def test_c_abi_argument_errors_are_reported_before_any_device_work():
+    lib = _lib.lib()
+    assert lib.kea_lowbit_gemm(None, None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(wbits=3)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(parts=4)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(y_dtype=2)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(m=0)), None) == _lib.OK          # empty: a no-op
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(q=24)), None) == _lib.ALIGNMENT
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(ldq=1000)), None) == _lib.INVALID_VALUE   # ldq < k
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(ldq=1032, k=1030)), None) == _lib.ALIGNMENT  # ldq % 16
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=64)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_prepare(None, 1, 4, 8, None, None, None) == _lib.INVALID_VALUE
+    with pytest.raises(ValueError):
+        _lib.check(_lib.ALIGNMENT, "gemm")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.CUDA, "gemm")
+
+
+def test_python_boundary_refuses_host_tensors():
+    q = torch.zeros(1, 4, 16, dtype=torch.int8)
+    with pytest.raises(ValueError, match="CUDA"):
+        lowbit.gemm(q, torch.ones(1, 4), 16, 4, torch.zeros(2048, dtype=torch.uint8), 1, 8, 16, torch.ones(8), None,
+                    torch.zeros(4, 8), parts=1)
+    with pytest.raises(ValueError, match="CUDA"):
+        lowbit.prepare_panels(torch.zeros(8, 2, dtype=torch.uint8), 1, 8, 16)
+    codes = bits.pack_signs(torch.ones(8, 16, dtype=torch.int8))
+    with pytest.raises(ValueError, match="CUDA devices only"):
+        L.Int8MmaLayer.prepare(codes, torch.ones(8), None, 16, "cpu")
+
+
+def test_validate_weights_rejections():
+    codes = torch.zeros(2, 2, dtype=torch.uint8)
+    codes[0, 1] = 0x80
+    with pytest.raises(ValueError, match="tail"):
+        bits.validate_weights(codes, torch.ones(2), None, 12)
+    good = torch.zeros(2, 2, dtype=torch.uint8)
+    assert bits.validate_weights(good, torch.ones(2), None, 12) == (2, 12)
+    with pytest.raises(ValueError, match="finite"):
+        bits.validate_weights(good, torch.tensor([1.0, float("nan")]), None, 12)
+    with pytest.raises(ValueError, match="codes must be"):
+        bits.validate_weights(good, torch.ones(2), None, 20)
+    with pytest.raises(ValueError, match="bias"):
+        bits.validate_weights(good, torch.ones(2), torch.ones(3), 12)
+    with pytest.raises(ValueError, match="in_features"):
+        bits.validate_weights(good, torch.ones(2), None, True)
+
+
+def test_dot_config_validation():
+    configs.DotConfig(128, 4, 2).validate(1)
+    with pytest.raises(ValueError):
+        configs.DotConfig(100, 1, 1).validate(1)
+    with pytest.raises(ValueError):
+        configs.DotConfig(256, 1, 1).validate(3)
+    with pytest.raises(ValueError):
+        configs.DotConfig(128, 17, 1).validate(1)
+    assert configs.DotConfig(128, 4, 2).label() == "t128_c4_s2"
+
+
+def test_part_count_overrides_components_and_forwards_writes():
+    calls = []
+
+    class Provider:
+        defer_epilogue = False
+
+        def __call__(self, x, mod, conv=False, components=3, activation="", norm=None, config=None,
+                     input_activation=""):
+            calls.append(components)
+            return x
+
+    inner = Provider()
+    wrapped = PartCount(inner, 2)
+    wrapped(torch.zeros(1), None, components=3)
+    assert calls == [2]
+    wrapped.defer_epilogue = True
+    assert inner.defer_epilogue is True and wrapped.n == 2
+    with pytest.raises(ValueError):
+        PartCount(inner, 4)
+
+
+def test_table_handles_resolve_fused_rows():
+    class FakeLayer:
+        def __init__(self, n):
+            self.n = n
+
+        def weight_bytes(self):
+            return self.n
+
+        def project(self, x, **kw):
+            return torch.arange(x.shape[-2] * self.n, dtype=torch.float32).view(1, x.shape[-2], self.n)
+
+    table = Table()
+    qkv = table.add("qkv", FakeLayer(12), "linear", 12, 4, members=("q", "k", "v"))
+    out = table.add("out", FakeLayer(4), "linear", 4, 4)
+    assert table.resolve(4, 4) == (qkv, 4) and table.resolve(12, 4) == (out, 0)
+    with pytest.raises(ValueError):
+        table.resolve(10, 4)
+    with pytest.raises(KeyError):
+        table.resolve(16, 1)
+    k_mod = BinaryLinear(qkv, 4, 4, 4, torch.ones(4), None)
+    provider = BinaryProjection(table)
+    y = provider(torch.zeros(1, 3, 4), k_mod)
+    assert y.shape == (1, 3, 4) and y[0, 0].tolist() == [4.0, 5.0, 6.0, 7.0]
+    assert provider.bytes == 16
+    with pytest.raises(ValueError):
+        provider(torch.zeros(1, 3, 4), k_mod, config=(1, 2))
+    bad = BinaryLinear(qkv, 0, 4, 4, torch.ones(4), None)
+    object.__setattr__(bad, "packed_t", handle(0, 4).flip(1))
+    with pytest.raises(ValueError, match="non-contiguous"):
+        provider(torch.zeros(1, 3, 4), bad)
+
+
+def test_ternary_validation_matches_the_reference_errors():
+    packed = formats.pack_ternary(torch.zeros(4, 8, dtype=torch.int8))
+    assert formats.validate_ternary(packed, torch.ones(4), None, 8) == (4, 8)
+    with pytest.raises(ValueError, match="finite"):
+        formats.validate_ternary(packed, torch.full((4,), float("inf")), None, 8)
+    with pytest.raises(ValueError):
+        formats.validate_ternary(torch.tensor([[0b11, 0]], dtype=torch.uint8), torch.ones(1), None, 8)
+    with pytest.raises(ValueError, match="positive"):
+        formats.validate_ternary(packed, torch.ones(4), None, 0)
