@@ -1,0 +1,460 @@
+"""Benchmark of the B200 low-bit GEMM on BASELINE config 1: the M sweep {1, 16, 125, 512, 2048, 8192} at
+(N, K) = (4096, 1024) and (1024, 4096), for 1-bit (sign) and 2-bit (ternary) weights x one INT8 activation part.
+
+A step is one pass over the 24 GEMMs of that sweep (fp16 outputs), replayed as one CUDA graph. Every GEMM reads a
+weight set and activations from rotating pools, and a step writes about 220 MB of outputs, so each step streams
+more than the 126 MB L2. `value` is the whole job's effective INT8 rate, sum(2 M N K) / time, over all ranks
+(replicas: each rank runs the full sweep on its own GPU; weak scaling). `e2e` is the same rate through the C-ABI call
+with host buffers (pinned host -> device activations, device -> pinned host outputs, inside the timed region).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`--impl reference` times the reference's CPU algorithm (unpack the packed codes, exact integer GEMM, FP32 epilogue;
+the C restatement in oracle/) on a bounded sample of the sweep, with every host core.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "kea-kernels_b200"))
+
+METRIC = "1-bit GEMM effective TOPS and % of HBM/INT8 roofline; ms per synthetic 10 s clip"
+UNIT = "TOPS"
+SHAPES = [(4096, 1024), (1024, 4096)]
+MS = [1, 16, 125, 512, 2048, 8192]
+CASES = [(wbits, n, k, m) for wbits in (1, 2) for (n, k) in SHAPES for m in MS]
+SAMPLE_MS = (1, 16, 125, 512)           # the CPU sample: every case with M <= 512
+POOL = 4                                 # distinct weight / activation sets per case in the step graphs
+COLD_BYTES = 512 << 20                   # per (wbits, N, K): distinct weights swept by the per-case cold timing
+L2_BYTES = 126 << 20
+
+
+def ops(m, n, k, parts=1):
+    return 2 * m * n * k * parts
+
+
+def alg_bytes(wbits, n, k, m, parts=1, out_bytes=2):
+    """Algorithmic bytes of one GEMM: packed weights + activations (+ scales, fp16 output for `full`)."""
+    wa = n * k * wbits // 8 + parts * m * k
+    return wa, wa + 4 * parts * m + 4 * n + out_bytes * m * n
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---- clocks ------------------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self, busy_mhz: float = 500.0) -> dict:
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        loaded = [r for r in rows if r[0] >= busy_mhz] or rows
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[2]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(loaded)}
+
+
+# ---- the CPU side (reference arm and cpu_baseline) --------------------------------------------------------------
+def cpu_sample(threads: int, min_seconds: float = 10.0, max_seconds: float = 30.0, repeats: int | None = None):
+    """Times the reference's CPU algorithm (oracle port) over the M <= 512 cases of the sweep. Returns
+    (TOPS, seconds, passes)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+    import kea_oracle as oracle
+
+    rng = np.random.default_rng(0)
+    work = []
+    for wbits, n, k, m in CASES:
+        if m not in SAMPLE_MS:
+            continue
+        if wbits == 1:
+            codes = oracle.pack_signs(rng.choice(np.array([-1, 1], dtype=np.int8), size=(n, k)))
+        else:
+            codes = oracle.pack_ternary(rng.choice(np.array([-1, 0, 1], dtype=np.int8), size=(n, k), p=[.3, .4, .3]))
+        q = rng.integers(-127, 128, size=(1, m, k), dtype=np.int8)
+        qs = rng.uniform(0.005, 0.02, size=(1, m)).astype(np.float32)
+        alpha = rng.uniform(0.01, 0.05, size=n).astype(np.float16).astype(np.float32)
+        work.append((codes, wbits, n, k, q, qs, alpha))
+    total_ops = sum(ops(q.shape[1], n, k) for _, _, n, k, q, _, _ in work)
+
+    def one_pass():
+        for codes, wbits, n, k, q, qs, alpha in work:
+            w, status = oracle.unpack_c(codes, wbits, n, k)
+            assert status == 0
+            y, _ = oracle.gemm(q, qs, w, alpha, threads=threads)
+            oracle.to_f16(y)
+
+    one_pass()  # warm-up (also builds the oracle library if needed)
+    passes, t0 = 0, time.perf_counter()
+    while True:
+        one_pass()
+        passes += 1
+        elapsed = time.perf_counter() - t0
+        if repeats is not None and passes >= repeats:
+            break
+        if repeats is None and (elapsed >= min_seconds or elapsed + elapsed / passes > max_seconds):
+            break
+    return total_ops * passes / elapsed / 1e12, elapsed, passes, total_ops
+
+
+def reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    tops_w, _, _, total_ops = cpu_sample(threads, repeats=max(1, args.warmup))
+    tops, seconds, passes, _ = cpu_sample(threads, repeats=max(1, args.steps))
+    sample = (f"the M<=512 cases of the config-1 sweep ({len(SAMPLE_MS) * 4} GEMMs, {total_ops / 1e9:.1f} GOP per "
+              f"step): unpack the packed codes, exact integer GEMM, FP32 epilogue, fp16 cast")
+    line = {"impl": "reference", "metric": METRIC, "value": tops, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": passes, "warmup": args.warmup, "ms_per_step": seconds * 1e3 / passes,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "BASELINE config 1 (M sweep, 1-bit and 2-bit) - bounded CPU sample",
+                       "sample": sample},
+            "cpu_baseline": {"value": tops, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": tops, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- the GPU side -----------------------------------------------------------------------------------------------
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--no-pdl", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from kea_kernels import _lib, formats, lowbit
+    from kea_kernels.binary import bits, configs
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    pdl = not args.no_pdl
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+    def random_codes(wbits, n, k):
+        if wbits == 1:
+            signs = torch.where(torch.rand(n, k, device=dev, generator=gen) < 0.5, -1, 1).to(torch.int8)
+            return bits.pack_signs(signs)
+        u = torch.rand(n, k, device=dev, generator=gen)
+        return formats.pack_ternary(torch.where(u < 0.3, -1, torch.where(u < 0.7, 0, 1)).to(torch.int8))
+
+    def random_panels(wbits, n, k, count):
+        pb = _lib.panel_bytes(wbits, n, k)
+        out = torch.empty(count, pb, dtype=torch.uint8, device=dev)
+        base = [lowbit.prepare_panels(random_codes(wbits, n, k), wbits, n, k) for _ in range(min(count, 8))]
+        for i in range(count):   # distinct storage per set (the bytes of sets >= 8 repeat, the addresses do not)
+            out[i].copy_(base[i % len(base)])
+        return out
+
+    # ---- buffers of the step graphs ----
+    combos = sorted({(w, n, k) for w, n, k, _ in CASES})
+    alphas = {c: (torch.rand(c[1], device=dev, generator=gen) * 0.04 + 0.01).half().float() for c in combos}
+    weights = {c: random_panels(*c, POOL) for c in combos}
+    acts, outs = {}, {}
+    for case in CASES:
+        wbits, n, k, m = case
+        acts[case] = (torch.randint(-127, 128, (POOL, 1, m, k), dtype=torch.int8, device=dev, generator=gen),
+                      torch.rand(POOL, 1, m, device=dev, generator=gen) * 0.015 + 0.005)
+        outs[case] = torch.empty(m, n, device=dev, dtype=torch.float16)
+
+    def launch(case, j, *, y=None, q=None, qs=None):
+        wbits, n, k, m = case
+        qq, ss = acts[case]
+        lowbit.gemm(qq[j] if q is None else q, ss[j] if qs is None else qs, k, m, weights[(wbits, n, k)][j], wbits,
+                    n, k, alphas[(wbits, n, k)], None, outs[case] if y is None else y, parts=1, pdl=pdl)
+
+    # one-time set-up on this device happens outside any capture
+    for case in CASES:
+        launch(case, 0)
+    torch.cuda.synchronize()
+    if _lib.read_device_error():
+        raise RuntimeError("device error word set during set-up")
+
+    stream = torch.cuda.Stream(device=dev)
+    graphs = []
+    with torch.cuda.stream(stream):
+        for j in range(POOL):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for case in CASES:
+                    launch(case, j)
+            graphs.append(g)
+    torch.cuda.synchronize()
+    step_ops = sum(ops(m, n, k) for _, n, k, m in CASES)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    hbm_peak, bf16_peak, peak_kind = measured_peaks()
+    sampler = ClockSampler(local)
+    with sampler:
+        with torch.cuda.stream(stream):
+            for i in range(args.warmup):
+                graphs[i % POOL].replay()
+            burn_until = time.perf_counter() + 1.0      # >= 1 s of load before timing, so clocks settle / sample
+            i = 0
+            while time.perf_counter() < burn_until:
+                graphs[i % POOL].replay()
+                i += 1
+                if i % 20 == 0:
+                    stream.synchronize()
+            stream.synchronize()
+            barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(args.steps):
+                graphs[i % POOL].replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        value = world * step_ops * args.steps / (ms / 1e3) / 1e12
+
+        # ---- per-case device timing (cold: distinct weights sweep >= 4 x L2; rank 0 reports) ----
+        per_case = []
+        int8_peak, int8_kind = None, None
+        if rank == 0:
+            per_case = time_cases(torch, lowbit, _lib, configs, dev, stream, random_panels, alphas, pdl)
+            int8_peak, int8_kind = int8_peak_tops(torch, dev)
+    clocks = sampler.summary()
+
+    # ---- e2e through the C-ABI call with host buffers ----
+    e2e = e2e_rate(torch, lowbit, dev, weights, alphas, args, world, dist if world > 1 else None, local)
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        del graphs
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    # dominant kernel of the step: the case with the largest share of the step's device time
+    share = max(per_case, key=lambda c: c["us"])
+    tensor_peak = int8_peak if int8_peak else 2 * bf16_peak
+    if share["m"] >= 2048:
+        achieved = ops(share["m"], share["n"], share["k"]) / (share["us"] * 1e-6) / 1e12
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
+                    "frac": achieved / tensor_peak, "traffic": None,
+                    "kernel": f"lowbit_gemm_kernel<{share['wbits']}> M={share['m']} N={share['n']} K={share['k']}",
+                    "peak_kind": int8_kind or f"2 x bf16 ({peak_kind})",
+                    "note": "INT8 ops/s; peak = dense INT8 measured with torch._int_mm 8192^3 on this GPU"}
+    else:
+        achieved = share["gbs_full"]
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                    "frac": achieved / hbm_peak, "traffic": None, "kernel": f"lowbit_gemm_kernel<{share['wbits']}>",
+                    "peak_kind": peak_kind}
+    small = [c for c in per_case if c["m"] == 125]
+    roofline_small = [{"case": f"w{c['wbits']} N={c['n']} K={c['k']} M=125", "bound": "hbm",
+                       "achieved_gbs_wa": c["gbs_wa"], "achieved_gbs_full": c["gbs_full"], "peak": hbm_peak,
+                       "frac_wa": c["gbs_wa"] / hbm_peak, "frac_full": c["gbs_full"] / hbm_peak,
+                       "us_cold": c["us"], "us_hot": c.get("us_hot")} for c in small]
+
+    cpu = None
+    if world == 1:
+        threads = os.cpu_count() or 1
+        tops, seconds, passes, total = cpu_sample(threads)
+        cpu = {"value": tops, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"M<=512 cases of the sweep ({total / 1e9:.1f} GOP per pass, {passes} passes, "
+                         f"{seconds:.1f} s): unpack + exact integer GEMM + FP32 epilogue (oracle/kea_oracle.c)"}
+
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "BASELINE config 1: M sweep {1,16,125,512,2048,8192} x (N,K) in "
+                                   "{(4096,1024),(1024,4096)} x {1-bit, 2-bit} weights, 1 INT8 part, fp16 out",
+                       "gemms_per_step": len(CASES), "gop_per_step": step_ops / 1e9,
+                       "l2": "inputs larger than L2: rotating pools of weights/activations, ~220 MB written per step",
+                       "parallelism": f"replicas x{world}", "pdl": pdl},
+            "roofline": roofline, "roofline_small_m": roofline_small, "cpu_baseline": cpu, "e2e": e2e,
+            "clocks": clocks, "gpu_launches": len(CASES) * args.steps, "cases": per_case,
+            "int8_peak_tops": int8_peak, "int8_peak_kind": int8_kind}
+    print(json.dumps(line), flush=True)
+
+
+def time_cases(torch, lowbit, _lib, configs, dev, stream, random_panels, alphas, pdl):
+    """Average device time per launch of each case: a CUDA graph of launches that each read a different weight
+    set (cold: the sets span COLD_BYTES >= 4 x L2), timed with CUDA events; small-M cases are also timed hot."""
+    out = []
+    cold_pools = {}
+    for wbits, n, k, m in CASES:
+        key = (wbits, n, k)
+        pb = _lib.panel_bytes(wbits, n, k)
+        if key not in cold_pools:
+            cold_pools[key] = random_panels(wbits, n, k, max(1, min(1024, COLD_BYTES // pb)))
+        pool = cold_pools[key]
+        launches = len(pool) if m <= 512 else 24
+        nq = 8
+        q = torch.randint(-127, 128, (nq, 1, m, k), dtype=torch.int8, device=dev)
+        qs = torch.rand(nq, 1, m, device=dev) * 0.015 + 0.005
+        y = torch.empty(m, n, device=dev, dtype=torch.float16)
+
+        def run(i, hot=False):
+            lowbit.gemm(q[i % nq], qs[i % nq], k, m, pool[0 if hot else i % len(pool)], wbits, n, k, alphas[key],
+                        None, y, parts=1, pdl=pdl)
+
+        def timed(hot):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(g, stream=stream):
+                    for i in range(launches):
+                        run(i, hot)
+                g.replay()
+                stream.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+                stream.synchronize()
+            return e0.elapsed_time(e1) * 1e3 / launches
+
+        us = timed(False)
+        wa, full = alg_bytes(wbits, n, k, m)
+        c = configs.choose(m, n, k, wbits, 1)
+        rec = {"wbits": wbits, "n": n, "k": k, "m": m, "us": us, "tops": ops(m, n, k) / us / 1e6,
+               "gbs_wa": wa / us / 1e3, "gbs_full": full / us / 1e3, "config": c.label(), "launches": launches}
+        if m <= 512:
+            rec["us_hot"] = timed(True)
+        out.append(rec)
+        del q, qs, y
+    return out
+
+
+def int8_peak_tops(torch, dev):
+    """Dense INT8 tensor rate of this GPU from torch._int_mm at 8192^3 (best of 10)."""
+    try:
+        a = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device=dev)
+        b = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device=dev)
+        for _ in range(3):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        return 2 * 8192 ** 3 / (best / 1e3) / 1e12, "measured: torch._int_mm 8192^3, best of 10"
+    except Exception as exc:  # noqa: BLE001
+        return None, f"unavailable ({type(exc).__name__})"
+
+
+def e2e_rate(torch, lowbit, dev, weights, alphas, args, world, dist, local):
+    """The sweep through the C-ABI call with host buffers: per GEMM, pinned host -> device copy of the INT8
+    activations and scales, the call, and a device -> pinned host copy of the fp16 output, all timed."""
+    host_q = {c: torch.randint(-127, 128, (1, c[3], c[2]), dtype=torch.int8).pin_memory() for c in CASES}
+    host_s = {c: (torch.rand(1, c[3]) * 0.015 + 0.005).pin_memory() for c in CASES}
+    host_y = {c: torch.empty(c[3], c[1], dtype=torch.float16).pin_memory() for c in CASES}
+    dq = {c: torch.empty_like(host_q[c], device=dev) for c in CASES}
+    ds = {c: torch.empty_like(host_s[c], device=dev) for c in CASES}
+    dy = {c: torch.empty(c[3], c[1], dtype=torch.float16, device=dev) for c in CASES}
+    h2d = sum(host_q[c].numel() + 4 * host_s[c].numel() for c in CASES)
+    d2h = sum(2 * host_y[c].numel() for c in CASES)
+
+    def step(j):
+        for c in CASES:
+            wbits, n, k, m = c
+            dq[c].copy_(host_q[c], non_blocking=True)
+            ds[c].copy_(host_s[c], non_blocking=True)
+            lowbit.gemm(dq[c], ds[c], k, m, weights[(wbits, n, k)][j % POOL], wbits, n, k, alphas[(wbits, n, k)],
+                        None, dy[c], parts=1)
+            host_y[c].copy_(dy[c], non_blocking=True)
+
+    steps = max(3, min(args.steps, 50))
+    for j in range(args.warmup):
+        step(j)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for j in range(steps):
+        step(j)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    step_ops = sum(ops(m, n, k) for _, n, k, m in CASES)
+    return {"value": world * step_ops * steps / (ms / 1e3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": ms / steps,
+            "path": "kea_lowbit_gemm via ctypes (kea_kernels.lowbit.gemm), pinned host buffers"}
+
+
+if __name__ == "__main__":
+    main()

@@ -20,13 +20,13 @@ __global__ void __launch_bounds__(256) prepare_panels_kernel(const uint8_t *__re
                                                              uint8_t *__restrict__ panels, uint32_t *err) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= chunks) return;
-    const int r = (int)(idx % kTileN);
-    long long rest = idx / kTileN;
+    const int r = (int)(idx % kPanelN);
+    long long rest = idx / kPanelN;
     const int s = (int)(rest % wbits);
     rest /= wbits;
     const int b = (int)(rest % kb_total);
     const long long t = rest / kb_total;
-    const long long n = t * kTileN + r;
+    const long long n = t * kPanelN + r;
     const int byte0 = b * 16 * wbits + s * 16;
     const int per_byte = 8 / wbits;
     uint32_t bad = 0;

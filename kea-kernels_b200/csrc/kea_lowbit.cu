@@ -19,7 +19,7 @@ using kea::GemmArgs;
 constexpr int kSmsB200 = 148;
 constexpr int kMaxDevices = 64;
 constexpr int kSmemPerSm = 233472;       // 228 KB of shared memory per SM
-constexpr int kMaxDynSmem = 227 * 1024 - 4096;  // leave room for the kernel's static shared memory
+constexpr int kMaxDynSmem = 227 * 1024 - 8192;  // leave room for the kernel's static shared memory (< 8 KB)
 constexpr int kMaxPortableCluster = 8;
 constexpr int kMaxCluster = 16;
 
@@ -66,7 +66,9 @@ int device_setup(int *device_out) {
             g_encode = reinterpret_cast<EncodeTiledFn>(fn);
     }
     if (status == KEA_OK) {
-        const void *kernels[2] = {(const void *)kea::lowbit_gemm_kernel<1>, (const void *)kea::lowbit_gemm_kernel<2>};
+        const void *kernels[6] = {(const void *)kea::lowbit_gemm_kernel<1, 1>, (const void *)kea::lowbit_gemm_kernel<1, 2>,
+                                  (const void *)kea::lowbit_gemm_kernel<1, 3>, (const void *)kea::lowbit_gemm_kernel<2, 1>,
+                                  (const void *)kea::lowbit_gemm_kernel<2, 2>, (const void *)kea::lowbit_gemm_kernel<2, 3>};
         for (const void *k : kernels) {
             if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem) != cudaSuccess ||
                 cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
@@ -83,69 +85,70 @@ int device_setup(int *device_out) {
 }
 
 // ---- configuration ---------------------------------------------------------------------------------------
-int stage_bytes(int bt, int parts, int wbits) { return round_up(kea::kExpBytes + parts * bt * 128 + wbits * kea::kPanelSubBytes, 1024); }
-
-int max_token_tile(int parts, int splits) {
-    // TMEM holds parts * bt INT32 columns (<= 512); the split-K exchange buffer holds parts * bt * 512 bytes.
-    int bt = std::min(256, (512 / parts) / 16 * 16);
-    if (splits > 1) bt = std::min(bt, (384 / parts) / 16 * 16);
-    return bt;
+int stage_bytes(int tile_m, int tile_n, int parts, int wbits) {
+    const int act = (tile_m / kea::kBM) * parts * kea::kActTileBytes;
+    return round_up(act + tile_n * kea::kBK + (tile_n / kea::kPanelN) * wbits * kea::kPanelSubBytes, 1024);
 }
 
-int dyn_smem_bytes(int bt, int parts, int wbits, int splits, int stages, uint32_t tmem_cols) {
-    int bytes = stages * stage_bytes(bt, parts, wbits);
-    if (splits > 1) bytes = std::max(bytes, parts * bt * kea::kTileN * 4);
-    bytes += 1024;  // alignment slack for the 1024-byte swizzle atoms
-    // Never let more CTAs share an SM than its 512 TMEM columns can serve: a CTA waiting in tcgen05.alloc
-    // while its cluster peers wait for it could otherwise deadlock.
-    const int max_ctas = std::max(1, (int)(512 / tmem_cols));
-    const int floor_bytes = kSmemPerSm / (max_ctas + 1) + 1;
-    return std::max(bytes, floor_bytes);
-}
-
-uint32_t tmem_columns(int parts, int bt) {
-    uint32_t need = (uint32_t)(parts * bt), cols = 32;
+uint32_t tmem_columns(int tile_m, int tile_n, int parts) {
+    uint32_t need = (uint32_t)((tile_m / kea::kBM) * parts * tile_n), cols = 32;
     while (cols < need) cols <<= 1;
     return cols;
 }
 
-// The M-bucketed split-K dispatch table. Small M (one token tile): one CTA per 128 channels, K split over a
-// cluster so the grid covers the SMs. Larger M: 128- or 256-token tiles, split only when the tile grid is
-// too small to fill the GPU.
+int exchange_bytes(int tile_m, int tile_n, int parts) { return (tile_m / kea::kBM) * parts * tile_n * kea::kBM * 4; }
+
+int dyn_smem_bytes(int tile_m, int tile_n, int parts, int wbits, int splits, int stages) {
+    int bytes = stages * stage_bytes(tile_m, tile_n, parts, wbits);
+    if (splits > 1) bytes = std::max(bytes, exchange_bytes(tile_m, tile_n, parts));
+    bytes += 1024;  // alignment slack for the 1024-byte swizzle atoms
+    // Never let more CTAs share an SM than its 512 TMEM columns can serve: a CTA waiting in tcgen05.alloc
+    // while its cluster peers wait for it could otherwise deadlock.
+    const uint32_t cols = tmem_columns(tile_m, tile_n, parts);
+    const int max_ctas = std::max(1, (int)(512 / cols));
+    const int floor_bytes = kSmemPerSm / (max_ctas + 1) + 1;
+    return std::max(bytes, floor_bytes);
+}
+
+int max_stages(int tile_m, int tile_n, int parts, int wbits) {
+    int s = kea::kMaxStages;
+    while (s > 1 && s * stage_bytes(tile_m, tile_n, parts, wbits) + 1024 > kMaxDynSmem) --s;
+    return s;
+}
+
+// The M-bucketed split-K dispatch table.
+//  * M <= 128: one 128-token tile; 128 channels per CTA; K split over a cluster so the grid covers the SMs.
+//  * M <= 256 (and P = 1): 256 tokens per CTA, so the weights of a 128-channel tile are expanded once for both halves.
+//  * larger M: 256-token x 128-channel tiles, split only when the tile grid is too small to fill the GPU.
 KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
     KeaGemmConfig c{};
-    const int kb = ceil_div(k, kea::kBK), nt = ceil_div(n, kea::kTileN);
-    const int m16 = round_up(std::max(m, 1), 16);
-    int bt;
-    if (m16 <= max_token_tile(parts, 1))
-        bt = m16;
-    else
-        bt = (parts == 1 && m > 2048) ? 256 : 128;
-    const int tiles = ceil_div(std::max(m, 1), bt);
-    const int ctas = nt * tiles;
+    const int kb = ceil_div(k, kea::kBK), nt = ceil_div(n, kea::kPanelN);
+    const int tile_n = 128;
+    const int tile_m = (m > 128 && parts == 1) ? 256 : 128;
+    const int tiles = ceil_div(std::max(m, 1), tile_m) * nt;
     int splits = 1;
-    if (ctas < sms / 2 || (tiles == 1 && ctas < sms)) splits = std::max(1, sms / ctas);
+    if (tiles < sms) splits = std::max(1, sms / tiles);
     splits = std::min({splits, kb, kMaxPortableCluster});
-    if (splits > 1 && bt > max_token_tile(parts, splits)) splits = 1;
+    while (splits > 1 && exchange_bytes(tile_m, tile_n, parts) + 1024 > kMaxDynSmem) --splits;
     const int per = ceil_div(kb, splits);
-    int stages = std::min(per, 4);
-    if (stages < 1) stages = 1;
-    while (stages > 1 && stages * stage_bytes(bt, parts, wbits) + 1024 > kMaxDynSmem) --stages;
-    c.token_tile = bt;
+    int stages = std::min({per, 4, max_stages(tile_m, tile_n, parts, wbits)});
+    c.tile_m = tile_m;
+    c.tile_n = tile_n;
     c.splits = splits;
-    c.stages = stages;
-    c.smem_bytes = dyn_smem_bytes(bt, parts, wbits, splits, stages, tmem_columns(parts, bt));
+    c.stages = std::max(stages, 1);
+    c.smem_bytes = dyn_smem_bytes(tile_m, tile_n, parts, wbits, splits, c.stages);
     return c;
 }
 
-int check_config(const KeaGemmConfig &c, int m, int k, int parts, int wbits) {
-    const int kb = ceil_div(k, kea::kBK);
-    if (c.token_tile < 16 || c.token_tile > 256 || c.token_tile % 16) return KEA_ERR_UNSUPPORTED;
+int check_config(const KeaGemmConfig &c, int n, int k, int parts, int wbits) {
+    const int kb = ceil_div(k, kea::kBK), nt = ceil_div(n, kea::kPanelN);
+    if (c.tile_m != 128 && c.tile_m != 256) return KEA_ERR_UNSUPPORTED;
+    if (c.tile_n != 128 && c.tile_n != 256) return KEA_ERR_UNSUPPORTED;
+    if (c.tile_n == 256 && nt % 2) return KEA_ERR_UNSUPPORTED;   // the second panel tile must exist
+    if ((c.tile_m / kea::kBM) * parts * c.tile_n > 512) return KEA_ERR_UNSUPPORTED;   // TMEM columns
     if (c.splits < 1 || c.splits > kMaxCluster || c.splits > kb) return KEA_ERR_UNSUPPORTED;
     if (c.stages < 1 || c.stages > kea::kMaxStages) return KEA_ERR_UNSUPPORTED;
-    if (c.token_tile > max_token_tile(parts, c.splits)) return KEA_ERR_UNSUPPORTED;
     if (c.smem_bytes > kMaxDynSmem) return KEA_ERR_UNSUPPORTED;
-    (void)m;
     (void)wbits;
     return KEA_OK;
 }
@@ -175,7 +178,7 @@ const char *kea_lowbit_status_string(int status) {
 
 size_t kea_lowbit_panel_bytes(int32_t wbits, int32_t n, int32_t k) {
     if ((wbits != 1 && wbits != 2) || n < 1 || k < 1) return 0;
-    return (size_t)ceil_div(n, kea::kTileN) * (size_t)ceil_div(k, kea::kBK) * (size_t)wbits * kea::kPanelSubBytes;
+    return (size_t)ceil_div(n, kea::kPanelN) * (size_t)ceil_div(k, kea::kBK) * (size_t)wbits * kea::kPanelSubBytes;
 }
 
 int kea_lowbit_choose_config(int32_t m, int32_t n, int32_t k, int32_t wbits, int32_t parts, KeaGemmConfig *out) {
@@ -199,7 +202,7 @@ int kea_lowbit_prepare(const uint8_t *codes, int32_t wbits, int32_t n, int32_t k
     if (st != KEA_OK) return st;
     const int row_bytes = ceil_div((long long)k * wbits, 8);
     const int kb = ceil_div(k, kea::kBK);
-    const long long chunks = (long long)ceil_div(n, kea::kTileN) * kb * wbits * kea::kTileN;
+    const long long chunks = (long long)ceil_div(n, kea::kPanelN) * kb * wbits * kea::kPanelN;
     const unsigned blocks = (unsigned)((chunks + 255) / 256);
     kea::prepare_panels_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(codes, row_bytes, wbits, n, k, kb, chunks,
                                                                           panels, error_word);
@@ -255,25 +258,28 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     if (st != KEA_OK) return st;
 
     KeaGemmConfig c = choose(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms);
-    if (d->token_tile || d->splits || d->stages) {
-        if (d->token_tile) c.token_tile = d->token_tile;
+    if (d->tile_m || d->tile_n || d->splits || d->stages) {
+        if (d->tile_m) c.tile_m = d->tile_m;
+        if (d->tile_n) c.tile_n = d->tile_n;
         if (d->splits) c.splits = d->splits;
-        if (d->stages) c.stages = d->stages;
-        const int per = ceil_div(ceil_div(d->k, kea::kBK), std::max(1, c.splits));
-        if (!d->stages) c.stages = std::max(1, std::min(per, c.stages));
-        c.smem_bytes = dyn_smem_bytes(c.token_tile, d->parts, d->wbits, c.splits, c.stages,
-                                      tmem_columns(d->parts, c.token_tile));
+        if (d->stages) {
+            c.stages = d->stages;
+        } else {
+            const int per = ceil_div(ceil_div(d->k, kea::kBK), std::max(1, c.splits));
+            c.stages = std::max(1, std::min({per, 4, max_stages(c.tile_m, c.tile_n, d->parts, d->wbits)}));
+        }
+        c.smem_bytes = dyn_smem_bytes(c.tile_m, c.tile_n, d->parts, d->wbits, c.splits, c.stages);
     }
-    const int cs = check_config(c, d->m, d->k, d->parts, d->wbits);
+    const int cs = check_config(c, d->n, d->k, d->parts, d->wbits);
     if (cs != KEA_OK) return cs;
 
-    // Activations: a 3-D tensor (k, m, part) of int8, tiles of 128 k x token_tile rows x 1 part, 128-byte
+    // Activations: a 3-D tensor (k, m, part) of int8, tiles of 128 k x 128 rows x 1 part, 128-byte
     // swizzle (the tcgen05 K-major layout). Columns >= k and rows >= m read as zero.
     CUtensorMap qmap;
     const cuuint64_t dims[3] = {(cuuint64_t)d->k, (cuuint64_t)d->m, (cuuint64_t)d->parts};
     const long long pstride = d->parts > 1 ? d->q_part_stride : (long long)d->m * d->ldq;
     const cuuint64_t strides[2] = {(cuuint64_t)d->ldq, (cuuint64_t)std::max<long long>(pstride, 16)};
-    const cuuint32_t box[3] = {(cuuint32_t)kea::kBK, (cuuint32_t)c.token_tile, 1};
+    const cuuint32_t box[3] = {(cuuint32_t)kea::kBK, (cuuint32_t)kea::kBM, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     if (g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t *>(d->q), dims, strides, box, estr,
                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -296,17 +302,21 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     a.N = d->n;
     a.K = d->k;
     a.parts = d->parts;
-    a.bt = c.token_tile;
+    a.tile_n = c.tile_n;
+    a.tm_blocks = c.tile_m / kea::kBM;
     a.splits = c.splits;
     a.stages = c.stages;
     a.kb_total = ceil_div(d->k, kea::kBK);
     a.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
-    a.tmem_cols = tmem_columns(d->parts, c.token_tile);
-    a.stage_bytes = (uint32_t)stage_bytes(c.token_tile, d->parts, d->wbits);
+    a.tmem_cols = tmem_columns(c.tile_m, c.tile_n, d->parts);
+    a.stage_bytes = (uint32_t)stage_bytes(c.tile_m, c.tile_n, d->parts, d->wbits);
+    const int esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
+    a.vec_y = aligned16(d->y) && ((d->ldy * esize) % 16 == 0);
+    a.vec_acc = d->acc && aligned16(d->acc) && ((d->ld_acc * 4) % 16 == 0) && ((d->acc_part_stride * 4) % 16 == 0);
     a.err = d->error_word;
 
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)ceil_div(d->n, kea::kTileN), (unsigned)ceil_div(d->m, c.token_tile), (unsigned)c.splits);
+    cfg.gridDim = dim3((unsigned)ceil_div(d->n, c.tile_n), (unsigned)ceil_div(d->m, c.tile_m), (unsigned)c.splits);
     cfg.blockDim = dim3(kea::kThreads, 1, 1);
     cfg.dynamicSmemBytes = (size_t)c.smem_bytes;
     cfg.stream = (cudaStream_t)stream;
@@ -326,8 +336,15 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     }
     cfg.attrs = attrs;
     cfg.numAttrs = na;
-    cudaError_t e = d->wbits == 1 ? cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<1>, qmap, a)
-                                  : cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<2>, qmap, a);
+    cudaError_t e;
+    switch (d->wbits * 4 + d->parts) {
+        case 5: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<1, 1>, qmap, a); break;
+        case 6: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<1, 2>, qmap, a); break;
+        case 7: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<1, 3>, qmap, a); break;
+        case 9: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<2, 1>, qmap, a); break;
+        case 10: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<2, 2>, qmap, a); break;
+        default: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<2, 3>, qmap, a); break;
+    }
     if (e != cudaSuccess) {
         cudaGetLastError();
         return KEA_ERR_CUDA;

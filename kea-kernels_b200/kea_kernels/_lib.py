@@ -35,14 +35,14 @@ class GemmDesc(ctypes.Structure):
         ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64), ("y_dtype", ctypes.c_int32),
         ("acc", ctypes.c_void_p), ("ld_acc", ctypes.c_int64), ("acc_part_stride", ctypes.c_int64),
         ("m", ctypes.c_int32), ("flags", ctypes.c_int32),
-        ("token_tile", ctypes.c_int32), ("splits", ctypes.c_int32), ("stages", ctypes.c_int32),
-        ("error_word", ctypes.c_void_p),
+        ("tile_m", ctypes.c_int32), ("tile_n", ctypes.c_int32), ("splits", ctypes.c_int32),
+        ("stages", ctypes.c_int32), ("error_word", ctypes.c_void_p),
     ]
 
 
 class GemmConfig(ctypes.Structure):
-    _fields_ = [("token_tile", ctypes.c_int32), ("splits", ctypes.c_int32), ("stages", ctypes.c_int32),
-                ("smem_bytes", ctypes.c_int32)]
+    _fields_ = [("tile_m", ctypes.c_int32), ("tile_n", ctypes.c_int32), ("splits", ctypes.c_int32),
+                ("stages", ctypes.c_int32), ("smem_bytes", ctypes.c_int32)]
 
 
 class QuantizeDesc(ctypes.Structure):

@@ -1,9 +1,9 @@
 """Tile choices of the B200 low-bit GEMM: the M-bucketed split-K dispatch table.
 
 The reference picks an SM120 `DotConfig` from a table of RTX 5090 sweeps (src/kea_kernels/binary/configs.py:16-58). The
-B200 kernel has three knobs instead: `token_tile` (tokens per CTA = the tcgen05 N dimension, a multiple of 16 up to
-256), `splits` (K split across a thread-block cluster, reduced exactly in INT32 through distributed shared memory) and
-`stages` (k128 blocks in flight). The table itself lives in the C library (`kea_lowbit_choose_config`), so C callers
+B200 kernel has four knobs instead: `tile_m` (tokens per CTA: one or two tcgen05 M = 128 blocks), `tile_n` (channels
+per CTA = the tcgen05 N dimension, 128 or 256), `splits` (K split across a thread-block cluster, reduced exactly in
+INT32 through distributed shared memory) and `stages` (k128 blocks in flight). The table itself lives in the C library (`kea_lowbit_choose_config`), so C callers
 and Python pick the same tiles; selection is a pure function of (M, N, K, wbits, parts), with no run-time autotuning.
 """
 from __future__ import annotations
@@ -17,24 +17,25 @@ SMS = 148
 
 @dataclasses.dataclass(frozen=True)
 class DotConfig:
-    """CTA = 128 output channels x `token_tile` tokens over 1/`splits` of K, `stages` k128 blocks in flight."""
-    token_tile: int
+    """CTA = `tile_m` tokens x `tile_n` channels over 1/`splits` of K, `stages` k128 blocks in flight."""
+    tile_m: int
+    tile_n: int
     splits: int
     stages: int
 
     def label(self) -> str:
-        return f"t{self.token_tile}_c{self.splits}_s{self.stages}"
+        return f"m{self.tile_m}_n{self.tile_n}_c{self.splits}_s{self.stages}"
 
     def validate(self, parts: int = 1) -> None:
-        if not (16 <= self.token_tile <= 256 and self.token_tile % 16 == 0 and 1 <= self.splits <= 16
-                and 1 <= self.stages <= 8 and parts * self.token_tile <= 512):
+        if not (self.tile_m in (128, 256) and self.tile_n in (128, 256) and 1 <= self.splits <= 16
+                and 1 <= self.stages <= 8 and (self.tile_m // 128) * parts * self.tile_n <= 512):
             raise ValueError(f"invalid config {self}")
 
     def grid(self, m: int, n: int) -> tuple[int, int, int]:
-        return (-(-n // 128), -(-m // self.token_tile), self.splits)
+        return (-(-n // self.tile_n), -(-m // self.tile_m), self.splits)
 
 
 def choose(m: int, n: int, k: int, wbits: int = 1, parts: int = 1) -> DotConfig:
     """The configuration the library uses for this shape (the C table)."""
     c = _lib.choose_config(max(m, 0), n, k, wbits, parts)
-    return DotConfig(c.token_tile, c.splits, c.stages)
+    return DotConfig(c.tile_m, c.tile_n, c.splits, c.stages)

@@ -116,7 +116,7 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
     d.m = m
     d.flags = (_lib.FLAG_SILU if silu else 0) | (_lib.FLAG_ORDER1 if order else 0) | (_lib.FLAG_PDL if pdl else 0)
     if config is not None:
-        d.token_tile, d.splits, d.stages = config.token_tile, config.splits, config.stages
+        d.tile_m, d.tile_n, d.splits, d.stages = config.tile_m, config.tile_n, config.splits, config.stages
     if error_word is not None:
         d.error_word = error_word.data_ptr()
     with torch.cuda.device(y.device):

@@ -169,18 +169,33 @@ def test_gemm_silu_epilogue(out, parts):
     _check(y, acc, want, want_acc, 1)
 
 
-@pytest.mark.parametrize("config", [(16, 1, 1), (32, 2, 2), (64, 4, 1), (128, 8, 1), (128, 1, 4), (256, 1, 2),
-                                    (128, 16, 1), (128, 3, 2), (48, 5, 3), (256, 2, 2), (160, 1, 3), (128, 1, 8)])
+@pytest.mark.parametrize("config", [(128, 128, 1, 1), (128, 128, 2, 2), (128, 128, 4, 1), (128, 128, 8, 1),
+                                    (128, 128, 1, 4), (256, 128, 1, 2), (128, 128, 16, 1), (128, 128, 3, 2),
+                                    (256, 256, 1, 3), (256, 128, 2, 2), (128, 256, 5, 3), (128, 256, 1, 3),
+                                    (256, 256, 1, 1), (128, 128, 1, 6)])
 @pytest.mark.parametrize("wbits", [1, 2])
 def test_forced_tile_configs(config, wbits):
-    """Every token tile / cluster split / pipeline depth gives the same bits."""
-    n, k, m = 512, 2048, 200
+    """Every token / channel tile, cluster split and pipeline depth gives the same bits."""
+    n, k, m = 512, 2048, 300
     codes, w = _codes(wbits, n, k, 11)
     q, qs = _activations(1, m, k, 11)
     alpha, _ = _channel(n, 11, False)
     y, acc = _run(codes, wbits, n, k, q, qs, alpha, None, config=configs.DotConfig(*config))
     want, want_acc = oracle.reference(q, qs, w, alpha)
     _check(y, acc, want, want_acc, 0)
+
+
+def test_oversized_config_is_refused():
+    codes, _ = _codes(1, 512, 2048, 11)
+    q, qs = _activations(1, 200, 2048, 11)
+    alpha, _ = _channel(512, 11, False)
+    with pytest.raises(ValueError, match="unsupported"):
+        _run(codes, 1, 512, 2048, q, qs, alpha, None, config=configs.DotConfig(256, 256, 1, 8))   # > smem
+    codes384, _ = _codes(1, 384, 2048, 12)
+    with pytest.raises(ValueError, match="unsupported"):        # 256-channel tiles need an even tile count
+        _run(codes384, 1, 384, 2048, q, qs, alpha[:384], None, config=configs.DotConfig(128, 256, 1, 2))
+    with pytest.raises(ValueError, match="unsupported"):        # the split-K exchange would not fit
+        _run(codes, 1, 512, 2048, q, qs, alpha, None, config=configs.DotConfig(256, 256, 2, 1))
 
 
 @pytest.mark.parametrize("n,k,m", [(5, 300, 3), (200, 21, 7), (130, 4097, 1), (1, 128, 257), (129, 129, 129)])

@@ -45,12 +45,12 @@ def test_every_shape_has_a_valid_config(n, k, wbits, parts):
     kb = -(-k // 128)
     for m in (1, 16, 38, 125, 126, 249, 256, 368, 400, 512, 1500, 2048, 8192, 32000):
         c = _lib.choose_config(m, n, k, wbits, parts)
-        assert 16 <= c.token_tile <= 256 and c.token_tile % 16 == 0
-        assert parts * c.token_tile <= 512
+        assert c.tile_m in (128, 256) and c.tile_n in (128, 256)
+        assert (c.tile_m // 128) * parts * c.tile_n <= 512
         assert 1 <= c.splits <= min(kb, 16) and 1 <= c.stages <= 8
         assert c.smem_bytes <= 227 * 1024
         if c.splits > 1:
-            assert parts * c.token_tile * 128 * 4 <= c.smem_bytes
+            assert (c.tile_m // 128) * parts * c.tile_n * 128 * 4 <= c.smem_bytes
         cfg = configs.choose(m, n, k, wbits, parts)
         cfg.validate(parts)
         gx, gy, gz = cfg.grid(m, n)
@@ -59,13 +59,14 @@ def test_every_shape_has_a_valid_config(n, k, wbits, parts):
 
 def test_small_m_splits_k_and_large_m_does_not():
     c = _lib.choose_config(125, 4096, 1024, 1, 1)
-    assert c.token_tile == 128 and c.splits > 1
+    assert c.tile_m == 128 and c.splits > 1
     c = _lib.choose_config(8192, 4096, 1024, 1, 1)
     assert c.splits == 1
 
 
 def _desc(**kw):
     d = _lib.GemmDesc()
+    assert [f[0] for f in d._fields_][-5:] == ["tile_m", "tile_n", "splits", "stages", "error_word"]
     d.q, d.ldq, d.parts, d.qs, d.panels, d.wbits, d.n, d.k = 16, 1024, 1, 16, 16, 1, 4096, 1024
     d.alpha, d.y, d.ldy, d.y_dtype, d.m = 16, 16, 4096, 0, 125
     for key, value in kw.items():
@@ -121,14 +122,14 @@ def test_validate_weights_rejections():
 
 
 def test_dot_config_validation():
-    configs.DotConfig(128, 4, 2).validate(1)
+    configs.DotConfig(128, 128, 4, 2).validate(1)
     with pytest.raises(ValueError):
-        configs.DotConfig(100, 1, 1).validate(1)
+        configs.DotConfig(100, 128, 1, 1).validate(1)
     with pytest.raises(ValueError):
-        configs.DotConfig(256, 1, 1).validate(3)
+        configs.DotConfig(256, 256, 1, 1).validate(3)
     with pytest.raises(ValueError):
-        configs.DotConfig(128, 17, 1).validate(1)
-    assert configs.DotConfig(128, 4, 2).label() == "t128_c4_s2"
+        configs.DotConfig(128, 128, 17, 1).validate(1)
+    assert configs.DotConfig(128, 128, 4, 2).label() == "m128_n128_c4_s2"
 
 
 def test_part_count_overrides_components_and_forwards_writes():
