@@ -94,7 +94,7 @@ typedef struct KeaGemmDesc {
     int32_t m;                /* tokens (rows of q and y); 0 is a no-op */
     int32_t flags;            /* KEA_FLAG_* */
     int32_t tile_m;           /* 0: dispatch table; else tokens per CTA (128 or 256) */
-    int32_t tile_n;           /* 0: dispatch table; else channels per CTA (128 or 256) */
+    int32_t tile_n;           /* 0: dispatch table; else channels per CTA (32, 64, 128 or 256) */
     int32_t splits;           /* 0: dispatch table; else split-K ways = cluster size (1..16) */
     int32_t stages;           /* 0: dispatch table; else pipeline stages (1..8) */
     uint32_t *error_word;     /* device word OR-ed with KEA_DEVERR_* bits, or NULL for the library's own */
@@ -103,7 +103,7 @@ typedef struct KeaGemmDesc {
 /* Tile configuration picked for a shape (the M-bucketed split-K dispatch table). */
 typedef struct KeaGemmConfig {
     int32_t tile_m;           /* tokens per CTA: 128 or 256 (one or two tcgen05 M = 128 blocks) */
-    int32_t tile_n;           /* channels per CTA: 128 or 256 (the tcgen05 N dimension) */
+    int32_t tile_n;           /* channels per CTA: 32, 64, 128 or 256 (the tcgen05 N dimension) */
     int32_t splits;           /* K split across a thread-block cluster of this size */
     int32_t stages;           /* smem pipeline depth (k128 blocks in flight) */
     int32_t smem_bytes;       /* dynamic shared memory per CTA */

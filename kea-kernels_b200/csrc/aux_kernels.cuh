@@ -10,16 +10,17 @@
 namespace kea {
 
 // ---- prepare: export codes -> panels --------------------------------------------------------------------------
-// Panel layout: [ceil(N/128) tiles][ceil(K/128) k-blocks][wbits sub-blocks][128 rows][16 bytes]. Row r of
-// sub-block s of k-block b of tile t holds the export bytes of channel 128 t + r that cover
-// k in [128 b + s * 128 / wbits, ... + 128 / wbits): 16 consecutive bytes of the export row, unchanged
-// (LSB-first codes), zero past the row end. One thread builds one 16-byte panel row and checks its bytes:
-// bits past k = K must be 0, and a 2-bit field must not be 0b11.
+// Panel layout: [ceil(N/128) tiles][ceil(K/128) k-blocks][wbits sub-blocks][4 words][128 rows][4 bytes]. Sub-block s
+// of k-block b of channel row 128 t + r covers k in [128 b + s * 128 / wbits, ... + 128 / wbits): the 16 export bytes
+// of that row starting at byte 16 wbits b + 16 s (LSB-first codes, unchanged; zero past the row end), stored as four
+// little-endian words, word j at (j * 128 + r) * 4 (word-major, so the kernel's per-row word loads hit distinct
+// banks). One thread builds one row of one sub-block and checks its bytes: bits past k = K must be 0, and a 2-bit
+// field must not be 0b11.
 __global__ void __launch_bounds__(256) prepare_panels_kernel(const uint8_t *__restrict__ codes, int row_bytes, int wbits,
-                                                             int N, int K, int kb_total, long long chunks,
+                                                             int N, int K, int kb_total, long long rows_total,
                                                              uint8_t *__restrict__ panels, uint32_t *err) {
-    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= chunks) return;
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;   // (tile, k-block, sub-block, row)
+    if (idx >= rows_total) return;
     const int r = (int)(idx % kPanelN);
     long long rest = idx / kPanelN;
     const int s = (int)(rest % wbits);
@@ -49,7 +50,9 @@ __global__ void __launch_bounds__(256) prepare_panels_kernel(const uint8_t *__re
             words[i >> 2] |= v << (8 * (i & 3));
         }
     }
-    reinterpret_cast<uint4 *>(panels)[idx] = make_uint4(words[0], words[1], words[2], words[3]);
+    uint32_t *dst = reinterpret_cast<uint32_t *>(panels + (idx - r) * 16);   // the sub-block's first byte
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j * kPanelN + r] = words[j];
     if (bad) report(err, bad);
 }
 

@@ -1,18 +1,20 @@
 // gemm_kernel.cuh - the low-bit GEMM for sm_100a.
 //
-// One CTA computes a tile of `tile_m` tokens (1 or 2 tcgen05 M=128 blocks) x `tile_n` output channels (128 or 256,
-// the tcgen05 N) over the k128 blocks of its split of K:
-//   warp 0     producer: per stage one cp.async.bulk per 128-channel panel tile (wbits x 2 KB of packed codes) and
-//              one TMA tile per (token block, activation part) (128 rows x 128 int8, 128-byte swizzle), all
-//              completing on the stage's `full` mbarrier;
-//   warp 1     allocates tensor memory; one thread issues tcgen05.mma.kind::i8 (M = 128 tokens, N = tile_n
-//              channels, K = 32) with A = activations and B = expanded weights, INT32 accumulators in TMEM (one
-//              tile_n-column block per token block and part), and frees each stage with tcgen05.commit;
-//   warps 2-9  expand the packed codes (1 bit -> int8 +-1, 2 bits -> int8 -1/0/+1) into the 128-byte-swizzled
-//              K-major B tile, then run the epilogue: each thread owns one token row of a TMEM lane quarter.
-// Split-K: the `splits` CTAs of a thread-block cluster share one output tile; each copies its INT32 partials from
-// TMEM into its own shared memory, and after a cluster barrier every CTA sums a slice of the channels across the
-// cluster through distributed shared memory (exact INT32, so the order does not matter) and finishes it.
+// One CTA computes `tile_m` tokens (one or two tcgen05 M = 128 blocks) x `tile_n` output channels (32, 64, 128 or
+// 256 = the tcgen05 N) over the k128 blocks of its split of K. 18 warps:
+//   warp 0      producer: per stage the packed codes of the tile's channels (cp.async.bulk from the panels) and one
+//               TMA tile per (token block, activation part): 128 rows x 128 int8, 128-byte swizzle; the copies are
+//               spread over the warp's lanes and complete on the stage's `full` mbarrier;
+//   warp 1      allocates tensor memory; one lane issues tcgen05.mma.kind::i8 (A = activations, B = expanded
+//               weights, INT32 accumulators in TMEM: one tile_n-column block per token block and part) and frees
+//               each stage with tcgen05.commit;
+//   warps 2-17  expand the packed codes (1 bit -> int8 +-1, 2 bits -> int8 -1/0/+1) into the 128-byte-swizzled
+//               K-major B tile, then run the epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, so each thread
+//               owns one token row; the four warps of a lane quarter share its columns.
+// Split-K: the `splits` CTAs of a thread-block cluster share one output tile. Each pushes its INT32 partials of
+// channel group g (4 channels) into the shared memory of the rank that owns g (posted distributed-shared-memory
+// stores), and after one cluster barrier every rank sums its groups from local shared memory and finishes them.
+// INT32 sums are exact, so the result does not depend on the split.
 // Epilogue: comb_P, alpha / bias, optional SiLU; FP32 or FP16 rows stored as 16-byte vectors; optional INT32
 // accumulators.
 #pragma once
@@ -23,19 +25,46 @@
 
 namespace kea {
 
-constexpr int kThreads = 320;            // 10 warps
-constexpr int kEpiThreads = 256;         // warps 2-9
+constexpr int kWarps = 18;
+constexpr int kThreads = kWarps * 32;    // 576
+constexpr int kEpiWarps = 16;            // warps 2-17
+constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kBM = 128;                 // tokens per tcgen05 M block
 constexpr int kPanelN = 128;             // channels per panel tile
 constexpr int kBK = 128;                 // k per stage: one 128-byte swizzled row of int8
 constexpr int kMaxStages = 8;
 constexpr int kMaxTileN = 256;
 constexpr int kActTileBytes = kBM * kBK;                 // 16 KB per (token block, part)
-constexpr int kPanelRowBytes = 16;
-constexpr int kPanelSubBytes = kPanelN * kPanelRowBytes;   // 2 KB per sub-block (wbits sub-blocks per k128)
+constexpr int kPanelSubBytes = kPanelN * 16;               // 2 KB per panel sub-block (wbits sub-blocks per k128)
 constexpr long long kWaitBudget = 4000000000LL;            // SM clocks (about 2 s) before a wait gives up
 
 __device__ uint32_t g_device_error;  // the library's own error word (KEA_DEVERR_* bits)
+
+// Phase timestamps for latency studies: compiled in only with -DKEA_TRACE (one %globaltimer value per CTA and
+// phase, read back by kea_trace_read). The default build has no trace code.
+#ifdef KEA_TRACE
+// Phase 0 holds the CTA's start as %globaltimer ns (slow to read, so read once); the other phases hold SM clock
+// cycles since that start (clock64 is cheap and the whole CTA runs on one SM). The start clock lives in shared
+// memory (written before the kernel's first __syncthreads), so a trace point costs a clock read and one store.
+constexpr int kTraceCtas = 4096, kTracePhases = 32;
+__device__ unsigned long long g_trace[kTraceCtas][kTracePhases];
+__shared__ long long s_trace_clock0;
+KEA_DEVI void trace_point(int phase) {
+    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (cta >= kTraceCtas) return;
+    if (phase == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        s_trace_clock0 = clock64();
+        g_trace[cta][0] = t;
+    } else {
+        g_trace[cta][phase] = (unsigned long long)(clock64() - s_trace_clock0);
+    }
+}
+#define KEA_TRACE_POINT(cond, phase) do { if (cond) trace_point(phase); } while (0)
+#else
+#define KEA_TRACE_POINT(cond, phase) do { } while (0)
+#endif
 
 struct GemmArgs {
     const uint8_t *panels;
@@ -50,25 +79,49 @@ struct GemmArgs {
     long long ld_acc;
     long long acc_stride;
     int M, N, K;
-    int parts, tile_n, tm_blocks, splits, stages, kb_total;
+    int tile_n, tm_blocks, splits, stages, kb_total;
     int flags;
+    int pdl;                     // launched with programmatic dependent launch: wait for the previous grid
     int vec_y, vec_acc;          // 16-byte vector stores allowed (base and row stride aligned)
+    uint32_t recv_off;           // split-K receive buffer offset in dynamic shared memory
+    int recv_aliases_stages;     // 1: the receive buffer reuses the stage area (peers must finish first)
+    int tma_store;               // 1: stage y in shared memory and write it with TMA stores (ymap is valid)
+    int store_swizzle;           // ymap's swizzle span in bytes (64 or 128) = one warp's staged row
     uint32_t tmem_cols;
-    uint32_t stage_bytes;
+    uint32_t a_stage, b_stage, pk_stage;   // bytes per stage of the activation / expanded-weight / packed regions
+    uint32_t b_region, pk_region;         // region offsets in dynamic shared memory (the activation region is at 0)
+    int q4d;                     // qmap is 4-D (k in block, row, k-block, part) with 128 * tm_blocks-row boxes
+    int oneshot;                 // the whole K range of the CTA arrives at once on bar_full[0] (two TMA boxes)
+    int kbox;                    // k-blocks per activation / panel box in one-shot mode
+    uint32_t act_tx;             // activation bytes one stage receives (boxes shrink to the rows that exist)
+    int nacc;                    // independent accumulators per (token block, part): 1, or 4 for narrow tiles (one per
+                                 // K = 32 step, summed in the epilogue) so back-to-back MMAs do not wait on each other
+    uint32_t a_stride;           // distance between consecutive stages' activation tiles (one-shot boxes are dense:
+                                 // rows * 128 bytes; the MMA's reads past a short tile only reach unstored rows)
     uint32_t *err;
 };
 
 // ---- weight expansion --------------------------------------------------------------------------------------
-// `rep` holds one packed byte in all four byte lanes; `mask` selects a single bit per lane. Returns 1 in
-// every byte lane whose selected bit is set, else 0 (each lane stays below 0x100, so no carries).
-KEA_DEVI uint32_t lane_bits(uint32_t rep, uint32_t mask) { return (((rep & mask) + 0x7F7F7F7Fu) >> 7) & 0x01010101u; }
-// 1-bit codes: 1 -> int8 +1 (0x01), 0 -> int8 -1 (0xFF).
-KEA_DEVI uint32_t sign_lanes(uint32_t ones) { return ones | ((ones ^ 0x01010101u) * 0xFFu); }
-// 2-bit codes: 01 -> +1, 10 -> -1, 00 -> 0 for the four fields of `rep`'s byte.
-KEA_DEVI uint32_t ternary_lanes(uint32_t rep) {
-    return lane_bits(rep, 0x40100401u) | (lane_bits(rep, 0x80200802u) * 0xFFu);
+KEA_DEVI uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
 }
-KEA_DEVI uint32_t byte_in_all_lanes(uint32_t word, uint32_t i) { return __byte_perm(word, 0, i * 0x1111u); }
+// Lane i of the result is 0xFF when bit 7 of lane i of x is set, else 0x00 (prmt's sign-replicating selectors).
+KEA_DEVI uint32_t lane_sign(uint32_t x) { return prmt(x, 0, 0xBA98u); }
+// 1-bit codes 4h .. 4h+3 of the byte replicated in `rep` (LSB first): code 1 -> int8 +1 (0x01), code 0 -> -1 (0xFF).
+// Lane i keeps only its code's bit; adding 0x7F moves it to bit 7 without carrying into the next lane.
+KEA_DEVI uint32_t signs4(uint32_t rep, int h) {
+    const uint32_t t = (rep & (h ? 0x80402010u : 0x08040201u)) + 0x7F7F7F7Fu;
+    return ~lane_sign(t) | 0x01010101u;
+}
+// 2-bit codes of the byte replicated in `rep`: field i at bits 2i (+1) and 2i+1 (-1); 00 -> 0.
+KEA_DEVI uint32_t ternary4(uint32_t rep) {
+    const uint32_t plus = (rep & 0x40100401u) + 0x7F7F7F7Fu;
+    const uint32_t minus = (rep & 0x80200802u) + 0x7F7F7F7Fu;
+    return lane_sign(minus) | ((plus >> 7) & 0x01010101u);
+}
+KEA_DEVI uint32_t byte_rep(uint32_t word, int k) { return prmt(word, 0, (uint32_t)k * 0x1111u); }
 
 KEA_DEVI void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
@@ -78,56 +131,36 @@ KEA_DEVI uint4 ld_shared_v4(uint32_t addr) {
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
     return v;
 }
-KEA_DEVI uint2 ld_shared_v2(uint32_t addr) {
-    uint2 v;
-    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
+KEA_DEVI uint32_t ld_shared_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
     return v;
 }
-KEA_DEVI int4 ld_cluster_v4(uint32_t addr) {
-    int4 v;
-    asm volatile("ld.shared::cluster.v4.s32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
-    return v;
+KEA_DEVI void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
-// Expands chunks [c0, c0 + NCH) (16 codes each) of channel row `row` of one k128 stage. Packed codes of row r of
-// a 128-channel panel tile: sub-block s at pk + s * 2048 + (r % 128) * 16, where pk is the tile's packed area.
-// Output: the int8 B tile at `dst`, row r at r * 128, 16-byte chunk c stored at chunk c ^ (r & 7).
-template <int WBITS, int NCH>
-KEA_DEVI void expand_chunks(uint32_t pk, uint32_t dst, int row, int c0) {
-    const uint32_t rowbase = dst + row * 128;
-    const uint32_t sw = row & 7;
+// Packed codes of one stage in shared memory: [panel tile][sub-block s][word j][R rows][4 bytes], R = min(tile_n,
+// 128) (the panels' own word-major order). Word j of sub-block s of a channel row holds (1 bit) codes 32 j .. + 31,
+// (2 bits) codes 64 s + 16 j .. + 15. Unit u expands channel row r = u % tile_n: 1 bit - word j = u / tile_n
+// (chunks 2 j and 2 j + 1); 2 bits - chunk c = u / tile_n (word c % 4 of sub-block c / 4). A chunk is 16 codes =
+// 16 bytes of the B tile, stored at chunk position c ^ (r & 7) of row r (128-byte swizzle). tn_log2 = log2(tile_n).
+template <int WBITS>
+KEA_DEVI void expand_unit(uint32_t pk, uint32_t dst, int tn_log2, int u) {
+    // tile_n and R are powers of two: shifts and masks, never integer division, on this hot path
+    const int r_log2 = tn_log2 < 7 ? tn_log2 : 7;          // R = min(tile_n, 128)
+    const int r = u & ((1 << tn_log2) - 1), q = u >> tn_log2;
+    const int pt = r >> r_log2, rr = r & ((1 << r_log2) - 1);
+    const uint32_t rowbase = dst + (uint32_t)r * 128;
+    const uint32_t sw = (uint32_t)(r & 7);
+    const uint32_t w = ld_shared_u32(pk + ((uint32_t)((((pt * (4 * WBITS) + q) << r_log2) | rr)) << 2));
     if constexpr (WBITS == 1) {
-        // chunks c0..c0+NCH-1 are packed bytes 2 c0 .. 2 (c0 + NCH) - 1 (LSB first)
-        uint32_t w[NCH / 2];
-        if constexpr (NCH == 8) {
-            const uint4 v = ld_shared_v4(pk + row * kPanelRowBytes);
-            w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-        } else {
-            const uint2 v = ld_shared_v2(pk + row * kPanelRowBytes + 2 * c0);
-            w[0] = v.x; w[1] = v.y;
-        }
-#pragma unroll
-        for (int i = 0; i < NCH; ++i) {
-            const uint32_t word = w[i >> 1];
-            const uint32_t r0 = byte_in_all_lanes(word, 2 * (i & 1)), r1 = byte_in_all_lanes(word, 2 * (i & 1) + 1);
-            st_shared_v4(rowbase + (((c0 + i) ^ sw) << 4), sign_lanes(lane_bits(r0, 0x08040201u)),
-                         sign_lanes(lane_bits(r0, 0x80402010u)), sign_lanes(lane_bits(r1, 0x08040201u)),
-                         sign_lanes(lane_bits(r1, 0x80402010u)));
-        }
+        const uint32_t b0 = byte_rep(w, 0), b1 = byte_rep(w, 1), b2 = byte_rep(w, 2), b3 = byte_rep(w, 3);
+        st_shared_v4(rowbase + (((uint32_t)(2 * q) ^ sw) << 4), signs4(b0, 0), signs4(b0, 1), signs4(b1, 0), signs4(b1, 1));
+        st_shared_v4(rowbase + (((uint32_t)(2 * q + 1) ^ sw) << 4), signs4(b2, 0), signs4(b2, 1), signs4(b3, 0), signs4(b3, 1));
     } else {
-        // chunk c: sub-block c / 4 (64 codes), packed word c % 4 of it (4 codes per byte)
-#pragma unroll
-        for (int h = 0; h < NCH / 4; ++h) {
-            const int sub = c0 / 4 + h;
-            const uint4 v = ld_shared_v4(pk + sub * kPanelSubBytes + row * kPanelRowBytes);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                st_shared_v4(rowbase + (((sub * 4 + i) ^ sw) << 4), ternary_lanes(byte_in_all_lanes(w[i], 0)),
-                             ternary_lanes(byte_in_all_lanes(w[i], 1)), ternary_lanes(byte_in_all_lanes(w[i], 2)),
-                             ternary_lanes(byte_in_all_lanes(w[i], 3)));
-            }
-        }
+        st_shared_v4(rowbase + (((uint32_t)q ^ sw) << 4), ternary4(byte_rep(w, 0)), ternary4(byte_rep(w, 1)),
+                     ternary4(byte_rep(w, 2)), ternary4(byte_rep(w, 3)));
     }
 }
 
@@ -153,8 +186,8 @@ KEA_DEVI uint32_t pack_half2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-// Finishes and stores `cnt` (a multiple of 4, <= 16) consecutive channels n .. of token t from acc[p][0..cnt).
-// Channel-indexed constants come from shared memory (s_alpha / s_bias at tile column c).
+// Finishes and stores CNT (4 or 16) consecutive channels n .. of token t from acc[p][0..CNT). Channel constants
+// come from shared memory (s_alpha / s_bias at tile column c).
 template <int P, int CNT>
 KEA_DEVI void finish_store(const GemmArgs &a, int t, int n, int c, const int (&acc)[P][CNT], const float (&s)[P],
                            const float *s_alpha, const float *s_bias) {
@@ -213,6 +246,21 @@ KEA_DEVI void finish_store(const GemmArgs &a, int t, int n, int c, const int (&a
     }
 }
 
+// 16 columns of accumulator block `blk` (nacc partial accumulators of TN columns each, summed exactly).
+KEA_DEVI void load_acc16(uint32_t lane_addr, int blk, int nacc, int TN, int c, uint32_t (&v)[16]) {
+    const uint32_t col = (uint32_t)(blk * nacc * TN + c);
+    tmem_ld16(lane_addr + col, v);
+    if (nacc > 1) {
+        uint32_t w1[16], w2[16], w3[16];
+        tmem_ld16(lane_addr + col + (uint32_t)TN, w1);
+        tmem_ld16(lane_addr + col + (uint32_t)(2 * TN), w2);
+        tmem_ld16(lane_addr + col + (uint32_t)(3 * TN), w3);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = v[j] + w1[j] + w2[j] + w3[j];
+    }
+}
+
 KEA_DEVI void named_barrier_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -220,7 +268,9 @@ KEA_DEVI void named_barrier_sync(uint32_t id, uint32_t threads) {
 KEA_DEVI void report(uint32_t *err, uint32_t bits) { atomicOr(err ? err : &g_device_error, bits); }
 
 template <int WBITS, int P>
-__global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_constant__ CUtensorMap qmap, const GemmArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                   const __grid_constant__ CUtensorMap ymap,
+                                                                   const __grid_constant__ CUtensorMap wmap, const GemmArgs a) {
     extern __shared__ uint8_t dyn_smem[];
     __shared__ __align__(8) uint64_t bar_full[kMaxStages];
     __shared__ __align__(8) uint64_t bar_exp[kMaxStages];
@@ -235,27 +285,33 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
     const uint32_t raw = smem_u32(dyn_smem);
     const uint32_t base = (raw + 1023u) & ~1023u;   // 128-byte swizzle atoms need 1024-byte alignment
     const int TN = a.tile_n, TMB = a.tm_blocks;
+    const int tn_log2 = 31 - __clz(TN);
     const int n0 = blockIdx.x * TN, t0 = blockIdx.y * (TMB * kBM);
     const int rank = a.splits > 1 ? (int)cluster_ctarank() : 0;
     const int kb0 = (int)((long long)a.kb_total * rank / a.splits);
     const int kb1 = (int)((long long)a.kb_total * (rank + 1) / a.splits);
     const int nkb = kb1 - kb0;
     const int S = a.stages;
-    const int ptiles = TN / kPanelN;                            // 128-channel panel tiles per CTA
-    const uint32_t b_off = (uint32_t)(TMB * P) * kActTileBytes;  // expanded weights after the activation tiles
-    const uint32_t pk_off = b_off + (uint32_t)TN * kBK;          // packed codes after the expanded weights
-    const uint32_t pk_tile_bytes = WBITS * kPanelSubBytes;
-    const uint32_t tx_bytes = (uint32_t)(TMB * P) * kActTileBytes + (uint32_t)ptiles * pk_tile_bytes;
+    const int R = TN < kPanelN ? TN : kPanelN;             // channel rows taken from one panel tile
+    const int ptiles = TN / R;                              // panel tiles per CTA (2 when TN = 256)
+    // Shared memory: [activation tiles: S x a_stage][expanded weights: S x b_stage][packed codes: S x pk_stage].
+    // Stage s: activation tile of (part p, token block tb) at a(s) + (p * TMB + tb) * 16 KB (a part's token blocks
+    // are adjacent, so one 256-row TMA box fills both), B tile at b(s), packed codes at pk(s).
+    const uint32_t A0 = base, B0 = base + a.b_region, PK0 = base + a.pk_region;
+    const uint32_t tx_bytes = a.act_tx + a.pk_stage;
 
+    KEA_TRACE_POINT(threadIdx.x == 0, 0);
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&bar_full[s]), 1);
-            mbar_init(smem_u32(&bar_exp[s]), kEpiThreads / 32);
+            mbar_init(smem_u32(&bar_exp[s]), kEpiWarps);
             mbar_init(smem_u32(&bar_empty[s]), 1);
         }
         mbar_init(smem_u32(&bar_acc), 1);
         fence_barrier_init();
         prefetch_tensormap(&qmap);
+        if (a.tma_store) prefetch_tensormap(&ymap);
+        if (a.oneshot) prefetch_tensormap(&wmap);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(&tmem_slot), a.tmem_cols);
@@ -265,70 +321,138 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
+    KEA_TRACE_POINT(threadIdx.x == 0, 1);
 
-    // Everything below may read what the previous kernel in the stream wrote.
-    grid_dependency_wait();
+    // With programmatic dependent launch, everything below may read what the previous kernel wrote.
+    if (a.pdl) grid_dependency_wait();
 
     bool ok = true;
     if (warp == 0) {
-        // ---------------- producer ----------------
-        if (lane == 0) {
-            const size_t tile_stride = (size_t)a.kb_total * pk_tile_bytes;
-            const uint8_t *wsrc = a.panels + (size_t)(n0 / kPanelN) * tile_stride;
-            int issued = 0;
-            for (int i = 0; i < nkb; ++i) {
-                const int s = i % S;
-                if (i >= S && !mbar_wait(smem_u32(&bar_empty[s]), ((i / S) - 1) & 1, kWaitBudget)) {
+        // ---------------- producer: the whole warp waits and issues (the warp stays converged) ----------------
+        // Panels: [tile][k-block][sub-block][word][128 rows][4 bytes]; this CTA's rows start at n0 % 128.
+        const size_t kblock_bytes = (size_t)WBITS * kPanelSubBytes;
+        const size_t tile_bytes = (size_t)a.kb_total * kblock_bytes;
+        const uint8_t *wsrc = a.panels + (size_t)(n0 / kPanelN) * tile_bytes + (size_t)(n0 % kPanelN) * 4;
+        // CTAs that share token rows start at different k-blocks, so they do not all read the same activation
+        // lines at once (INT32 accumulation makes the order free).
+        const int rot = nkb > 0 ? (int)(blockIdx.x % (unsigned)nkb) : 0;
+        const int pk_copies = R == kPanelN ? ptiles : WBITS * 4;
+        const int act_copies = a.q4d ? P : TMB * P;
+        const int ncopies = pk_copies + act_copies;   // <= 14
+        int issued = 0;
+        if (a.oneshot) {
+            // Every k-block of this CTA at once: one TMA box of the panels (kbox k-blocks x wbits x 4 word planes
+            // of this CTA's R rows) and one 4-D box of activations (128 rows x kbox k-blocks), both on bar_full[0].
+            if (lane == 0) {
+                const uint32_t full = smem_u32(&bar_full[0]);
+                mbar_arrive_expect_tx(full, (uint32_t)a.kbox * tx_bytes);
+                const int plane0 = ((n0 / kPanelN) * a.kb_total + kb0) * WBITS * 4;
+                tma_load_2d(PK0, &wmap, full, (n0 % kPanelN) * 4, plane0);
+                tma_load_4d(A0, &qmap, full, 0, t0, kb0, 0);
+            }
+            __syncwarp();
+            issued = nkb;
+        }
+        int s = 0, ph = 0, kbi = rot;   // stage slot, its round parity, k-block offset (incremental: no division)
+        for (int i = 0; i < (a.oneshot ? 0 : nkb); ++i) {
+            if (i >= S) {
+                const bool freed = mbar_wait(smem_u32(&bar_empty[s]), (uint32_t)(ph ^ 1), kWaitBudget);
+                if (!__all_sync(0xFFFFFFFFu, freed)) {
                     ok = false;
                     break;
                 }
-                const uint32_t st = base + (uint32_t)s * a.stage_bytes;
-                const uint32_t full = smem_u32(&bar_full[s]);
-                const int kb = kb0 + i;
-                mbar_arrive_expect_tx(full, tx_bytes);
-                for (int pt = 0; pt < ptiles; ++pt)
-                    bulk_load(st + pk_off + pt * pk_tile_bytes, wsrc + pt * tile_stride + (size_t)kb * pk_tile_bytes,
-                              pk_tile_bytes, full);
-                for (int tb = 0; tb < TMB; ++tb)
-                    for (int p = 0; p < P; ++p)
-                        tma_load_3d(st + (tb * P + p) * kActTileBytes, &qmap, full, kb * kBK, t0 + tb * kBM, p);
-                issued = i + 1;
             }
-            if (!ok) {
-                report(a.err, 1u);
-                for (int i = (issued > S ? issued - S : 0); i < issued; ++i)   // let issued copies land first
-                    mbar_wait(smem_u32(&bar_full[i % S]), (i / S) & 1, kWaitBudget);
+            // One lane arms the stage's barrier; then the stage's copies are spread over the warp's lanes
+            // (round-robin across stages): issuing a bulk copy holds its thread for a while, so one issuing
+            // lane would starve the tensor cores.
+            const uint32_t sa = A0 + (uint32_t)s * a.a_stride, spk = PK0 + (uint32_t)s * a.pk_stage;
+            const uint32_t full = smem_u32(&bar_full[s]);
+            const int kb = kb0 + kbi;
+            if (lane == 0) mbar_arrive_expect_tx(full, tx_bytes);
+            __syncwarp();
+            const int c = (lane - i * ncopies) & 31;   // this lane's copy index in stage i (valid when < ncopies)
+            if (c < ncopies) {
+                if (c < pk_copies) {
+                    if (R == kPanelN)        // whole sub-blocks of one or two panel tiles
+                        bulk_load(spk + c * kblock_bytes, wsrc + c * tile_bytes + (size_t)kb * kblock_bytes,
+                                  (uint32_t)kblock_bytes, full);
+                    else                     // R rows of one word plane
+                        bulk_load(spk + c * R * 4, wsrc + (size_t)kb * kblock_bytes + (size_t)c * kPanelN * 4,
+                                  (uint32_t)(R * 4), full);
+                } else if (a.q4d) {          // one box of 128 * TMB rows per part
+                    const int p = c - pk_copies;
+                    tma_load_4d(sa + p * TMB * kActTileBytes, &qmap, full, 0, t0, kb, p);
+                } else {                     // one 128-row box per (part, token block)
+                    const int blk = c - pk_copies, p = blk / TMB, tb = blk - p * TMB;
+                    tma_load_3d(sa + blk * kActTileBytes, &qmap, full, kb * kBK, t0 + tb * kBM, p);
+                }
             }
+            __syncwarp();
+            issued = i + 1;
+            KEA_TRACE_POINT(lane == 0 && i == 0, 2);
+            if (++kbi == nkb) kbi = 0;
+            if (++s == S) {
+                s = 0;
+                ph ^= 1;
+            }
+        }
+        KEA_TRACE_POINT(lane == 0, 3);
+        if (!ok) {
+            if (lane == 0) report(a.err, 1u);
+            for (int i = (issued > S ? issued - S : 0); i < issued; ++i)   // let issued copies land first
+                mbar_wait(smem_u32(&bar_full[a.oneshot ? 0 : i % S]), a.oneshot ? 0 : (i / S) & 1, kWaitBudget);
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            const uint32_t idesc = idesc_i8(kBM, (uint32_t)TN);
-            for (int i = 0; i < nkb; ++i) {
-                const int s = i % S;
-                const uint32_t ph = (i / S) & 1;
-                if (!mbar_wait(smem_u32(&bar_full[s]), ph, kWaitBudget) || !mbar_wait(smem_u32(&bar_exp[s]), ph, kWaitBudget)) {
-                    ok = false;
-                    report(a.err, 1u);
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t st = base + (uint32_t)s * a.stage_bytes;
+        // ---------------- MMA issuer: the whole warp waits, lane 0 issues ----------------
+        const uint32_t idesc = idesc_i8(kBM, (uint32_t)TN);
+        int s = 0;
+        uint32_t ph = 0;
+        for (int i = 0; i < nkb; ++i) {
+            const bool ready = mbar_wait(smem_u32(&bar_full[a.oneshot ? 0 : s]), a.oneshot ? 0 : ph, kWaitBudget) &&
+                               mbar_wait(smem_u32(&bar_exp[s]), ph, kWaitBudget);
+            if (!__all_sync(0xFFFFFFFFu, ready)) {
+                ok = false;
+                if (lane == 0) report(a.err, 1u);
+                break;
+            }
+            KEA_TRACE_POINT(lane == 0 && i == 0, 6);
+            KEA_TRACE_POINT(lane == 0 && i == nkb - 1, 14);
+            KEA_TRACE_POINT(lane == 0 && i < 8, 23 + i);
+            // The mbarrier wait orders the operands (TMA writes, or expander writes behind fence.proxy.async) before
+            // the MMAs' shared-memory reads; no tcgen05 fence per stage (it would drain the MMA pipe).
+            if (lane == 0) {
+                const uint32_t sa = A0 + (uint32_t)s * a.a_stride, sb = B0 + (uint32_t)s * a.b_stage;
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    const uint64_t bd = sw128_kmajor_desc(st + b_off + kk * 32);
-                    for (int blk = 0; blk < TMB * P; ++blk) {
-                        const uint64_t ad = sw128_kmajor_desc(st + blk * kActTileBytes + kk * 32);
-                        mma_i8(tmem + (uint32_t)(blk * TN), ad, bd, idesc, (i | kk) != 0 ? 1u : 0u);
+                    const uint64_t bd = sw128_kmajor_desc(sb + kk * 32);
+#pragma unroll
+                    for (int p = 0; p < P; ++p) {
+#pragma unroll
+                        for (int tb = 0; tb < 2; ++tb) {
+                            if (tb < TMB) {
+                                const uint64_t ad = sw128_kmajor_desc(sa + (p * TMB + tb) * kActTileBytes + kk * 32);
+                                const int acc = a.nacc > 1 ? kk : 0;
+                                mma_i8(tmem + (uint32_t)(((tb * P + p) * a.nacc + acc) * TN), ad, bd, idesc,
+                                       (i != 0 || kk > acc) ? 1u : 0u);
+                            }
+                        }
                     }
                 }
+                KEA_TRACE_POINT(i == 0, 7);
                 mma_commit(smem_u32(&bar_empty[s]));
             }
-            mma_commit(smem_u32(&bar_acc));
+            __syncwarp();
+            if (++s == S) {
+                s = 0;
+                ph ^= 1u;
+            }
         }
+        if (lane == 0) mma_commit(smem_u32(&bar_acc));
+        __syncwarp();
+        KEA_TRACE_POINT(lane == 0, 8);
     } else {
         // ---------------- expanders ----------------
-        const int e = threadIdx.x - 64;   // 0 .. 255
+        const int e = threadIdx.x - 64;   // 0 .. 511
         for (int i = e; i < P * TMB * kBM; i += kEpiThreads) {
             const int p = i / (TMB * kBM), t = t0 + (i - p * TMB * kBM);
             s_qs[i] = t < a.M ? a.qs[p * a.qs_stride + t] : 0.f;
@@ -338,53 +462,127 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
             s_alpha[i] = n < a.N ? a.alpha[n] : 0.f;
             s_bias[i] = (a.bias && n < a.N) ? a.bias[n] : 0.f;
         }
+        const int units = TN * (WBITS == 1 ? 4 : 8);
+        int s = 0;
+        uint32_t ph = 0;
         for (int i = 0; i < nkb; ++i) {
-            const int s = i % S;
-            bool landed = mbar_wait(smem_u32(&bar_full[s]), (i / S) & 1, kWaitBudget);
+            const bool landed = mbar_wait(smem_u32(&bar_full[a.oneshot ? 0 : s]), a.oneshot ? 0u : ph, kWaitBudget);
             if (!__all_sync(0xFFFFFFFFu, landed)) {
                 ok = false;
                 if (lane == 0) report(a.err, 1u);
                 break;
             }
-            const uint32_t st = base + (uint32_t)s * a.stage_bytes;
-            if (TN == 128) {      // two threads per channel row, four chunks each
-                const int row = e & 127, half = e >> 7;
-                expand_chunks<WBITS, 4>(st + pk_off, st + b_off, row, half * 4);
-            } else {              // one thread per channel row of the two panel tiles
-                // packed row of channel e: tile e / 128, row e % 128 (expand_chunks adds e * 16)
-                const uint32_t pk = st + pk_off + (uint32_t)(e >> 7) * (pk_tile_bytes - kPanelSubBytes);
-                expand_chunks<WBITS, 8>(pk, st + b_off, e, 0);
-            }
+            KEA_TRACE_POINT(threadIdx.x == 64 && i == 0, 4);
+            KEA_TRACE_POINT(threadIdx.x == 64 && i < 8, 15 + i);
+            const uint32_t spk = PK0 + (uint32_t)s * a.pk_stage, sb = B0 + (uint32_t)s * a.b_stage;
+            for (int u = e; u < units; u += kEpiThreads) expand_unit<WBITS>(spk, sb, tn_log2, u);
             fence_async_shared();
+            KEA_TRACE_POINT(threadIdx.x == 64 && i == 0, 5);
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&bar_exp[s]));
+            if (++s == S) {
+                s = 0;
+                ph ^= 1u;
+            }
         }
     }
 
-    // ---------------- epilogue (warps 2-9) ----------------
-    const int quad = warp & 3;                  // the TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;           // which of the two warps on this quarter
+    // ---------------- epilogue (warps 2-17) ----------------
+    // Warp w may read TMEM lanes 32 (w % 4) .. + 31; the four warps of a lane quarter take 16-column chunks
+    // sub, sub + 4, ... of every block.
+    const int quad = warp & 3;
+    const int sub = (warp - 2) >> 2;
     const int row = quad * 32 + lane;           // token row within a 128-token block
     const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
-    uint32_t red = base;                        // split-K exchange buffer (reuses the stage area)
+    const int chunks = TN / 16;
+    const uint32_t recv = base + a.recv_off;    // split-K receive buffer
+    if (warp < 2 && a.splits > 1 && a.recv_aliases_stages) {   // matches the epilogue warps' early barrier
+        cluster_arrive();
+        cluster_wait();
+    }
     if (warp >= 2) {
         named_barrier_sync(1, kEpiThreads);     // s_qs / s_alpha / s_bias complete
         bool done = ok && mbar_wait(smem_u32(&bar_acc), 0, kWaitBudget);
         done = __all_sync(0xFFFFFFFFu, done);
         if (!done && ok && lane == 0) report(a.err, 1u);
+        KEA_TRACE_POINT(threadIdx.x == 64, 9);
         tc_fence_after();
-        if (a.splits == 1) {
+        if (a.splits == 1 && a.tma_store) {
+            // Each warp stages its 32 token rows x W = TN / 4 channels of y (64 or 128 bytes a row, swizzled like the
+            // store's tensor map) in the free stage area, then one lane stores the box with TMA: a few bulk stores
+            // instead of thousands of scattered 16-byte ones.
+            if (done) {
+                const int W = TN / 4, c_lo = sub * W;
+                const uint32_t row_bytes = (uint32_t)a.store_swizzle;             // = W * element size
+                const uint32_t sw_mask = row_bytes == 128 ? 7u : 3u;
+                const bool has_bias = a.bias != nullptr;
+                for (int tb = 0; tb < TMB; ++tb) {
+                    const int t = t0 + tb * kBM + row;
+                    const uint32_t stg = base + (uint32_t)((tb * kEpiWarps + (warp - 2)) * 32) * row_bytes;
+                    float s[P];
+#pragma unroll
+                    for (int p = 0; p < P; ++p) s[p] = s_qs[p * TMB * kBM + tb * kBM + row];
+                    for (int c16 = 0; c16 < W; c16 += 16) {
+                        const int c = c_lo + c16;
+                        uint32_t v[P][16];
+#pragma unroll
+                        for (int p = 0; p < P; ++p) load_acc16(lane_addr, tb * P + p, a.nacc, TN, c, v[p]);
+                        tmem_wait_ld();
+                        float f[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            f[j] = finish_value((int)v[0][j], P > 1 ? (int)v[P > 1 ? 1 : 0][j] : 0,
+                                                P > 2 ? (int)v[P > 2 ? 2 : 0][j] : 0, s[0], P > 1 ? s[P > 1 ? 1 : 0] : 0.f,
+                                                P > 2 ? s[P > 2 ? 2 : 0] : 0.f, P, a.flags, s_alpha[c + j], has_bias,
+                                                has_bias ? s_bias[c + j] : 0.f);
+                        // 16 values = 32 bytes (fp16) or 64 bytes (fp32) of this thread's staged row
+                        if (a.y_f16) {
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const uint32_t off = (uint32_t)lane * row_bytes + (uint32_t)(c16 * 2 + h * 16);
+                                const uint32_t phys = off ^ (((off >> 7) & sw_mask) << 4);
+                                st_shared_v4(stg + phys, pack_half2(f[8 * h], f[8 * h + 1]), pack_half2(f[8 * h + 2], f[8 * h + 3]),
+                                             pack_half2(f[8 * h + 4], f[8 * h + 5]), pack_half2(f[8 * h + 6], f[8 * h + 7]));
+                            }
+                        } else {
+#pragma unroll
+                            for (int h = 0; h < 4; ++h) {
+                                const uint32_t off = (uint32_t)lane * row_bytes + (uint32_t)(c16 * 4 + h * 16);
+                                const uint32_t phys = off ^ (((off >> 7) & sw_mask) << 4);
+                                st_shared_v4(stg + phys, __float_as_uint(f[4 * h]), __float_as_uint(f[4 * h + 1]),
+                                             __float_as_uint(f[4 * h + 2]), __float_as_uint(f[4 * h + 3]));
+                            }
+                        }
+                        if (a.acc && t < a.M) {
+#pragma unroll
+                            for (int p = 0; p < P; ++p)
+#pragma unroll
+                                for (int j = 0; j < 16; ++j)
+                                    if (n0 + c + j < a.N) a.acc[p * a.acc_stride + (long long)t * a.ld_acc + n0 + c + j] = (int)v[p][j];
+                        }
+                    }
+                    fence_async_shared();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&ymap, stg, n0 + c_lo, t0 + tb * kBM + quad * 32);
+                        bulk_commit_group();
+                    }
+                }
+                if (lane == 0) bulk_wait_group0();   // the stores have read shared memory and landed
+                __syncwarp();
+            }
+        } else if (a.splits == 1) {
             if (done) {
                 for (int tb = 0; tb < TMB; ++tb) {
                     const int t = t0 + tb * kBM + row;
                     float s[P];
 #pragma unroll
                     for (int p = 0; p < P; ++p) s[p] = s_qs[p * TMB * kBM + tb * kBM + row];
-                    // 16-column chunks of this block, alternating between the two warps of the quarter
-                    for (int c = half * 16; c < TN; c += 32) {
+                    for (int ch = sub; ch < chunks; ch += 4) {
+                        const int c = ch * 16;
                         uint32_t v[P][16];
 #pragma unroll
-                        for (int p = 0; p < P; ++p) tmem_ld16(lane_addr + (uint32_t)((tb * P + p) * TN + c), v[p]);
+                        for (int p = 0; p < P; ++p) load_acc16(lane_addr, tb * P + p, a.nacc, TN, c, v[p]);
                         tmem_wait_ld();
                         if (t < a.M && n0 + c < a.N) {
                             int accv[P][16];
@@ -398,60 +596,75 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                 }
             }
         } else {
-            // partials -> red: [block = tb * P + p][channel group g = c / 4][row][4] int32 (16-byte rows)
+            // Push this CTA's INT32 partials to the rank that finishes them: channel group g (4 channels) belongs
+            // to rank g / per; its receive buffer holds [source rank][block][group - first group of the owner]
+            // [row] x 16 bytes. Remote stores are posted; the cluster barrier below makes them visible.
+            const int groups = TN / 4;
+            const int per = (groups + a.splits - 1) / a.splits;
+            // owner = g / per by a reciprocal (exact for g < 1024, per <= 64): no division per group
+            const uint32_t inv_per = (65536u + (uint32_t)per - 1u) / (uint32_t)per;
             const int blocks = TMB * P;
+            if (a.recv_aliases_stages) {   // peers may still be in their main loops: wait until every CTA is done
+                cluster_arrive();
+                cluster_wait();
+            }
             for (int blk = 0; blk < blocks; ++blk) {
-                for (int c = half * 16; c < TN; c += 32) {
+                const bool live = t0 + (blk / P) * kBM + row < a.M;   // rows past M are never read by the owner
+                for (int ch = sub; ch < chunks; ch += 4) {
                     uint32_t v[16];
                     if (done) {
-                        tmem_ld16(lane_addr + (uint32_t)(blk * TN + c), v);
+                        load_acc16(lane_addr, blk, a.nacc, TN, ch * 16, v);
                         tmem_wait_ld();
                     } else {
 #pragma unroll
                         for (int j = 0; j < 16; ++j) v[j] = 0;
                     }
+                    if (live) {
 #pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        const uint32_t addr = red + (uint32_t)((((blk * (TN / 4) + c / 4 + g) * kBM) + row) * 16);
-                        st_shared_v4(addr, v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+                        for (int q = 0; q < 4; ++q) {
+                            const int g = ch * 4 + q;
+                            const int owner = (int)(((uint32_t)g * inv_per) >> 16);
+                            const uint32_t local =
+                                recv + (uint32_t)((((rank * blocks + blk) * per + (g - owner * per)) * kBM + row) * 16);
+                            if (owner == rank)
+                                st_shared_v4(local, v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                            else
+                                st_cluster_v4(map_to_rank(local, (uint32_t)owner), v[4 * q], v[4 * q + 1], v[4 * q + 2],
+                                              v[4 * q + 3]);
+                        }
                     }
                 }
             }
         }
     }
 
+    KEA_TRACE_POINT(threadIdx.x == 64, 10);
     if (a.splits > 1) {
-        cluster_sync_all();  // every CTA's partials are in its shared memory
+        cluster_sync_all();  // every partial has landed in its owner's shared memory
+        KEA_TRACE_POINT(threadIdx.x == 64, 11);
         if (warp >= 2) {
-            // this rank finishes channel groups [g_lo, g_hi) of the tile; the quarter's two warps alternate groups
             const int groups = TN / 4;
             const int per = (groups + a.splits - 1) / a.splits;
+            const int blocks = TMB * P;
             const int g_lo = rank * per, g_hi = min(groups, g_lo + per);
             for (int tb = 0; tb < TMB; ++tb) {
                 const int t = t0 + tb * kBM + row;
+                if (t >= a.M) continue;
                 float s[P];
 #pragma unroll
                 for (int p = 0; p < P; ++p) s[p] = s_qs[p * TMB * kBM + tb * kBM + row];
-                if (t >= a.M) continue;
-                for (int g = g_lo + half; g < g_hi; g += 2) {
+                for (int g = g_lo + sub; g < g_hi; g += 4) {
                     int accv[P][4];
 #pragma unroll
                     for (int p = 0; p < P; ++p) {
-                        const uint32_t off = red + (uint32_t)(((((tb * P + p) * groups + g) * kBM) + row) * 16);
                         int4 sum = make_int4(0, 0, 0, 0);
-                        for (int r0 = 0; r0 < a.splits; r0 += 4) {   // four peers' loads in flight at a time
-                            int4 part[4];
-#pragma unroll
-                            for (int r = 0; r < 4; ++r)
-                                if (r0 + r < a.splits) part[r] = ld_cluster_v4(map_to_rank(off, (uint32_t)(r0 + r)));
-#pragma unroll
-                            for (int r = 0; r < 4; ++r)
-                                if (r0 + r < a.splits) {
-                                    sum.x += part[r].x;
-                                    sum.y += part[r].y;
-                                    sum.z += part[r].z;
-                                    sum.w += part[r].w;
-                                }
+                        for (int src = 0; src < a.splits; ++src) {
+                            const uint4 u = ld_shared_v4(
+                                recv + (uint32_t)((((src * blocks + tb * P + p) * per + (g - g_lo)) * kBM + row) * 16));
+                            sum.x += (int)u.x;
+                            sum.y += (int)u.y;
+                            sum.z += (int)u.z;
+                            sum.w += (int)u.w;
                         }
                         accv[p][0] = sum.x;
                         accv[p][1] = sum.y;
@@ -462,15 +675,16 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                 }
             }
         }
-        cluster_sync_all();  // no CTA leaves while a peer still reads its shared memory
     }
 
+    KEA_TRACE_POINT(threadIdx.x == 64, 12);
     grid_launch_dependents();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, a.tmem_cols);
+        KEA_TRACE_POINT(lane == 0, 13);
     }
 }
 

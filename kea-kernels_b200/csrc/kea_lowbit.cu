@@ -85,22 +85,42 @@ int device_setup(int *device_out) {
 }
 
 // ---- configuration ---------------------------------------------------------------------------------------
+// Per-stage bytes of the three shared-memory regions (activation tiles, expanded weights, packed codes).
+int a_stage_bytes(int tile_m, int parts) { return (tile_m / kea::kBM) * parts * kea::kActTileBytes; }
+int b_stage_bytes(int tile_n) { return tile_n * kea::kBK; }
+int pk_stage_bytes(int tile_n, int wbits) { return tile_n * 16 * wbits; }
 int stage_bytes(int tile_m, int tile_n, int parts, int wbits) {
-    const int act = (tile_m / kea::kBM) * parts * kea::kActTileBytes;
-    return round_up(act + tile_n * kea::kBK + (tile_n / kea::kPanelN) * wbits * kea::kPanelSubBytes, 1024);
+    return a_stage_bytes(tile_m, parts) + b_stage_bytes(tile_n) + pk_stage_bytes(tile_n, wbits);
 }
 
+bool valid_tile_n(int tile_n) { return tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 256; }
+
+// Narrow tiles with one token block and one part keep four partial accumulators (one per K = 32 step).
+int accumulators(int tile_m, int tile_n, int parts) { return (tile_n <= 64 && tile_m == kea::kBM && parts == 1) ? 4 : 1; }
+
 uint32_t tmem_columns(int tile_m, int tile_n, int parts) {
-    uint32_t need = (uint32_t)((tile_m / kea::kBM) * parts * tile_n), cols = 32;
+    uint32_t need = (uint32_t)((tile_m / kea::kBM) * parts * tile_n * accumulators(tile_m, tile_n, parts)), cols = 32;
     while (cols < need) cols <<= 1;
     return cols;
 }
 
-int exchange_bytes(int tile_m, int tile_n, int parts) { return (tile_m / kea::kBM) * parts * tile_n * kea::kBM * 4; }
+// Split-K receive buffer: [source rank][token block x part][owned channel groups][128 rows] x 16 bytes.
+int exchange_bytes(int tile_m, int tile_n, int parts, int splits) {
+    if (splits <= 1) return 0;
+    const int groups = tile_n / 4, per = ceil_div(groups, splits);
+    return splits * (tile_m / kea::kBM) * parts * per * kea::kBM * 16;
+}
+
+// The receive buffer gets its own region when it fits beside the stages; otherwise it reuses the stage area.
+bool exchange_aliases(int tile_m, int tile_n, int parts, int wbits, int splits, int stages) {
+    return stages * stage_bytes(tile_m, tile_n, parts, wbits) + exchange_bytes(tile_m, tile_n, parts, splits) + 1024 >
+           kMaxDynSmem;
+}
 
 int dyn_smem_bytes(int tile_m, int tile_n, int parts, int wbits, int splits, int stages) {
-    int bytes = stages * stage_bytes(tile_m, tile_n, parts, wbits);
-    if (splits > 1) bytes = std::max(bytes, exchange_bytes(tile_m, tile_n, parts));
+    const int st = stages * stage_bytes(tile_m, tile_n, parts, wbits);
+    const int ex = exchange_bytes(tile_m, tile_n, parts, splits);
+    int bytes = exchange_aliases(tile_m, tile_n, parts, wbits, splits, stages) ? std::max(st, ex) : st + ex;
     bytes += 1024;  // alignment slack for the 1024-byte swizzle atoms
     // Never let more CTAs share an SM than its 512 TMEM columns can serve: a CTA waiting in tcgen05.alloc
     // while its cluster peers wait for it could otherwise deadlock.
@@ -116,22 +136,37 @@ int max_stages(int tile_m, int tile_n, int parts, int wbits) {
     return s;
 }
 
-// The M-bucketed split-K dispatch table.
-//  * M <= 128: one 128-token tile; 128 channels per CTA; K split over a cluster so the grid covers the SMs.
-//  * M <= 256 (and P = 1): 256 tokens per CTA, so the weights of a 128-channel tile are expanded once for both halves.
-//  * larger M: 256-token x 128-channel tiles, split only when the tile grid is too small to fill the GPU.
+// The M-bucketed split-K dispatch table (B200, 148 SMs).
+//  * M <= 128 (one token block): narrow channel tiles, so the grid covers the SMs with little or no split-K
+//    (each CTA then reads the whole K of its channels and needs no partial exchange); split K only while the
+//    tile grid is below the SM count.
+//  * 128 < M <= 512: 128-channel tiles, 256 tokens per CTA when one part (the weight expansion serves both
+//    token blocks), split K up to the SM count.
+//  * larger M: 256 tokens x 256 channels per CTA when the tile count allows (fewest operand bytes per MMA).
 KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
     KeaGemmConfig c{};
-    const int kb = ceil_div(k, kea::kBK), nt = ceil_div(n, kea::kPanelN);
-    const int tile_n = 128;
-    const int tile_m = (m > 128 && parts == 1) ? 256 : 128;
-    const int tiles = ceil_div(std::max(m, 1), tile_m) * nt;
+    const int kb = ceil_div(k, kea::kBK), nt128 = ceil_div(n, kea::kPanelN);
+    int tile_m, tile_n;
+    if (m <= kea::kBM) {
+        tile_m = kea::kBM;
+        tile_n = 32;
+        while (tile_n < 128 && ceil_div(n, tile_n * 2) * 2 >= sms) tile_n *= 2;   // keep >= sms / 2 CTAs
+    } else if (m <= 512) {
+        tile_m = parts == 1 ? 256 : kea::kBM;
+        tile_n = 128;
+    } else {
+        tile_m = parts == 1 ? 256 : kea::kBM;
+        tile_n = (parts == 1 && nt128 % 2 == 0) ? 256 : 128;
+        const int tiles256 = ceil_div(n, tile_n) * ceil_div(m, tile_m);
+        if (tiles256 < sms && tile_n == 256) tile_n = 128;                  // too few tiles: narrower channels
+    }
+    const int tiles = ceil_div(std::max(m, 1), tile_m) * ceil_div(n, tile_n);
     int splits = 1;
     if (tiles < sms) splits = std::max(1, sms / tiles);
     splits = std::min({splits, kb, kMaxPortableCluster});
-    while (splits > 1 && exchange_bytes(tile_m, tile_n, parts) + 1024 > kMaxDynSmem) --splits;
+    while (splits > 1 && exchange_bytes(tile_m, tile_n, parts, splits) + 1024 > kMaxDynSmem) --splits;
     const int per = ceil_div(kb, splits);
-    int stages = std::min({per, 4, max_stages(tile_m, tile_n, parts, wbits)});
+    int stages = std::min(per, max_stages(tile_m, tile_n, parts, wbits));
     c.tile_m = tile_m;
     c.tile_n = tile_n;
     c.splits = splits;
@@ -143,7 +178,7 @@ KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
 int check_config(const KeaGemmConfig &c, int n, int k, int parts, int wbits) {
     const int kb = ceil_div(k, kea::kBK), nt = ceil_div(n, kea::kPanelN);
     if (c.tile_m != 128 && c.tile_m != 256) return KEA_ERR_UNSUPPORTED;
-    if (c.tile_n != 128 && c.tile_n != 256) return KEA_ERR_UNSUPPORTED;
+    if (!valid_tile_n(c.tile_n)) return KEA_ERR_UNSUPPORTED;
     if (c.tile_n == 256 && nt % 2) return KEA_ERR_UNSUPPORTED;   // the second panel tile must exist
     if ((c.tile_m / kea::kBM) * parts * c.tile_n > 512) return KEA_ERR_UNSUPPORTED;   // TMEM columns
     if (c.splits < 1 || c.splits > kMaxCluster || c.splits > kb) return KEA_ERR_UNSUPPORTED;
@@ -202,9 +237,9 @@ int kea_lowbit_prepare(const uint8_t *codes, int32_t wbits, int32_t n, int32_t k
     if (st != KEA_OK) return st;
     const int row_bytes = ceil_div((long long)k * wbits, 8);
     const int kb = ceil_div(k, kea::kBK);
-    const long long chunks = (long long)ceil_div(n, kea::kPanelN) * kb * wbits * kea::kPanelN;
-    const unsigned blocks = (unsigned)((chunks + 255) / 256);
-    kea::prepare_panels_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(codes, row_bytes, wbits, n, k, kb, chunks,
+    const long long rows = (long long)ceil_div(n, kea::kPanelN) * kb * wbits * kea::kPanelN;
+    const unsigned blocks = (unsigned)((rows + 255) / 256);
+    kea::prepare_panels_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(codes, row_bytes, wbits, n, k, kb, rows,
                                                                           panels, error_word);
     return cudaGetLastError() == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
 }
@@ -266,27 +301,96 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
             c.stages = d->stages;
         } else {
             const int per = ceil_div(ceil_div(d->k, kea::kBK), std::max(1, c.splits));
-            c.stages = std::max(1, std::min({per, 4, max_stages(c.tile_m, c.tile_n, d->parts, d->wbits)}));
+            c.stages = std::max(1, std::min(per, max_stages(c.tile_m, c.tile_n, d->parts, d->wbits)));
         }
         c.smem_bytes = dyn_smem_bytes(c.tile_m, c.tile_n, d->parts, d->wbits, c.splits, c.stages);
     }
     const int cs = check_config(c, d->n, d->k, d->parts, d->wbits);
     if (cs != KEA_OK) return cs;
 
-    // Activations: a 3-D tensor (k, m, part) of int8, tiles of 128 k x 128 rows x 1 part, 128-byte
-    // swizzle (the tcgen05 K-major layout). Columns >= k and rows >= m read as zero.
+    // Activations. When K is a multiple of 128: a 4-D view (k within a 128-block, row, k-block, part) whose boxes are
+    // 128 k x (128 * token blocks) rows x kbox k-blocks x 1 part, so one TMA instruction fills a part's token blocks
+    // (and, in one-shot mode, several k-blocks). Otherwise a 3-D view (k, row, part) with 128 x 128 boxes, whose
+    // columns >= k read as zero. Both use the 128-byte swizzle of the tcgen05 K-major layout; rows >= m read as 0.
+    const int tmb = c.tile_m / kea::kBM;
+    const int kb_total = ceil_div(d->k, kea::kBK);
+    const int nkb_max = ceil_div(kb_total, c.splits);
+    const bool q4d = d->k % kea::kBK == 0;
+    const int R = std::min(c.tile_n, kea::kPanelN);
+    // One-shot: the CTA's whole K range fits in the stages and arrives in two TMA boxes (one token block, one
+    // part, narrow channel tile so the panel box is at most 256 bytes wide).
+    const bool oneshot = q4d && tmb * d->parts == 1 && c.tile_n <= 64 && nkb_max <= c.stages && nkb_max <= 8;
+    const int kbox = oneshot ? nkb_max : 1;
     CUtensorMap qmap;
-    const cuuint64_t dims[3] = {(cuuint64_t)d->k, (cuuint64_t)d->m, (cuuint64_t)d->parts};
     const long long pstride = d->parts > 1 ? d->q_part_stride : (long long)d->m * d->ldq;
-    const cuuint64_t strides[2] = {(cuuint64_t)d->ldq, (cuuint64_t)std::max<long long>(pstride, 16)};
-    const cuuint32_t box[3] = {(cuuint32_t)kea::kBK, (cuuint32_t)kea::kBM, 1};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    if (g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t *>(d->q), dims, strides, box, estr,
-                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return KEA_ERR_CUDA;
+    // Rows past m only feed accumulator rows that are never stored, so a single token tile loads just the rows
+    // that exist (rounded up to the 8-row swizzle atom) instead of zero-filling the rest.
+    const int box_rows4 = std::min(kea::kBM * tmb, round_up(d->m, 8));
+    const int box_rows3 = std::min(kea::kBM, round_up(d->m, 8));
+    uint32_t act_tx;
+    if (q4d) {
+        act_tx = (uint32_t)(d->parts * box_rows4 * kea::kBK);
+        const cuuint64_t dims[4] = {(cuuint64_t)kea::kBK, (cuuint64_t)d->m, (cuuint64_t)kb_total, (cuuint64_t)d->parts};
+        const cuuint64_t strides[3] = {(cuuint64_t)d->ldq, (cuuint64_t)kea::kBK, (cuuint64_t)std::max<long long>(pstride, 16)};
+        const cuuint32_t box[4] = {(cuuint32_t)kea::kBK, (cuuint32_t)box_rows4, (cuuint32_t)kbox, 1};
+        const cuuint32_t estr[4] = {1, 1, 1, 1};
+        if (g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t *>(d->q), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return KEA_ERR_CUDA;
+    } else {
+        act_tx = (uint32_t)(tmb * d->parts * box_rows3 * kea::kBK);
+        const cuuint64_t dims[3] = {(cuuint64_t)d->k, (cuuint64_t)d->m, (cuuint64_t)d->parts};
+        const cuuint64_t strides[2] = {(cuuint64_t)d->ldq, (cuuint64_t)std::max<long long>(pstride, 16)};
+        const cuuint32_t box[3] = {(cuuint32_t)kea::kBK, (cuuint32_t)box_rows3, 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        if (g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t *>(d->q), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return KEA_ERR_CUDA;
+    }
+    // Panels in one-shot mode: a 2-D view (byte within one 512-byte word plane, plane), plane index
+    // ((tile * kb_total + k-block) * wbits + sub-block) * 4 + word; a box takes this CTA's R rows of kbox * wbits * 4
+    // consecutive planes.
+    CUtensorMap wmap;
+    std::memset(&wmap, 0, sizeof(wmap));
+    if (oneshot) {
+        const long long planes = (long long)ceil_div(d->n, kea::kPanelN) * kb_total * d->wbits * 4;
+        const cuuint64_t dims[2] = {(cuuint64_t)(kea::kPanelN * 4), (cuuint64_t)planes};
+        const cuuint64_t strides[1] = {(cuuint64_t)(kea::kPanelN * 4)};
+        const cuuint32_t box[2] = {(cuuint32_t)(R * 4), (cuuint32_t)(kbox * d->wbits * 4)};
+        const cuuint32_t estr[2] = {1, 1};
+        if (g_encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(d->panels), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return KEA_ERR_CUDA;
+    }
+
+    // Output: TMA stores of 32-row x tile_n / 4-column boxes when the row stride allows (16-byte multiple) and a
+    // warp's staged row is 64 or 128 bytes (the swizzle span of the shared-memory staging).
+    CUtensorMap ymap;
+    std::memset(&ymap, 0, sizeof(ymap));
+    const int out_esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
+    const int warp_row_bytes = (c.tile_n / 4) * out_esize;
+    const int staging_bytes = (c.tile_m / kea::kBM) * kea::kEpiWarps * 32 * warp_row_bytes;   // reuses the stages
+    bool tma_store = c.splits == 1 && aligned16(d->y) && (d->ldy * out_esize) % 16 == 0 &&
+                     (warp_row_bytes == 64 || warp_row_bytes == 128) &&
+                     staging_bytes <= c.stages * stage_bytes(c.tile_m, c.tile_n, d->parts, d->wbits);
+    if (tma_store) {
+        const cuuint64_t ydims[2] = {(cuuint64_t)d->n, (cuuint64_t)d->m};
+        const cuuint64_t ystrides[1] = {(cuuint64_t)(d->ldy * out_esize)};
+        const cuuint32_t ybox[2] = {(cuuint32_t)(c.tile_n / 4), 32};
+        const cuuint32_t yestr[2] = {1, 1};
+        if (g_encode(&ymap, out_esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, d->y,
+                     ydims, ystrides, ybox, yestr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     warp_row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            tma_store = false;
+    }
 
     GemmArgs a{};
+    a.tma_store = tma_store ? 1 : 0;
+    a.store_swizzle = warp_row_bytes;
     a.panels = d->panels;
     a.qs = d->qs;
     a.qs_stride = d->qs_part_stride;
@@ -301,15 +405,27 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     a.M = d->m;
     a.N = d->n;
     a.K = d->k;
-    a.parts = d->parts;
     a.tile_n = c.tile_n;
     a.tm_blocks = c.tile_m / kea::kBM;
     a.splits = c.splits;
     a.stages = c.stages;
     a.kb_total = ceil_div(d->k, kea::kBK);
     a.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
+    a.pdl = (d->flags & KEA_FLAG_PDL) ? 1 : 0;
     a.tmem_cols = tmem_columns(c.tile_m, c.tile_n, d->parts);
-    a.stage_bytes = (uint32_t)stage_bytes(c.tile_m, c.tile_n, d->parts, d->wbits);
+    a.a_stage = (uint32_t)a_stage_bytes(c.tile_m, d->parts);
+    a.b_stage = (uint32_t)b_stage_bytes(c.tile_n);
+    a.pk_stage = (uint32_t)pk_stage_bytes(c.tile_n, d->wbits);
+    a.b_region = (uint32_t)c.stages * a.a_stage;
+    a.pk_region = a.b_region + (uint32_t)c.stages * a.b_stage;
+    a.q4d = q4d ? 1 : 0;
+    a.oneshot = oneshot ? 1 : 0;
+    a.kbox = kbox;
+    a.act_tx = act_tx;
+    a.nacc = accumulators(c.tile_m, c.tile_n, d->parts);
+    a.a_stride = oneshot ? (uint32_t)(box_rows4 * kea::kBK) : a.a_stage;
+    a.recv_aliases_stages = exchange_aliases(c.tile_m, c.tile_n, d->parts, d->wbits, c.splits, c.stages) ? 1 : 0;
+    a.recv_off = a.recv_aliases_stages ? 0u : (uint32_t)(c.stages * stage_bytes(c.tile_m, c.tile_n, d->parts, d->wbits));
     const int esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
     a.vec_y = aligned16(d->y) && ((d->ldy * esize) % 16 == 0);
     a.vec_acc = d->acc && aligned16(d->acc) && ((d->ld_acc * 4) % 16 == 0) && ((d->acc_part_stride * 4) % 16 == 0);
@@ -338,12 +454,12 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     cfg.numAttrs = na;
     cudaError_t e;
     switch (d->wbits * 4 + d->parts) {
-        case 5: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<1, 1>, qmap, a); break;
-        case 6: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<1, 2>, qmap, a); break;
-        case 7: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<1, 3>, qmap, a); break;
-        case 9: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<2, 1>, qmap, a); break;
-        case 10: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<2, 2>, qmap, a); break;
-        default: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<2, 3>, qmap, a); break;
+        case 5: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<1, 1>, qmap, ymap, wmap, a); break;
+        case 6: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<1, 2>, qmap, ymap, wmap, a); break;
+        case 7: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<1, 3>, qmap, ymap, wmap, a); break;
+        case 9: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<2, 1>, qmap, ymap, wmap, a); break;
+        case 10: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<2, 2>, qmap, ymap, wmap, a); break;
+        default: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_kernel<2, 3>, qmap, ymap, wmap, a); break;
     }
     if (e != cudaSuccess) {
         cudaGetLastError();
@@ -351,6 +467,17 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     }
     return KEA_OK;
 }
+
+#ifdef KEA_TRACE
+// Trace builds only: copy out / clear the phase timestamps (kTraceCtas x kTracePhases uint64).
+int kea_trace_read(unsigned long long *out) {
+    return cudaMemcpyFromSymbol(out, kea::g_trace, sizeof(kea::g_trace)) == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
+}
+int kea_trace_clear(void) {
+    static unsigned long long zeros[kea::kTraceCtas * kea::kTracePhases];
+    return cudaMemcpyToSymbol(kea::g_trace, zeros, sizeof(zeros)) == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
+}
+#endif
 
 int kea_lowbit_read_error(uint32_t *out) {
     if (!out) return KEA_ERR_INVALID_VALUE;

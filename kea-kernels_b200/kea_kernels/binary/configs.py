@@ -1,10 +1,11 @@
 """Tile choices of the B200 low-bit GEMM: the M-bucketed split-K dispatch table.
 
 The reference picks an SM120 `DotConfig` from a table of RTX 5090 sweeps (src/kea_kernels/binary/configs.py:16-58). The
-B200 kernel has four knobs instead: `tile_m` (tokens per CTA: one or two tcgen05 M = 128 blocks), `tile_n` (channels
-per CTA = the tcgen05 N dimension, 128 or 256), `splits` (K split across a thread-block cluster, reduced exactly in
-INT32 through distributed shared memory) and `stages` (k128 blocks in flight). The table itself lives in the C library (`kea_lowbit_choose_config`), so C callers
-and Python pick the same tiles; selection is a pure function of (M, N, K, wbits, parts), with no run-time autotuning.
+B200 kernel has four knobs instead: `tile_m` (tokens per CTA: one or two tcgen05 M = 128 blocks), `tile_n`
+(channels per CTA = the tcgen05 N dimension: 32, 64, 128 or 256), `splits` (K split across a thread-block cluster,
+reduced exactly in INT32 through distributed shared memory) and `stages` (k128 blocks in flight). The table itself
+lives in the C library (`kea_lowbit_choose_config`), so C callers and Python pick the same tiles; selection is a pure
+function of (M, N, K, wbits, parts), with no run-time autotuning.
 """
 from __future__ import annotations
 
@@ -27,7 +28,7 @@ class DotConfig:
         return f"m{self.tile_m}_n{self.tile_n}_c{self.splits}_s{self.stages}"
 
     def validate(self, parts: int = 1) -> None:
-        if not (self.tile_m in (128, 256) and self.tile_n in (128, 256) and 1 <= self.splits <= 16
+        if not (self.tile_m in (128, 256) and self.tile_n in (32, 64, 128, 256) and 1 <= self.splits <= 16
                 and 1 <= self.stages <= 8 and (self.tile_m // 128) * parts * self.tile_n <= 512):
             raise ValueError(f"invalid config {self}")
 

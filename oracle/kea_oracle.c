@@ -53,19 +53,21 @@ int kea_oracle_unpack(const uint8_t *codes, int wbits, int n, int k, int8_t *w) 
     return status;
 }
 
-/* Panels: [ceil(n/128)][ceil(k/128)][wbits][128][16] bytes; row r of sub-block s of k-block b of tile t holds the
- * 16 export bytes of channel 128 t + r starting at byte 16 wbits b + 16 s (zero past the row end). */
+/* Panels: [ceil(n/128)][ceil(k/128)][wbits][4 words][128 rows][4 bytes]; row r of sub-block s of k-block b of tile
+ * t holds the 16 export bytes of channel 128 t + r starting at byte 16 wbits b + 16 s (zero past the row end), as four
+ * words; byte i of the 16 goes to word i / 4, byte i % 4, at ((i / 4) * 128 + r) * 4 within the sub-block. */
 void kea_oracle_panels(const uint8_t *codes, int wbits, int n, int k, uint8_t *out) {
     const int row_bytes = (k * wbits + 7) / 8;
     const int nt = (n + 127) / 128, kb = (k + 127) / 128;
-    long idx = 0;
+    long sub = 0;
     for (int t = 0; t < nt; ++t)
         for (int b = 0; b < kb; ++b)
-            for (int s = 0; s < wbits; ++s)
+            for (int s = 0; s < wbits; ++s, ++sub)
                 for (int r = 0; r < 128; ++r)
-                    for (int i = 0; i < 16; ++i, ++idx) {
+                    for (int i = 0; i < 16; ++i) {
                         const int ch = t * 128 + r, byte = b * 16 * wbits + s * 16 + i;
-                        out[idx] = (ch < n && byte < row_bytes) ? codes[(long)ch * row_bytes + byte] : 0;
+                        out[sub * 2048 + ((i / 4) * 128 + r) * 4 + i % 4] =
+                            (ch < n && byte < row_bytes) ? codes[(long)ch * row_bytes + byte] : 0;
                     }
 }
 

@@ -172,7 +172,8 @@ def test_gemm_silu_epilogue(out, parts):
 @pytest.mark.parametrize("config", [(128, 128, 1, 1), (128, 128, 2, 2), (128, 128, 4, 1), (128, 128, 8, 1),
                                     (128, 128, 1, 4), (256, 128, 1, 2), (128, 128, 16, 1), (128, 128, 3, 2),
                                     (256, 256, 1, 3), (256, 128, 2, 2), (128, 256, 5, 3), (128, 256, 1, 3),
-                                    (256, 256, 1, 1), (128, 128, 1, 6)])
+                                    (256, 256, 1, 1), (128, 128, 1, 6), (128, 32, 1, 4), (128, 64, 2, 3),
+                                    (256, 32, 4, 2), (128, 32, 16, 1), (256, 64, 1, 4)])
 @pytest.mark.parametrize("wbits", [1, 2])
 def test_forced_tile_configs(config, wbits):
     """Every token / channel tile, cluster split and pipeline depth gives the same bits."""

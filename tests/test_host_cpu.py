@@ -45,12 +45,13 @@ def test_every_shape_has_a_valid_config(n, k, wbits, parts):
     kb = -(-k // 128)
     for m in (1, 16, 38, 125, 126, 249, 256, 368, 400, 512, 1500, 2048, 8192, 32000):
         c = _lib.choose_config(m, n, k, wbits, parts)
-        assert c.tile_m in (128, 256) and c.tile_n in (128, 256)
+        assert c.tile_m in (128, 256) and c.tile_n in (32, 64, 128, 256)
         assert (c.tile_m // 128) * parts * c.tile_n <= 512
         assert 1 <= c.splits <= min(kb, 16) and 1 <= c.stages <= 8
         assert c.smem_bytes <= 227 * 1024
         if c.splits > 1:
-            assert (c.tile_m // 128) * parts * c.tile_n * 128 * 4 <= c.smem_bytes
+            per = -(-(c.tile_n // 4) // c.splits)
+            assert c.splits * (c.tile_m // 128) * parts * per * 128 * 16 <= c.smem_bytes
         cfg = configs.choose(m, n, k, wbits, parts)
         cfg.validate(parts)
         gx, gy, gz = cfg.grid(m, n)
@@ -58,7 +59,9 @@ def test_every_shape_has_a_valid_config(n, k, wbits, parts):
 
 
 def test_small_m_splits_k_and_large_m_does_not():
-    c = _lib.choose_config(125, 4096, 1024, 1, 1)
+    c = _lib.choose_config(125, 4096, 1024, 1, 1)       # 32-channel tiles already give 128 CTAs
+    assert c.tile_m == 128 and c.tile_n == 32 and c.splits == 1
+    c = _lib.choose_config(125, 1024, 4096, 1, 1)       # 32 channel tiles: K split over a cluster
     assert c.tile_m == 128 and c.splits > 1
     c = _lib.choose_config(8192, 4096, 1024, 1, 1)
     assert c.splits == 1
