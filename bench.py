@@ -35,6 +35,9 @@ SAMPLE_MS = (1, 16, 125, 512)           # the CPU sample: every case with M <= 5
 POOL = 4                                 # distinct weight / activation sets per case in the step graphs
 COLD_BYTES = 512 << 20                   # per (wbits, N, K): distinct weights swept by the per-case cold timing
 L2_BYTES = 126 << 20
+# dram__bytes_read.sum + dram__bytes_write.sum of one cold launch, from the ncu captures summarised in
+# profiles/lowbit_gemm_<case>.md (keyed by (wbits, N, K, M)); None for a case without a capture.
+NCU_TRAFFIC = {(2, 4096, 1024, 8192): 9_564_416 + 10_128_384, (1, 4096, 1024, 125): 739_072}
 
 
 def ops(m, n, k, parts=1):
@@ -172,11 +175,16 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--case", default=None, metavar="WBITS,N,K,M",
+                    help="profiling mode: launch one GEMM case W + K times (rotating cold weights), print its timing")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.case:
+        profile_case(args)
         return
 
     import torch
@@ -305,14 +313,17 @@ def main() -> None:
     if share["m"] >= 2048:
         achieved = ops(share["m"], share["n"], share["k"]) / (share["us"] * 1e-6) / 1e12
         roofline = {"bound": "tensor", "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
-                    "frac": achieved / tensor_peak, "traffic": None,
+                    "frac": achieved / tensor_peak,
+                    "traffic": NCU_TRAFFIC.get((share["wbits"], share["n"], share["k"], share["m"])),
                     "kernel": f"lowbit_gemm_kernel<{share['wbits']}> M={share['m']} N={share['n']} K={share['k']}",
                     "peak_kind": int8_kind or f"2 x bf16 ({peak_kind})",
                     "note": "INT8 ops/s; peak = dense INT8 measured with torch._int_mm 8192^3 on this GPU"}
     else:
         achieved = share["gbs_full"]
         roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                    "frac": achieved / hbm_peak, "traffic": None, "kernel": f"lowbit_gemm_kernel<{share['wbits']}>",
+                    "frac": achieved / hbm_peak,
+                    "traffic": NCU_TRAFFIC.get((share["wbits"], share["n"], share["k"], share["m"])),
+                    "kernel": f"lowbit_gemm_kernel<{share['wbits']}>",
                     "peak_kind": peak_kind}
     small = [c for c in per_case if c["m"] == 125]
     roofline_small = [{"case": f"w{c['wbits']} N={c['n']} K={c['k']} M=125", "bound": "hbm",
@@ -388,6 +399,56 @@ def time_cases(torch, lowbit, _lib, configs, dev, stream, random_panels, alphas,
         out.append(rec)
         del q, qs, y
     return out
+
+
+def profile_case(args) -> None:
+    """One case, W + K plain launches on the current stream, each on a different weight set (>= 4 x L2 of weights
+    rotate unless the set is larger) and activation set; prints the average of the last K launches (CUDA events).
+    This is the command the kernel's ncu captures run (`-s W -c 1` selects one cold launch)."""
+    import torch
+
+    from kea_kernels import _lib, formats, lowbit
+    from kea_kernels.binary import bits, configs
+
+    wbits, n, k, m = (int(v) for v in args.case.split(","))
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(99)
+    sets = max(1, min(64, (4 * L2_BYTES) // max(1, _lib.panel_bytes(wbits, n, k))))
+    panels = []
+    for _ in range(min(sets, 8)):
+        if wbits == 1:
+            codes = bits.pack_signs(torch.where(torch.rand(n, k, device=dev, generator=gen) < 0.5, -1, 1).to(torch.int8))
+        else:
+            u = torch.rand(n, k, device=dev, generator=gen)
+            codes = formats.pack_ternary(torch.where(u < 0.3, -1, torch.where(u < 0.7, 0, 1)).to(torch.int8))
+        panels.append(lowbit.prepare_panels(codes, wbits, n, k))
+    panels = [panels[i % len(panels)].clone() for i in range(sets)]
+    nq = 2 if m * k * 4 > L2_BYTES else 4
+    q = torch.randint(-127, 128, (nq, 1, m, k), dtype=torch.int8, device=dev, generator=gen)
+    qs = torch.rand(nq, 1, m, device=dev, generator=gen) * 0.015 + 0.005
+    alpha = (torch.rand(n, device=dev, generator=gen) * 0.04 + 0.01).half().float()
+    y = torch.empty(m, n, device=dev, dtype=torch.float16)
+    torch.cuda.synchronize()
+
+    def run(i):
+        lowbit.gemm(q[i % nq], qs[i % nq], k, m, panels[i % sets], wbits, n, k, alpha, None, y, parts=1)
+
+    for i in range(args.warmup):
+        run(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        run(args.warmup + i)
+    e1.record()
+    torch.cuda.synchronize()
+    if _lib.read_device_error():
+        raise RuntimeError("device error word set")
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    wa, full = alg_bytes(wbits, n, k, m)
+    print(json.dumps({"case": {"wbits": wbits, "n": n, "k": k, "m": m}, "config": configs.choose(m, n, k, wbits).label(),
+                      "us_per_launch": us, "tops": ops(m, n, k) / us / 1e6, "alg_bytes_wa": wa,
+                      "alg_bytes_full": full, "weight_sets": sets}), flush=True)
 
 
 def int8_peak_tops(torch, dev):

@@ -261,6 +261,27 @@ KEA_DEVI void load_acc16(uint32_t lane_addr, int blk, int nacc, int TN, int c, u
     }
 }
 
+// The MMAs of one k128 stage: 4 K = 32 steps x P parts x TMB token blocks, D = 128 tokens x TN channels each.
+// Accumulator (token block tb, part p) starts at TMEM column ((tb * P + p) * NACC) * TN; with NACC = 4 each K step
+// has its own accumulator (summed in the epilogue) so consecutive narrow MMAs do not wait on one another.
+template <int P, int TMB, int NACC>
+KEA_DEVI void issue_stage(uint32_t tmem, uint64_t ad_s, uint64_t bd_s, uint32_t idesc, int TN, bool first) {
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+        const uint64_t bd = bd_s + (uint64_t)(kk * 2);      // + kk * 32 bytes (descriptor address unit: 16 bytes)
+        const uint32_t accumulate = (!first || (NACC == 1 && kk != 0)) ? 1u : 0u;
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+#pragma unroll
+            for (int tb = 0; tb < TMB; ++tb) {
+                const uint64_t ad = ad_s + (uint64_t)(((p * TMB + tb) * kActTileBytes + kk * 32) >> 4);
+                const uint32_t col = (uint32_t)(((tb * P + p) * NACC + (NACC > 1 ? kk : 0)) * TN);
+                mma_i8(tmem + col, ad, bd, idesc, accumulate);
+            }
+        }
+    }
+}
+
 KEA_DEVI void named_barrier_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -405,6 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
     } else if (warp == 1) {
         // ---------------- MMA issuer: the whole warp waits, lane 0 issues ----------------
         const uint32_t idesc = idesc_i8(kBM, (uint32_t)TN);
+        const uint64_t a_desc0 = sw128_kmajor_desc(A0), b_desc0 = sw128_kmajor_desc(B0);
         int s = 0;
         uint32_t ph = 0;
         for (int i = 0; i < nkb; ++i) {
@@ -420,25 +442,18 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
             KEA_TRACE_POINT(lane == 0 && i < 8, 23 + i);
             // The mbarrier wait orders the operands (TMA writes, or expander writes behind fence.proxy.async) before
             // the MMAs' shared-memory reads; no tcgen05 fence per stage (it would drain the MMA pipe).
-            if (lane == 0) {
-                const uint32_t sa = A0 + (uint32_t)s * a.a_stride, sb = B0 + (uint32_t)s * a.b_stage;
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint64_t bd = sw128_kmajor_desc(sb + kk * 32);
-#pragma unroll
-                    for (int p = 0; p < P; ++p) {
-#pragma unroll
-                        for (int tb = 0; tb < 2; ++tb) {
-                            if (tb < TMB) {
-                                const uint64_t ad = sw128_kmajor_desc(sa + (p * TMB + tb) * kActTileBytes + kk * 32);
-                                const int acc = a.nacc > 1 ? kk : 0;
-                                mma_i8(tmem + (uint32_t)(((tb * P + p) * a.nacc + acc) * TN), ad, bd, idesc,
-                                       (i != 0 || kk > acc) ? 1u : 0u);
-                            }
-                        }
-                    }
-                }
-                KEA_TRACE_POINT(i == 0, 7);
+            // The whole warp forms the stage's descriptors (warp-uniform values); one elected lane issues the stage's
+            // MMAs from a fully unrolled body (no run-time loop bounds around tcgen05.mma, which slow its issue
+            // several-fold).
+            const uint64_t ad_s = a_desc0 + (uint64_t)((s * a.a_stride) >> 4);
+            const uint64_t bd_s = b_desc0 + (uint64_t)((s * a.b_stage) >> 4);
+            if (elect_one()) {
+                if (TMB == 2)
+                    issue_stage<P, 2, 1>(tmem, ad_s, bd_s, idesc, TN, i == 0);
+                else if (a.nacc > 1)
+                    issue_stage<P, 1, 4>(tmem, ad_s, bd_s, idesc, TN, i == 0);
+                else
+                    issue_stage<P, 1, 1>(tmem, ad_s, bd_s, idesc, TN, i == 0);
                 mma_commit(smem_u32(&bar_empty[s]));
             }
             __syncwarp();
@@ -447,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                 ph ^= 1u;
             }
         }
-        if (lane == 0) mma_commit(smem_u32(&bar_acc));
+        if (elect_one()) mma_commit(smem_u32(&bar_acc));
         __syncwarp();
         KEA_TRACE_POINT(lane == 0, 8);
     } else {
@@ -463,9 +478,31 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
             s_bias[i] = (a.bias && n < a.N) ? a.bias[n] : 0.f;
         }
         const int units = TN * (WBITS == 1 ? 4 : 8);
+        const int units_log2 = tn_log2 + (WBITS == 1 ? 2 : 3);
+        if (a.oneshot) {
+            // Every k-block is already resident: spread all of them over the 512 threads, then one proxy fence and
+            // the stage arrivals (a fence per stage would put its latency into every stage of the MMA chain).
+            const bool landed = mbar_wait(smem_u32(&bar_full[0]), 0u, kWaitBudget);
+            if (!__all_sync(0xFFFFFFFFu, landed)) {
+                ok = false;
+                if (lane == 0) report(a.err, 1u);
+            } else {
+                KEA_TRACE_POINT(threadIdx.x == 64, 4);
+                for (int f = e; f < (nkb << units_log2); f += kEpiThreads) {
+                    const int st = f >> units_log2;
+                    expand_unit<WBITS>(PK0 + (uint32_t)st * a.pk_stage, B0 + (uint32_t)st * a.b_stage, tn_log2,
+                                       f & (units - 1));
+                }
+                fence_async_shared();
+                KEA_TRACE_POINT(threadIdx.x == 64, 5);
+                __syncwarp();
+                if (lane == 0)
+                    for (int st = 0; st < nkb; ++st) mbar_arrive(smem_u32(&bar_exp[st]));
+            }
+        }
         int s = 0;
         uint32_t ph = 0;
-        for (int i = 0; i < nkb; ++i) {
+        for (int i = 0; i < (a.oneshot ? 0 : nkb); ++i) {
             const bool landed = mbar_wait(smem_u32(&bar_full[a.oneshot ? 0 : s]), a.oneshot ? 0u : ph, kWaitBudget);
             if (!__all_sync(0xFFFFFFFFu, landed)) {
                 ok = false;
@@ -568,7 +605,9 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                         bulk_commit_group();
                     }
                 }
-                if (lane == 0) bulk_wait_group0();   // the stores have read shared memory and landed
+                // The staging area must outlive the stores' reads of it; their global writes complete with the grid
+                // (a dependent grid's griddepcontrol.wait sees them), so nothing waits for the writes themselves.
+                if (lane == 0) bulk_wait_group_read0();
                 __syncwarp();
             }
         } else if (a.splits == 1) {

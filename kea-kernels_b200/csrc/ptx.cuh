@@ -48,6 +48,14 @@ KEA_DEVI void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.c
 // Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA / tcgen05) accesses.
 KEA_DEVI void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// One lane of the (converged) warp gets true: elect.sync, which lets the compiler keep warp-uniform operands of the
+// elected lane's instructions in uniform registers.
+KEA_DEVI bool elect_one() {
+    uint32_t pred;
+    asm volatile("{\n\t.reg .pred P1;\n\telect.sync _|P1, 0xffffffff;\n\tselp.b32 %0, 1, 0, P1;\n\t}\n" : "=r"(pred));
+    return pred != 0;
+}
+
 // ---- copies into shared memory ----------------------------------------------------------------------------
 // 3-D tiled TMA load (no multicast) completing on an mbarrier of this CTA.
 KEA_DEVI void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y, int z) {
