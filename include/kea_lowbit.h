@@ -50,7 +50,8 @@ enum { KEA_OUT_F32 = 0, KEA_OUT_F16 = 1 };
 enum {
     KEA_FLAG_SILU = 1,
     KEA_FLAG_ORDER1 = 2,
-    KEA_FLAG_PDL = 4            /* launch with programmatic dependent launch (overlap with the previous kernel) */
+    KEA_FLAG_PDL = 4,           /* launch with programmatic dependent launch (overlap with the previous kernel) */
+    KEA_FLAG_NO_PAIR = 8        /* never use the persistent CTA-pair kernel (the per-tile kernel runs instead) */
 };
 
 /* Device error word bits (written by kernels into `error_word`, or into the library's own device word). */
@@ -93,7 +94,8 @@ typedef struct KeaGemmDesc {
     int64_t acc_part_stride;  /* elements between parts of acc */
     int32_t m;                /* tokens (rows of q and y); 0 is a no-op */
     int32_t flags;            /* KEA_FLAG_* */
-    int32_t tile_m;           /* 0: dispatch table; else tokens per CTA (128 or 256) */
+    int32_t tile_m;           /* 0: dispatch table; else tokens per CTA (128 or 256); any forced field selects the
+                                 per-tile kernel */
     int32_t tile_n;           /* 0: dispatch table; else channels per CTA (32, 64, 128 or 256) */
     int32_t splits;           /* 0: dispatch table; else split-K ways = cluster size (1..16) */
     int32_t stages;           /* 0: dispatch table; else pipeline stages (1..8) */
@@ -107,6 +109,8 @@ typedef struct KeaGemmConfig {
     int32_t splits;           /* K split across a thread-block cluster of this size */
     int32_t stages;           /* smem pipeline depth (k128 blocks in flight) */
     int32_t smem_bytes;       /* dynamic shared memory per CTA */
+    int32_t pair;             /* 1: the persistent CTA-pair kernel (tcgen05 cta_group::2, 256 x 256 tiles per pair of
+                                 SMs, double-buffered accumulators); 0: the per-tile kernel */
 } KeaGemmConfig;
 
 int kea_lowbit_gemm(const KeaGemmDesc *desc, void *stream);

@@ -10,11 +10,27 @@
 namespace kea {
 
 // ---- prepare: export codes -> panels --------------------------------------------------------------------------
+// Within each 32-bit panel word the export codes (LSB first) are re-ordered so that the expansion is a byte-permute
+// lookup: 1 bit - code i moves to bit 4 (i % 8) + i / 8, so (word >> j) & 0x11111111 holds codes 8 j .. 8 j + 7 one
+// per nibble; 2 bits - field i moves to bits 4 (i % 8) + 2 (i / 8), so word & 0x33333333 holds fields 0-7 and
+// (word >> 2) & 0x33333333 fields 8-15, one per nibble. A nibble is then a prmt selector into a 4-byte table.
+KEA_DEVI uint32_t interleave_codes(uint32_t w, int wbits) {
+    uint32_t out = 0;
+    if (wbits == 1) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) out |= ((w >> i) & 1u) << (4 * (i & 7) + (i >> 3));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) out |= ((w >> (2 * i)) & 3u) << (4 * (i & 7) + 2 * (i >> 3));
+    }
+    return out;
+}
+
 // Panel layout: [ceil(N/128) tiles][ceil(K/128) k-blocks][wbits sub-blocks][4 words][128 rows][4 bytes]. Sub-block s
 // of k-block b of channel row 128 t + r covers k in [128 b + s * 128 / wbits, ... + 128 / wbits): the 16 export bytes
-// of that row starting at byte 16 wbits b + 16 s (LSB-first codes, unchanged; zero past the row end), stored as four
-// little-endian words, word j at (j * 128 + r) * 4 (word-major, so the kernel's per-row word loads hit distinct
-// banks). One thread builds one row of one sub-block and checks its bytes: bits past k = K must be 0, and a 2-bit
+// of that row starting at byte 16 wbits b + 16 s (zero past the row end), read as four little-endian words whose
+// codes are then interleaved (below), word j stored at (j * 128 + r) * 4 (word-major, so the kernel's per-row word
+// loads hit distinct banks). One thread builds one row of one sub-block and checks its bytes: bits past k = K must be 0, and a 2-bit
 // field must not be 0b11.
 __global__ void __launch_bounds__(256) prepare_panels_kernel(const uint8_t *__restrict__ codes, int row_bytes, int wbits,
                                                              int N, int K, int kb_total, long long rows_total,
@@ -52,7 +68,7 @@ __global__ void __launch_bounds__(256) prepare_panels_kernel(const uint8_t *__re
     }
     uint32_t *dst = reinterpret_cast<uint32_t *>(panels + (idx - r) * 16);   // the sub-block's first byte
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j * kPanelN + r] = words[j];
+    for (int j = 0; j < 4; ++j) dst[j * kPanelN + r] = interleave_codes(words[j], wbits);
     if (bad) report(err, bad);
 }
 

@@ -107,21 +107,11 @@ KEA_DEVI uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
     return d;
 }
-// Lane i of the result is 0xFF when bit 7 of lane i of x is set, else 0x00 (prmt's sign-replicating selectors).
-KEA_DEVI uint32_t lane_sign(uint32_t x) { return prmt(x, 0, 0xBA98u); }
-// 1-bit codes 4h .. 4h+3 of the byte replicated in `rep` (LSB first): code 1 -> int8 +1 (0x01), code 0 -> -1 (0xFF).
-// Lane i keeps only its code's bit; adding 0x7F moves it to bit 7 without carrying into the next lane.
-KEA_DEVI uint32_t signs4(uint32_t rep, int h) {
-    const uint32_t t = (rep & (h ? 0x80402010u : 0x08040201u)) + 0x7F7F7F7Fu;
-    return ~lane_sign(t) | 0x01010101u;
-}
-// 2-bit codes of the byte replicated in `rep`: field i at bits 2i (+1) and 2i+1 (-1); 00 -> 0.
-KEA_DEVI uint32_t ternary4(uint32_t rep) {
-    const uint32_t plus = (rep & 0x40100401u) + 0x7F7F7F7Fu;
-    const uint32_t minus = (rep & 0x80200802u) + 0x7F7F7F7Fu;
-    return lane_sign(minus) | ((plus >> 7) & 0x01010101u);
-}
-KEA_DEVI uint32_t byte_rep(uint32_t word, int k) { return prmt(word, 0, (uint32_t)k * 0x1111u); }
+// Byte tables indexed by a code nibble (prmt selector, low 16 bits = 4 output bytes): 1 bit - 0 -> int8 -1 (0xFF),
+// 1 -> +1; 2 bits - 00 -> 0, 01 -> +1, 10 -> -1.
+constexpr uint32_t kSignTable = 0x000001FFu;
+constexpr uint32_t kTernaryTable = 0x00FF0100u;
+KEA_DEVI uint32_t lookup4(uint32_t table, uint32_t sel) { return prmt(table, 0, sel); }
 
 KEA_DEVI void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
@@ -142,9 +132,10 @@ KEA_DEVI void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, u
 
 // Packed codes of one stage in shared memory: [panel tile][sub-block s][word j][R rows][4 bytes], R = min(tile_n,
 // 128) (the panels' own word-major order). Word j of sub-block s of a channel row holds (1 bit) codes 32 j .. + 31,
-// (2 bits) codes 64 s + 16 j .. + 15. Unit u expands channel row r = u % tile_n: 1 bit - word j = u / tile_n
-// (chunks 2 j and 2 j + 1); 2 bits - chunk c = u / tile_n (word c % 4 of sub-block c / 4). A chunk is 16 codes =
-// 16 bytes of the B tile, stored at chunk position c ^ (r & 7) of row r (128-byte swizzle). tn_log2 = log2(tile_n).
+// (2 bits) codes 64 s + 16 j .. + 15, interleaved by prepare so each code is one nibble of a masked shift of the word.
+// Unit u expands channel row r = u % tile_n: 1 bit - word j = u / tile_n (chunks 2 j and 2 j + 1); 2 bits - chunk
+// c = u / tile_n (word c % 4 of sub-block c / 4). A chunk is 16 codes = 16 bytes of the B tile, stored at chunk
+// position c ^ (r & 7) of row r (128-byte swizzle). tn_log2 = log2(tile_n).
 template <int WBITS>
 KEA_DEVI void expand_unit(uint32_t pk, uint32_t dst, int tn_log2, int u) {
     // tile_n and R are powers of two: shifts and masks, never integer division, on this hot path
@@ -154,13 +145,17 @@ KEA_DEVI void expand_unit(uint32_t pk, uint32_t dst, int tn_log2, int u) {
     const uint32_t rowbase = dst + (uint32_t)r * 128;
     const uint32_t sw = (uint32_t)(r & 7);
     const uint32_t w = ld_shared_u32(pk + ((uint32_t)((((pt * (4 * WBITS) + q) << r_log2) | rr)) << 2));
-    if constexpr (WBITS == 1) {
-        const uint32_t b0 = byte_rep(w, 0), b1 = byte_rep(w, 1), b2 = byte_rep(w, 2), b3 = byte_rep(w, 3);
-        st_shared_v4(rowbase + (((uint32_t)(2 * q) ^ sw) << 4), signs4(b0, 0), signs4(b0, 1), signs4(b1, 0), signs4(b1, 1));
-        st_shared_v4(rowbase + (((uint32_t)(2 * q + 1) ^ sw) << 4), signs4(b2, 0), signs4(b2, 1), signs4(b3, 0), signs4(b3, 1));
-    } else {
-        st_shared_v4(rowbase + (((uint32_t)q ^ sw) << 4), ternary4(byte_rep(w, 0)), ternary4(byte_rep(w, 1)),
-                     ternary4(byte_rep(w, 2)), ternary4(byte_rep(w, 3)));
+    if constexpr (WBITS == 1) {   // (w >> j) & 0x11111111: codes 8 j .. 8 j + 7, one per nibble
+        const uint32_t s0 = w & 0x11111111u, s1 = (w >> 1) & 0x11111111u;
+        const uint32_t s2 = (w >> 2) & 0x11111111u, s3 = (w >> 3) & 0x11111111u;
+        st_shared_v4(rowbase + (((uint32_t)(2 * q) ^ sw) << 4), lookup4(kSignTable, s0), lookup4(kSignTable, s0 >> 16),
+                     lookup4(kSignTable, s1), lookup4(kSignTable, s1 >> 16));
+        st_shared_v4(rowbase + (((uint32_t)(2 * q + 1) ^ sw) << 4), lookup4(kSignTable, s2), lookup4(kSignTable, s2 >> 16),
+                     lookup4(kSignTable, s3), lookup4(kSignTable, s3 >> 16));
+    } else {                      // w & 0x33333333: fields 0-7; (w >> 2) & 0x33333333: fields 8-15
+        const uint32_t lo = w & 0x33333333u, hi = (w >> 2) & 0x33333333u;
+        st_shared_v4(rowbase + (((uint32_t)q ^ sw) << 4), lookup4(kTernaryTable, lo), lookup4(kTernaryTable, lo >> 16),
+                     lookup4(kTernaryTable, hi), lookup4(kTernaryTable, hi >> 16));
     }
 }
 

@@ -10,6 +10,7 @@
 
 #include "kea_lowbit.h"
 #include "gemm_kernel.cuh"
+#include "gemm_pair_kernel.cuh"
 #include "aux_kernels.cuh"
 
 namespace {
@@ -20,6 +21,8 @@ constexpr int kSmsB200 = 148;
 constexpr int kMaxDevices = 64;
 constexpr int kSmemPerSm = 233472;       // 228 KB of shared memory per SM
 constexpr int kMaxDynSmem = 227 * 1024 - 8192;  // leave room for the kernel's static shared memory (< 8 KB)
+// The pair kernel's static shared memory is a few hundred bytes, so its dynamic share may reach 226 KB.
+constexpr int kPairMaxDynSmem = 227 * 1024 - 1024;
 constexpr int kMaxPortableCluster = 8;
 constexpr int kMaxCluster = 16;
 
@@ -74,6 +77,11 @@ int device_setup(int *device_out) {
                 cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
                 status = KEA_ERR_CUDA;
         }
+        const void *pair_kernels[2] = {(const void *)kea::lowbit_gemm_pair_kernel<1>,
+                                       (const void *)kea::lowbit_gemm_pair_kernel<2>};
+        for (const void *k : pair_kernels)
+            if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairMaxDynSmem) != cudaSuccess)
+                status = KEA_ERR_CUDA;
         if (cudaFuncSetAttribute((const void *)kea::quantize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  64 * 1024) != cudaSuccess)
             status = KEA_ERR_CUDA;
@@ -136,6 +144,25 @@ int max_stages(int tile_m, int tile_n, int parts, int wbits) {
     return s;
 }
 
+// ---- the persistent CTA-pair kernel (gemm_pair_kernel.cuh) ---------------------------------------------------------
+// Dynamic shared memory: alignment slack + stages x (activation box + B tile + packed codes) + epilogue staging.
+int pair_stage_bytes(int wbits) { return 2 * (int)kea::kPairHalfTile + wbits * kea::kPanelSubBytes; }
+int pair_smem_bytes(int wbits, int stages) {
+    return 1024 + stages * pair_stage_bytes(wbits) + (int)kea::kPairStagingBytes + (int)kea::kPairChannelBytes;
+}
+int pair_max_stages(int wbits) {
+    int s = kea::kPairMaxStages;
+    while (s > 2 && pair_smem_bytes(wbits, s) > kPairMaxDynSmem) --s;
+    return s;
+}
+// The pair kernel takes one activation part and whole 256-channel tiles; above this many tokens it replaces the
+// per-tile kernel (its 256 x 256 pair tiles keep the shared-memory traffic per MAC at half the per-tile kernel's).
+constexpr int kPairMinM = 257;
+// K <= 32768 keeps |acc| <= 127 K below 2^22, where the epilogue's two-operation INT32 -> FP32 conversion is exact.
+bool pair_shape(int m, int n, int k, int parts) {
+    return parts == 1 && n % kea::kPairTileN == 0 && m >= kPairMinM && k <= 32768;
+}
+
 // The M-bucketed split-K dispatch table (B200, 148 SMs).
 //  * M <= 128 (one token block): narrow channel tiles, so the grid covers the SMs with little or no split-K
 //    (each CTA then reads the whole K of its channels and needs no partial exchange); split K only while the
@@ -143,7 +170,7 @@ int max_stages(int tile_m, int tile_n, int parts, int wbits) {
 //  * 128 < M <= 512: 128-channel tiles, 256 tokens per CTA when one part (the weight expansion serves both
 //    token blocks), split K up to the SM count.
 //  * larger M: 256 tokens x 256 channels per CTA when the tile count allows (fewest operand bytes per MMA).
-KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
+KeaGemmConfig choose_tile(int m, int n, int k, int wbits, int parts, int sms) {
     KeaGemmConfig c{};
     const int kb = ceil_div(k, kea::kBK), nt128 = ceil_div(n, kea::kPanelN);
     int tile_m, tile_n;
@@ -172,6 +199,21 @@ KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
     c.splits = splits;
     c.stages = std::max(stages, 1);
     c.smem_bytes = dyn_smem_bytes(tile_m, tile_n, parts, wbits, splits, c.stages);
+    c.pair = 0;
+    return c;
+}
+
+// The full table: the pair kernel where its shape rule holds, else the per-tile kernel's entry.
+KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
+    KeaGemmConfig c = choose_tile(m, n, k, wbits, parts, sms);
+    if (pair_shape(m, n, k, parts)) {
+        c.tile_m = kea::kPairTileM;
+        c.tile_n = kea::kPairTileN;
+        c.splits = 1;
+        c.stages = pair_max_stages(wbits);
+        c.smem_bytes = pair_smem_bytes(wbits, c.stages);
+        c.pair = 1;
+    }
     return c;
 }
 
@@ -189,6 +231,84 @@ int check_config(const KeaGemmConfig &c, int n, int k, int parts, int wbits) {
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launches the persistent CTA-pair kernel. KEA_ERR_UNSUPPORTED when an operand's alignment or stride rules it out
+// (the caller then runs the per-tile kernel); other codes are final.
+int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *stream) {
+    const int esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
+    if (!aligned16(d->y) || (d->ldy * esize) % 16 || !aligned16(d->alpha) || (d->bias && !aligned16(d->bias)) ||
+        (d->acc && (!aligned16(d->acc) || d->ld_acc % 4)))
+        return KEA_ERR_UNSUPPORTED;
+    // Activations: 2-D (k, row) with 128 x 128 boxes in the 128-byte swizzle; columns >= k and rows >= m read as 0.
+    CUtensorMap qmap, ymap;
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)d->k, (cuuint64_t)d->m};
+        const cuuint64_t strides[1] = {(cuuint64_t)d->ldq};
+        const cuuint32_t box[2] = {(cuuint32_t)kea::kBK, (cuuint32_t)kea::kBM};
+        const cuuint32_t estr[2] = {1, 1};
+        if (g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(d->q), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return KEA_ERR_CUDA;
+    }
+    // Output: 32 rows x 64 bytes per store (32 FP16 or 16 FP32 channels), 64-byte swizzle; rows >= m are not written.
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)d->n, (cuuint64_t)d->m};
+        const cuuint64_t strides[1] = {(cuuint64_t)(d->ldy * esize)};
+        const cuuint32_t box[2] = {(cuuint32_t)(64 / esize), 32};
+        const cuuint32_t estr[2] = {1, 1};
+        if (g_encode(&ymap, esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, d->y, dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return KEA_ERR_UNSUPPORTED;
+    }
+    kea::PairArgs a{};
+    a.panels = d->panels;
+    a.qs = d->qs;
+    a.alpha = d->alpha;
+    a.bias = d->bias;
+    a.acc = d->acc;
+    a.ld_acc = d->ld_acc;
+    a.M = d->m;
+    a.N = d->n;
+    a.K = d->k;
+    a.kb_total = ceil_div(d->k, kea::kBK);
+    a.n_tiles = d->n / kea::kPairTileN;
+    a.tiles = a.n_tiles * ceil_div(d->m, kea::kPairTileM);
+    a.flags = d->flags & KEA_FLAG_SILU;
+    a.pdl = (d->flags & KEA_FLAG_PDL) ? 1 : 0;
+    a.y_f16 = esize == 2;
+    a.stages = c.stages;
+    a.err = d->error_word;
+    const int pairs = std::min(a.tiles, std::max(1, sms / 2));
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+    cfg.blockDim = dim3(kea::kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)c.smem_bytes;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attrs[2];
+    unsigned na = 0;
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = 2;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+    if (d->flags & KEA_FLAG_PDL) {
+        attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attrs[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = na;
+    const cudaError_t e = d->wbits == 1 ? cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<1>, qmap, ymap, a)
+                                        : cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<2>, qmap, ymap, a);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return KEA_ERR_CUDA;
+    }
+    return KEA_OK;
+}
 
 }  // namespace
 
@@ -286,14 +406,20 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
         return KEA_ERR_INVALID_VALUE;
     if (!aligned16(d->q) || d->ldq % 16 || !aligned16(d->panels)) return KEA_ERR_ALIGNMENT;
     if (d->parts > 1 && (d->q_part_stride % 16 || d->q_part_stride < (int64_t)d->m * d->ldq)) return KEA_ERR_ALIGNMENT;
-    if (d->flags & ~(KEA_FLAG_SILU | KEA_FLAG_ORDER1 | KEA_FLAG_PDL)) return KEA_ERR_INVALID_VALUE;
+    if (d->flags & ~(KEA_FLAG_SILU | KEA_FLAG_ORDER1 | KEA_FLAG_PDL | KEA_FLAG_NO_PAIR)) return KEA_ERR_INVALID_VALUE;
 
     int dev = 0;
     const int st = device_setup(&dev);
     if (st != KEA_OK) return st;
 
     KeaGemmConfig c = choose(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms);
-    if (d->tile_m || d->tile_n || d->splits || d->stages) {
+    const bool forced = d->tile_m || d->tile_n || d->splits || d->stages;
+    if (c.pair && !forced && !(d->flags & KEA_FLAG_NO_PAIR)) {
+        const int ps = launch_pair(d, c, g_devices[dev].sms, stream);
+        if (ps != KEA_ERR_UNSUPPORTED) return ps;
+    }
+    if (c.pair) c = choose_tile(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms);
+    if (forced) {
         if (d->tile_m) c.tile_m = d->tile_m;
         if (d->tile_n) c.tile_n = d->tile_n;
         if (d->splits) c.splits = d->splits;
@@ -472,6 +598,9 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
 // Trace builds only: copy out / clear the phase timestamps (kTraceCtas x kTracePhases uint64).
 int kea_trace_read(unsigned long long *out) {
     return cudaMemcpyFromSymbol(out, kea::g_trace, sizeof(kea::g_trace)) == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
+}
+int kea_pair_trace_read(long long *out) {
+    return cudaMemcpyFromSymbol(out, kea::g_pair_trace, sizeof(kea::g_pair_trace)) == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
 }
 int kea_trace_clear(void) {
     static unsigned long long zeros[kea::kTraceCtas * kea::kTracePhases];

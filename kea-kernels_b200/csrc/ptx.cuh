@@ -35,14 +35,37 @@ KEA_DEVI bool mbar_test(uint32_t bar, uint32_t parity) {
         : "memory");
     return done != 0;
 }
+// Non-blocking test of phase `parity` (no suspension): the cheap first look of every wait.
+KEA_DEVI bool mbar_peek(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
 // Waits for phase `parity` of the barrier; false when `budget` SM clocks pass first.
 KEA_DEVI bool mbar_wait(uint32_t bar, uint32_t parity, long long budget) {
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_peek(bar, parity)) return true;
     const long long start = clock64();
     while (!mbar_test(bar, parity)) {
         if (clock64() - start > budget) return false;
     }
     return true;
+}
+// For long waits of warps that have nothing else to do (an epilogue waiting for a whole main loop): between tests the
+// warp sleeps `ns` nanoseconds, so its polling takes no issue slots or shared-memory cycles from the working warps.
+KEA_DEVI bool mbar_wait_sleep(uint32_t bar, uint32_t parity, long long budget, uint32_t ns) {
+    if (mbar_test(bar, parity)) return true;
+    const long long start = clock64();
+    while (true) {
+        __nanosleep(ns);
+        if (mbar_test(bar, parity)) return true;
+        if (clock64() - start > budget) return false;
+    }
 }
 KEA_DEVI void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 // Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA / tcgen05) accesses.
@@ -91,6 +114,8 @@ KEA_DEVI void tma_store_2d(const CUtensorMap *map, uint32_t src, int x, int y) {
 }
 KEA_DEVI void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 KEA_DEVI void bulk_wait_group_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// At most one committed bulk group may still be reading its shared-memory source.
+KEA_DEVI void bulk_wait_group_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 KEA_DEVI void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 KEA_DEVI void prefetch_tensormap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
@@ -165,6 +190,67 @@ KEA_DEVI int ld_cluster_s32(uint32_t addr) {
     int v;
     asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
     return v;
+}
+
+// Cluster barrier without .aligned: legal when the warps of a CTA reach it from different code paths.
+KEA_DEVI void cluster_sync_relaxed_paths() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// ---- CTA pairs (tcgen05 cta_group::2) -------------------------------------------------------------------------
+// Every tcgen05 instruction of a pair kernel uses cta_group::2. One warp of EACH CTA of the pair (the same warp
+// index in both) allocates and frees; the allocation covers the same columns in both CTAs' tensor memory.
+KEA_DEVI void tmem_alloc_pair(uint32_t slot, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(cols) : "memory");
+}
+KEA_DEVI void tmem_relinquish_pair() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory"); }
+KEA_DEVI void tmem_dealloc_pair(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+// Issued by the even CTA of the pair: D (M = 256 rows: rows 0-127 in the even CTA's tensor memory, 128-255 in the
+// odd CTA's) (+)= A (rows 0-127 from the even CTA's shared memory, 128-255 from the odd CTA's, at the same offset)
+// x B^T (N / 2 rows from each CTA's shared memory, at the same offset). Signed INT8, INT32 accumulators.
+KEA_DEVI void mma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}\n"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives once on the mbarrier at shared-memory offset `bar` in every CTA of `cta_mask` when the pair MMAs this
+// thread issued before it have completed (a tcgen05 completion signal; it moves no data).
+KEA_DEVI void mma_commit_pair(uint32_t bar, uint16_t cta_mask) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(bar), "h"(cta_mask)
+                 : "memory");
+}
+// Arrive on an mbarrier given by its shared::cluster address (own CTA or a peer), with the instruction's default
+// semantics (release at CTA scope). A cluster-scope release here waits for every outstanding memory operation of the
+// thread and cost about 1 us per arrival in the pair kernel's pipeline; the data this arrival publishes is in the
+// arriving CTA's own shared memory, made visible to the tensor cores by fence.proxy.async before the arrival.
+KEA_DEVI void mbar_arrive_cluster(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// Like mbar_test / mbar_wait, with acquire at cluster scope (the phase was completed by arrivals from a peer CTA).
+KEA_DEVI bool mbar_test_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(1000000u)
+        : "memory");
+    return done != 0;
+}
+KEA_DEVI bool mbar_wait_cluster(uint32_t bar, uint32_t parity, long long budget) {
+    if (mbar_test_cluster(bar, parity)) return true;
+    const long long start = clock64();
+    while (!mbar_test_cluster(bar, parity)) {
+        if (clock64() - start > budget) return false;
+    }
+    return true;
 }
 
 // ---- programmatic dependent launch --------------------------------------------------------------------------

@@ -17,7 +17,7 @@ LIB_PATH = Path(os.environ.get("KEA_LOWBIT_LIB", Path(__file__).resolve().parent
 
 OK, INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES, CUDA, NO_DEVICE, DEVICE_TIMEOUT, CAPTURE = range(9)
 OUT_F32, OUT_F16 = 0, 1
-FLAG_SILU, FLAG_ORDER1, FLAG_PDL = 1, 2, 4
+FLAG_SILU, FLAG_ORDER1, FLAG_PDL, FLAG_NO_PAIR = 1, 2, 4, 8
 QUANT_INPUT_SILU = 1
 DEVERR_TIMEOUT, DEVERR_TAIL_BITS, DEVERR_TERNARY_11 = 1, 2, 4
 
@@ -42,7 +42,7 @@ class GemmDesc(ctypes.Structure):
 
 class GemmConfig(ctypes.Structure):
     _fields_ = [("tile_m", ctypes.c_int32), ("tile_n", ctypes.c_int32), ("splits", ctypes.c_int32),
-                ("stages", ctypes.c_int32), ("smem_bytes", ctypes.c_int32)]
+                ("stages", ctypes.c_int32), ("smem_bytes", ctypes.c_int32), ("pair", ctypes.c_int32)]
 
 
 class QuantizeDesc(ctypes.Structure):

@@ -18,13 +18,18 @@ SMS = 148
 
 @dataclasses.dataclass(frozen=True)
 class DotConfig:
-    """CTA = `tile_m` tokens x `tile_n` channels over 1/`splits` of K, `stages` k128 blocks in flight."""
+    """CTA = `tile_m` tokens x `tile_n` channels over 1/`splits` of K, `stages` k128 blocks in flight. With `pair`,
+    the persistent CTA-pair kernel: 256 x 256 tiles per pair of SMs (tcgen05 cta_group::2), walked by at most
+    SMS / 2 pairs, two accumulator buffers in tensor memory."""
     tile_m: int
     tile_n: int
     splits: int
     stages: int
+    pair: int = 0
 
     def label(self) -> str:
+        if self.pair:
+            return f"pair{self.tile_m}x{self.tile_n}_s{self.stages}"
         return f"m{self.tile_m}_n{self.tile_n}_c{self.splits}_s{self.stages}"
 
     def validate(self, parts: int = 1) -> None:
@@ -33,10 +38,13 @@ class DotConfig:
             raise ValueError(f"invalid config {self}")
 
     def grid(self, m: int, n: int) -> tuple[int, int, int]:
+        if self.pair:
+            tiles = -(-n // self.tile_n) * -(-m // self.tile_m)
+            return (2 * min(tiles, SMS // 2), 1, 1)
         return (-(-n // self.tile_n), -(-m // self.tile_m), self.splits)
 
 
 def choose(m: int, n: int, k: int, wbits: int = 1, parts: int = 1) -> DotConfig:
     """The configuration the library uses for this shape (the C table)."""
     c = _lib.choose_config(max(m, 0), n, k, wbits, parts)
-    return DotConfig(c.tile_m, c.tile_n, c.splits, c.stages)
+    return DotConfig(c.tile_m, c.tile_n, c.splits, c.stages, c.pair)

@@ -77,9 +77,11 @@ def quantize(x: Tensor, rows: tuple[int, int, int, int], m: int, k: int, parts: 
 
 def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n: int, k: int, alpha: Tensor,
          bias: Tensor | None, y: Tensor, *, parts: int, silu: bool = False, order: int = 0, acc: Tensor | None = None,
-         config=None, pdl: bool = False, error_word: Tensor | None = None) -> None:
+         config=None, pdl: bool = False, error_word: Tensor | None = None, pair: bool = True) -> None:
     """y[:m] (row stride y.stride(0); FP32 or FP16) from q int8 [parts, m, ldq] and qs FP32 [parts, m].
-    acc, when given, receives the exact INT32 accumulators as int32 [parts, m, n] (any row / part strides)."""
+    acc, when given, receives the exact INT32 accumulators as int32 [parts, m, n] (any row / part strides).
+    `config` forces the per-tile kernel's tiles (a pair config from the table forces nothing); pair=False keeps the
+    dispatch table away from the persistent CTA-pair kernel."""
     if m == 0:
         return
     if parts not in (1, 2, 3):
@@ -114,8 +116,9 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
     if acc is not None:
         d.acc, d.ld_acc, d.acc_part_stride = acc.data_ptr(), acc.stride(1), acc.stride(0)
     d.m = m
-    d.flags = (_lib.FLAG_SILU if silu else 0) | (_lib.FLAG_ORDER1 if order else 0) | (_lib.FLAG_PDL if pdl else 0)
-    if config is not None:
+    d.flags = (_lib.FLAG_SILU if silu else 0) | (_lib.FLAG_ORDER1 if order else 0) | (_lib.FLAG_PDL if pdl else 0) \
+        | (0 if pair else _lib.FLAG_NO_PAIR)
+    if config is not None and not getattr(config, "pair", 0):
         d.tile_m, d.tile_n, d.splits, d.stages = config.tile_m, config.tile_n, config.splits, config.stages
     if error_word is not None:
         d.error_word = error_word.data_ptr()

@@ -54,8 +54,19 @@ int kea_oracle_unpack(const uint8_t *codes, int wbits, int n, int k, int8_t *w) 
 }
 
 /* Panels: [ceil(n/128)][ceil(k/128)][wbits][4 words][128 rows][4 bytes]; row r of sub-block s of k-block b of tile
- * t holds the 16 export bytes of channel 128 t + r starting at byte 16 wbits b + 16 s (zero past the row end), as four
- * words; byte i of the 16 goes to word i / 4, byte i % 4, at ((i / 4) * 128 + r) * 4 within the sub-block. */
+ * t holds the 16 export bytes of channel 128 t + r starting at byte 16 wbits b + 16 s (zero past the row end), read
+ * as four little-endian words (bytes 4 j .. 4 j + 3 form word j), stored at (j * 128 + r) * 4 within the sub-block
+ * after the codes of each word are interleaved: 1 bit - code i (bit i) moves to bit 4 (i % 8) + i / 8; 2 bits -
+ * field i (bits 2 i, 2 i + 1) moves to bits 4 (i % 8) + 2 (i / 8), + 1. */
+static uint32_t interleave(uint32_t w, int wbits) {
+    uint32_t out = 0;
+    if (wbits == 1)
+        for (int i = 0; i < 32; ++i) out |= ((w >> i) & 1u) << (4 * (i % 8) + i / 8);
+    else
+        for (int i = 0; i < 16; ++i) out |= ((w >> (2 * i)) & 3u) << (4 * (i % 8) + 2 * (i / 8));
+    return out;
+}
+
 void kea_oracle_panels(const uint8_t *codes, int wbits, int n, int k, uint8_t *out) {
     const int row_bytes = (k * wbits + 7) / 8;
     const int nt = (n + 127) / 128, kb = (k + 127) / 128;
@@ -64,10 +75,15 @@ void kea_oracle_panels(const uint8_t *codes, int wbits, int n, int k, uint8_t *o
         for (int b = 0; b < kb; ++b)
             for (int s = 0; s < wbits; ++s, ++sub)
                 for (int r = 0; r < 128; ++r)
-                    for (int i = 0; i < 16; ++i) {
-                        const int ch = t * 128 + r, byte = b * 16 * wbits + s * 16 + i;
-                        out[sub * 2048 + ((i / 4) * 128 + r) * 4 + i % 4] =
-                            (ch < n && byte < row_bytes) ? codes[(long)ch * row_bytes + byte] : 0;
+                    for (int j = 0; j < 4; ++j) {
+                        const int ch = t * 128 + r;
+                        uint32_t w = 0;
+                        for (int i = 0; i < 4; ++i) {
+                            const int byte = b * 16 * wbits + s * 16 + 4 * j + i;
+                            if (ch < n && byte < row_bytes) w |= (uint32_t)codes[(long)ch * row_bytes + byte] << (8 * i);
+                        }
+                        w = interleave(w, wbits);
+                        for (int i = 0; i < 4; ++i) out[sub * 2048 + (j * 128 + r) * 4 + i] = (uint8_t)(w >> (8 * i));
                     }
 }
 

@@ -51,7 +51,7 @@ def _channel(n: int, seed: int, bias: bool):
     return alpha, b
 
 
-def _run(codes, wbits, n, k, q, qs, alpha, bias, *, flags=0, out=torch.float32, config=None, pdl=False):
+def _run(codes, wbits, n, k, q, qs, alpha, bias, *, flags=0, out=torch.float32, config=None, pdl=False, pair=True):
     parts, m, ldq = q.shape
     panels = lowbit.prepare_panels(torch.from_numpy(codes).to(DEV), wbits, n, k)
     qd, qsd = torch.from_numpy(q).to(DEV), torch.from_numpy(qs).to(DEV)
@@ -60,7 +60,7 @@ def _run(codes, wbits, n, k, q, qs, alpha, bias, *, flags=0, out=torch.float32, 
     y = torch.full((m, n), float("nan"), device=DEV, dtype=out)
     acc = torch.full((parts, m, n), -7, device=DEV, dtype=torch.int32)
     lowbit.gemm(qd, qsd, ldq, m, panels, wbits, n, k, ad, bd, y, parts=parts, silu=bool(flags & 1),
-                order=(flags >> 1) & 1, acc=acc, config=config, pdl=pdl)
+                order=(flags >> 1) & 1, acc=acc, config=config, pdl=pdl, pair=pair)
     torch.cuda.synchronize()
     assert _lib.read_device_error() == 0
     return y.cpu(), acc.cpu().numpy()
@@ -234,6 +234,62 @@ def test_full_size_m8192_rows_sampled(wbits):
     # checksum of checksums: sum_n acc[m, n] = q[m] . (sum_n w[n]) exactly, for every row
     colsum = w.astype(np.int64).sum(axis=0)
     assert np.array_equal(acc[0].astype(np.int64).sum(axis=1), q[0, :, :k].astype(np.int64) @ colsum)
+
+
+# ---- the persistent CTA-pair kernel (large M) ---------------------------------------------------------------------
+
+PAIR_SHAPES = [(256, 128, 257), (512, 2048, 300), (768, 136, 513), (256, 200, 700), (1024, 4096, 1000),
+               (4096, 1024, 2048), (2048, 1024, 611)]
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("n,k,m", PAIR_SHAPES)
+@pytest.mark.parametrize("out", [torch.float32, torch.float16])
+def test_pair_kernel_equals_oracle(wbits, n, k, m, out):
+    """Ragged K (zero-filled boxes), ragged M (clipped stores), one to several tiles per pair of SMs."""
+    assert configs.choose(m, n, k, wbits, 1).pair == 1
+    seed = wbits * 977 + n + k + m
+    codes, w = _codes(wbits, n, k, seed)
+    q, qs = _activations(1, m, k, seed)
+    alpha, bias = _channel(n, seed, m % 2 == 1)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias, out=out)
+    want, want_acc = oracle.reference(q, qs, w, alpha, bias)
+    _check(y, acc, want, want_acc, 0)
+
+
+@pytest.mark.parametrize("out", [torch.float32, torch.float16])
+def test_pair_kernel_silu_epilogue(out):
+    n, k, m = 1024, 1024, 777
+    codes, w = _codes(2, n, k, 41)
+    q, qs = _activations(1, m, k, 41)
+    alpha, bias = _channel(n, 41, True)
+    y, acc = _run(codes, 2, n, k, q, qs, alpha, bias, flags=1, out=out)
+    want, want_acc = oracle.reference(q, qs, w, alpha, bias, 1)
+    _check(y, acc, want, want_acc, 1)
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("n,k,m", [(4096, 1024, 8192), (1024, 4096, 8192), (3072, 1024, 32000)])
+def test_pair_kernel_equals_per_tile_kernel_bitwise(wbits, n, k, m):
+    """At full BASELINE sizes (7 and more tiles per pair, both accumulator buffers reused many times) the pair kernel
+    and the per-tile kernel give identical FP16 outputs and INT32 accumulators."""
+    codes, _ = _codes(wbits, n, k, m + n)
+    q, qs = _activations(1, m, k, 5)
+    alpha, _ = _channel(n, 5, False)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, None, out=torch.float16)
+    y2, acc2 = _run(codes, wbits, n, k, q, qs, alpha, None, out=torch.float16, pair=False)
+    assert np.array_equal(acc, acc2)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+
+
+def test_pair_kernel_pdl_chain_matches():
+    n, k, m = 1024, 1024, 1024
+    codes, w = _codes(1, n, k, 8)
+    q, qs = _activations(1, m, k, 8)
+    alpha, _ = _channel(n, 8, False)
+    y, acc = _run(codes, 1, n, k, q, qs, alpha, None, pdl=True)
+    want, want_acc = oracle.reference(q, qs, w, alpha)
+    _check(y, acc, want, want_acc, 0)
 
 
 def test_pdl_launch_chain_matches():
