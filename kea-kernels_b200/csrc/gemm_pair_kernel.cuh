@@ -13,17 +13,17 @@
 // 256-column accumulator buffers, so the epilogue of tile i (8 warps per CTA) runs while the MMAs of tile i + 1
 // accumulate into the other buffer.
 //
-// Warps per CTA (576 threads):
+// Warps per CTA (512 threads):
 //   warp 0       producer: per k-block one TMA box of activations (128 tokens x 128 k, 128-byte swizzle) and one bulk
 //                copy of the packed codes (128 channel rows x 128 k), on this CTA's `full` barrier;
 //   warp 1       allocates tensor memory for the pair; in the even CTA one elected lane issues the MMAs, frees each
 //                stage in both CTAs (tcgen05.commit to both CTAs' `empty`) and hands finished accumulators to both
 //                CTAs' epilogues (`acc_full`);
-//   warps 2-9    epilogue: TMEM -> comb_1 * alpha (+ bias) (SiLU) -> FP32 / FP16, staged in shared memory and written
-//                with TMA stores; then release the buffer (`acc_empty` of the even CTA, 16 warp arrivals);
-//   warps 10-17  expanders, two groups of four warps taking alternate k-blocks: packed codes -> INT8 +-1 / -1 0 +1 in
-//                the 128-byte-swizzled K-major B tile, then arrive on the even CTA's `ready` barrier (8 warp arrivals:
-//                the stage is complete in both CTAs).
+//   warps 2-7    expanders, two groups of three warps taking alternate k-blocks: packed codes -> INT8 +-1 / -1 0 +1
+//                in the 128-byte-swizzled K-major B tile, then arrive on the even CTA's `ready` barrier (6 warp
+//                arrivals: the stage is complete in both CTAs);
+//   warps 8-15   epilogue: TMEM -> comb_1 * alpha (+ bias) (SiLU) -> FP32 / FP16, staged in shared memory and written
+//                with TMA stores; then release the buffer (`acc_empty` of the even CTA, 16 warp arrivals).
 // Every wait is bounded (kWaitBudget); on expiry the kernel reports KEA_DEVERR_TIMEOUT, lets its copies and MMAs
 // drain, and returns.
 #pragma once
@@ -32,14 +32,15 @@
 
 namespace kea {
 
-constexpr int kPairWarps = 18;
-constexpr int kPairThreads = kPairWarps * 32;     // 576
+constexpr int kPairWarps = 16;
+constexpr int kPairThreads = kPairWarps * 32;     // 512: four warps per SM sub-partition, so 128 registers a thread
 constexpr int kPairTileM = 256;                   // tokens per pair tile (128 per CTA)
 constexpr int kPairTileN = 256;                   // channels per pair tile (one 128-row panel tile per CTA)
-constexpr int kPairEpiWarp0 = 2, kPairEpiWarps = 8;
-constexpr int kPairExpWarp0 = 10, kPairExpWarps = 8;
+constexpr int kPairExpWarp0 = 2, kPairExpWarps = 6;
+constexpr int kPairEpiWarp0 = 8, kPairEpiWarps = 8;
 constexpr int kPairExpGroups = 2, kPairExpGroupWarps = kPairExpWarps / kPairExpGroups;
-constexpr int kPairMaxStages = 8;
+constexpr int kPairMaxStages = 8;                // load slots (activation box + packed codes)
+constexpr int kPairBStages = 3;                   // expanded-weight (B) slots
 constexpr uint32_t kPairAccCols = 256;            // one accumulator buffer: 128 lanes x 256 INT32 columns
 constexpr uint32_t kPairTmemCols = 512;           // two buffers
 constexpr uint32_t kPairHalfTile = 16384;         // 128 rows x 128 bytes: one CTA's activation or B tile per stage
@@ -83,89 +84,119 @@ __shared__ long long s_ptrace_clock0;
 KEA_DEVI float int_to_float_exact(int a) { return __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f); }
 
 // comb_1, alpha / bias, optional SiLU: one IEEE FP32 rounding per operation (the reference's epilogue order).
-KEA_DEVI float finish1(int acc, float s, float alpha, bool has_bias, float bias, int flags) {
+template <bool BIAS, bool SILU>
+KEA_DEVI float finish1(int acc, float s, float alpha, float bias) {
     const float r = __fmul_rn(int_to_float_exact(acc), s);
-    float y = has_bias ? __fmaf_rn(r, alpha, bias) : __fmul_rn(r, alpha);
-    if (flags & 1) y = silu_approx(y);
+    float y = BIAS ? __fmaf_rn(r, alpha, bias) : __fmul_rn(r, alpha);
+    if constexpr (SILU) y = silu_approx(y);
     return y;
 }
 
-// One epilogue warp's share of a finished tile: its 32 token rows x 128 channels of tensor memory, in groups of
-// 4 KB of output (64 FP16 or 32 FP32 channels). For each 32 columns of a group the warp loads them from TMEM and
-// finishes them in registers (alpha / bias from the warp's shared-memory copy); before the group's first staging store
-// it waits until the previous group's TMA stores have read the warp's 4 KB staging buffer; then it stages the rows
-// (32 x 64-byte boxes, 64-byte swizzle as the store's tensor map), fences once and issues two TMA stores. After its
-// last TMEM read the warp releases the accumulator buffer (`acc_empty`, a shared::cluster address).
-template <bool F16, bool BIAS>
-KEA_DEVI void pair_epilogue_tile(const PairArgs &a, const CUtensorMap *ymap, uint32_t cbase, uint32_t stg,
-                                 uint32_t s_al, uint32_t s_bi, uint32_t acc_empty, int nbase, int trow0, int t, float sq) {
-    constexpr int GROUP = F16 ? 64 : 32;     // channels per 4 KB group
-    constexpr int CW = F16 ? 32 : 16;        // channels per 64-byte box row
+// One epilogue warp's share of a finished tile: its 32 token rows x 128 channels of tensor memory in four chunks of
+// 32 columns. The TMEM load of chunk i + 1 is in flight while chunk i is finished in registers (alpha / bias from the
+// warp's shared-memory copy). A chunk is 2 KB of FP16 output (one 32 x 64-byte box) or 4 KB of FP32 (two boxes);
+// it is staged in the warp's 4 KB buffer (64-byte swizzle, as the store's tensor map) once the store that last used
+// that space has read it, then fenced and written by TMA. After the last TMEM load the warp releases the accumulator
+// buffer (`acc_empty`, a shared::cluster address).
+template <bool F16, bool BIAS, bool SILU>
+KEA_DEVI void pair_finish_chunk(uint32_t (&v)[32], uint32_t s_al, uint32_t s_bi, int c, float sq) {
+#pragma unroll
+    for (int jj = 0; jj < 32; jj += 4) {
+        const uint4 alu = ld_shared_v4(s_al + (uint32_t)(c + jj) * 4u);
+        uint4 biu = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (BIAS) biu = ld_shared_v4(s_bi + (uint32_t)(c + jj) * 4u);
+        const float f0 = finish1<BIAS, SILU>((int)v[jj], sq, __uint_as_float(alu.x), __uint_as_float(biu.x));
+        const float f1 = finish1<BIAS, SILU>((int)v[jj + 1], sq, __uint_as_float(alu.y), __uint_as_float(biu.y));
+        const float f2 = finish1<BIAS, SILU>((int)v[jj + 2], sq, __uint_as_float(alu.z), __uint_as_float(biu.z));
+        const float f3 = finish1<BIAS, SILU>((int)v[jj + 3], sq, __uint_as_float(alu.w), __uint_as_float(biu.w));
+        if constexpr (F16) {   // FP16 pairs packed into v[0 .. 16)
+            v[jj / 2] = pack_half2(f0, f1);
+            v[jj / 2 + 1] = pack_half2(f2, f3);
+        } else {               // FP32 bit patterns in place
+            v[jj] = __float_as_uint(f0);
+            v[jj + 1] = __float_as_uint(f1);
+            v[jj + 2] = __float_as_uint(f2);
+            v[jj + 3] = __float_as_uint(f3);
+        }
+    }
+}
+
+template <bool F16>
+KEA_DEVI void pair_stage_and_store(const CUtensorMap *ymap, const uint32_t (&v)[32], uint32_t stg, int ci, int n,
+                                   int trow0) {
+    constexpr int BOXES = F16 ? 1 : 2;     // 64-byte box rows per chunk
     const int lane = threadIdx.x & 31;
-#pragma unroll 1
-    for (int c0 = 0; c0 < 128; c0 += GROUP) {
-        KEA_PTRACE(threadIdx.x == kPairEpiWarp0 * 32, 10, c0 / GROUP);
+    const uint32_t slot = stg + (F16 ? (uint32_t)(ci & 1) * kPairStageOut : 0u);
+    if (lane == 0) {   // the store that last read this space must be done with it
+        if constexpr (F16) bulk_wait_group_read1();
+        else bulk_wait_group_read0();
+    }
+    __syncwarp();
 #pragma unroll
-        for (int h = 0; h < GROUP / 32; ++h) {
-            const int c = c0 + 32 * h;
-            uint32_t v[32];
-            tmem_ld16(cbase + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-            tmem_ld16(cbase + (uint32_t)(c + 16), *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-            tmem_wait_ld();
-            if (c + 32 >= 128) {   // this warp's last read of the buffer: hand it back to the MMA warp
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(acc_empty);
-            }
-            if (a.acc && t < a.M) {
-                int4 *dst = reinterpret_cast<int4 *>(a.acc + (long long)t * a.ld_acc + nbase + c);
+    for (int b = 0; b < BOXES; ++b) {
 #pragma unroll
-                for (int q = 0; q < 8; ++q) dst[q] = make_int4((int)v[4 * q], (int)v[4 * q + 1], (int)v[4 * q + 2], (int)v[4 * q + 3]);
-            }
-            // finish in place: FP16 pairs packed into v[0 .. 16), FP32 bit patterns in v[0 .. 32)
-#pragma unroll
-            for (int jj = 0; jj < 32; jj += 4) {
-                const uint4 alu = ld_shared_v4(s_al + (uint32_t)(c + jj) * 4u);
-                uint4 biu = make_uint4(0u, 0u, 0u, 0u);
-                if constexpr (BIAS) biu = ld_shared_v4(s_bi + (uint32_t)(c + jj) * 4u);
-                const float f0 = finish1((int)v[jj], sq, __uint_as_float(alu.x), BIAS, __uint_as_float(biu.x), a.flags);
-                const float f1 = finish1((int)v[jj + 1], sq, __uint_as_float(alu.y), BIAS, __uint_as_float(biu.y), a.flags);
-                const float f2 = finish1((int)v[jj + 2], sq, __uint_as_float(alu.z), BIAS, __uint_as_float(biu.z), a.flags);
-                const float f3 = finish1((int)v[jj + 3], sq, __uint_as_float(alu.w), BIAS, __uint_as_float(biu.w), a.flags);
-                if constexpr (F16) {
-                    v[jj / 2] = pack_half2(f0, f1);
-                    v[jj / 2 + 1] = pack_half2(f2, f3);
-                } else {
-                    v[jj] = __float_as_uint(f0);
-                    v[jj + 1] = __float_as_uint(f1);
-                    v[jj + 2] = __float_as_uint(f2);
-                    v[jj + 3] = __float_as_uint(f3);
-                }
-            }
-            if (h == 0) {   // the previous group's stores must have read the staging buffer
-                if (lane == 0) bulk_wait_group_read0();
-                __syncwarp();
-            }
-            // FP16: these 32 channels are box h; FP32: boxes 0 and 1 (16 channels each)
-#pragma unroll
-            for (int b = 0; b < (F16 ? 1 : 2); ++b) {
-                const uint32_t box = stg + (uint32_t)(F16 ? h : b) * kPairStageOut;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t off = (uint32_t)lane * 64u + (uint32_t)q * 16u;
-                    const int w0 = b * 16 + q * 4;
-                    st_shared_v4(box + (off ^ (((off >> 7) & 3u) << 4)), v[w0], v[w0 + 1], v[w0 + 2], v[w0 + 3]);
-                }
-            }
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t off = (uint32_t)lane * 64u + (uint32_t)q * 16u;
+            const int w0 = b * 16 + q * 4;
+            st_shared_v4(slot + (uint32_t)b * kPairStageOut + (off ^ (((off >> 7) & 3u) << 4)), v[w0], v[w0 + 1],
+                         v[w0 + 2], v[w0 + 3]);
         }
-        fence_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-            tma_store_2d(ymap, stg, nbase + c0, trow0);
-            tma_store_2d(ymap, stg + kPairStageOut, nbase + c0 + CW, trow0);
-            bulk_commit_group();
+    }
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+#pragma unroll
+        for (int b = 0; b < BOXES; ++b) tma_store_2d(ymap, slot + (uint32_t)b * kPairStageOut, n + b * 16, trow0);
+        bulk_commit_group();
+    }
+}
+
+KEA_DEVI void pair_load32(uint32_t taddr, uint32_t (&v)[32]) {
+    tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+    tmem_ld16(taddr + 16u, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+}
+
+template <bool F16, bool BIAS, bool SILU>
+KEA_DEVI void pair_epilogue_tile(const PairArgs &a, const CUtensorMap *ymap, uint32_t cbase, uint32_t stg,
+                                 uint32_t s_al, uint32_t s_bi, uint32_t acc_empty, int nbase, int trow0, int t, float sq,
+                                 int j) {
+    const int lane = threadIdx.x & 31;
+    const bool tr = threadIdx.x == kPairEpiWarp0 * 32 && j < 16;
+    (void)tr;
+    uint32_t va[32], vb[32];
+    pair_load32(cbase, va);
+#pragma unroll
+    for (int ci = 0; ci < 4; ci += 2) {
+        // chunk ci in va; chunk ci + 1 into vb while va is finished
+        KEA_PTRACE(tr, 10, j * 4 + ci);
+        tmem_wait_ld();
+        KEA_PTRACE(tr, 11, j * 4 + ci);
+        pair_load32(cbase + (uint32_t)(32 * (ci + 1)), vb);
+        if (a.acc && t < a.M) {
+            int4 *dst = reinterpret_cast<int4 *>(a.acc + (long long)t * a.ld_acc + nbase + 32 * ci);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) dst[q] = make_int4((int)va[4 * q], (int)va[4 * q + 1], (int)va[4 * q + 2], (int)va[4 * q + 3]);
         }
-        KEA_PTRACE(threadIdx.x == kPairEpiWarp0 * 32, 14, c0 / GROUP);
+        pair_finish_chunk<F16, BIAS, SILU>(va, s_al, s_bi, 32 * ci, sq);
+        KEA_PTRACE(tr, 12, j * 4 + ci);
+        pair_stage_and_store<F16>(ymap, va, stg, ci, nbase + 32 * ci, trow0);
+        KEA_PTRACE(tr, 13, j * 4 + ci);
+        // chunk ci + 1 in vb; chunk ci + 2 into va
+        tmem_wait_ld();
+        if (ci + 2 < 4) {
+            pair_load32(cbase + (uint32_t)(32 * (ci + 2)), va);
+        } else {   // every TMEM read of the buffer is done: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc_empty);
+        }
+        if (a.acc && t < a.M) {
+            int4 *dst = reinterpret_cast<int4 *>(a.acc + (long long)t * a.ld_acc + nbase + 32 * (ci + 1));
+#pragma unroll
+            for (int q = 0; q < 8; ++q) dst[q] = make_int4((int)vb[4 * q], (int)vb[4 * q + 1], (int)vb[4 * q + 2], (int)vb[4 * q + 3]);
+        }
+        pair_finish_chunk<F16, BIAS, SILU>(vb, s_al, s_bi, 32 * (ci + 1), sq);
+        pair_stage_and_store<F16>(ymap, vb, stg, ci + 1, nbase + 32 * (ci + 1), trow0);
     }
 }
 
@@ -174,9 +205,10 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                                                                           const __grid_constant__ CUtensorMap ymap,
                                                                           const PairArgs a) {
     extern __shared__ uint8_t dyn_smem[];
-    __shared__ __align__(8) uint64_t bar_full[kPairMaxStages];    // this CTA's stage landed (TMA box + codes)
-    __shared__ __align__(8) uint64_t bar_ready[kPairMaxStages];   // even CTA: the stage is expanded in both CTAs
-    __shared__ __align__(8) uint64_t bar_empty[kPairMaxStages];   // the pair's MMAs are done with the stage
+    __shared__ __align__(8) uint64_t bar_full[kPairMaxStages];    // this CTA's load slot landed (TMA box + codes)
+    __shared__ __align__(8) uint64_t bar_empty[kPairMaxStages];   // the pair's MMAs are done with the load slot
+    __shared__ __align__(8) uint64_t bar_ready[kPairBStages];     // even CTA: the B slot is expanded in both CTAs
+    __shared__ __align__(8) uint64_t bar_bempty[kPairBStages];    // the pair's MMAs are done with the B slot
     __shared__ __align__(8) uint64_t bar_acc_full[2];             // accumulator buffer complete
     __shared__ __align__(8) uint64_t bar_acc_empty[2];            // even CTA: buffer drained by both epilogues
     __shared__ __align__(8) uint64_t bar_drain;                   // even CTA: every issued MMA has completed
@@ -187,8 +219,13 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
     const uint32_t rank = cluster_ctarank();
     const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
     const uint32_t base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
+    // Shared memory: [activation boxes: S x 16 KB][B tiles: kPairBStages x 16 KB][packed codes: S x PKB][epilogue
+    // staging][channel constants]. Load slot s (activations + codes) and B slot b turn over independently: a k-block
+    // step i uses load slot i % S and B slot i % kPairBStages, so the loads run S steps ahead of the MMAs while only
+    // a few expanded tiles are kept.
     const int S = a.stages;
-    const uint32_t A0 = base, B0 = base + (uint32_t)S * kPairHalfTile, PK0 = base + 2u * (uint32_t)S * kPairHalfTile;
+    const uint32_t A0 = base, B0 = base + (uint32_t)S * kPairHalfTile;
+    const uint32_t PK0 = B0 + (uint32_t)kPairBStages * kPairHalfTile;
     const uint32_t STG0 = (PK0 + (uint32_t)S * PKB + 1023u) & ~1023u;
     const int kbt = a.kb_total;
 
@@ -203,8 +240,11 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&bar_full[s]), 1);
-            mbar_init(smem_u32(&bar_ready[s]), 2 * kPairExpGroupWarps);
             mbar_init(smem_u32(&bar_empty[s]), 1);
+        }
+        for (int b = 0; b < kPairBStages; ++b) {
+            mbar_init(smem_u32(&bar_ready[b]), 2 * kPairExpGroupWarps);
+            mbar_init(smem_u32(&bar_bempty[b]), 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(smem_u32(&bar_acc_full[b]), 1);
@@ -269,8 +309,6 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
         if (rank == 0) {
             const uint32_t idesc = idesc_i8(2 * kBM, (uint32_t)kPairTileN);
             const uint64_t ad0 = sw128_kmajor_desc(A0), bd0 = sw128_kmajor_desc(B0);
-            int s = 0;
-            uint32_t ph = 0;
             int j = 0, step = 0;
             for (int tile = pair; tile < a.tiles; tile += npairs, ++j) {
                 const int buf = j & 1;
@@ -284,29 +322,27 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                 }
                 tc_fence_after();
                 const uint32_t dcol = tmem + (uint32_t)buf * kPairAccCols;
-                for (int kb = 0; kb < kbt; ++kb) {
-                    const bool ready = mbar_wait_cluster(smem_u32(&bar_ready[s]), ph, kWaitBudget);
+                for (int kb = 0; kb < kbt; ++kb, ++step) {
+                    const int sa = step % S, sb = step % kPairBStages;
+                    const bool ready = mbar_wait_cluster(smem_u32(&bar_ready[sb]), (uint32_t)((step / kPairBStages) & 1),
+                                                         kWaitBudget);
                     if (!__all_sync(0xFFFFFFFFu, ready)) {
                         ok = false;
                         break;
                     }
                     KEA_PTRACE(lane == 0, 3, step);
-                    const uint64_t ad = ad0 + (uint64_t)(((uint32_t)s * kPairHalfTile) >> 4);
-                    const uint64_t bd = bd0 + (uint64_t)(((uint32_t)s * kPairHalfTile) >> 4);
+                    const uint64_t ad = ad0 + (uint64_t)(((uint32_t)sa * kPairHalfTile) >> 4);
+                    const uint64_t bd = bd0 + (uint64_t)(((uint32_t)sb * kPairHalfTile) >> 4);
                     if (elect_one()) {
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)   // K = 32 per MMA: + 32 bytes = 2 descriptor units
                             mma_i8_pair(dcol, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
                                         (kb > 0 || kk > 0) ? 1u : 0u);
-                        mma_commit_pair(smem_u32(&bar_empty[s]), (uint16_t)3);
+                        mma_commit_pair(smem_u32(&bar_empty[sa]), (uint16_t)3);
+                        mma_commit_pair(smem_u32(&bar_bempty[sb]), (uint16_t)3);
                     }
                     __syncwarp();
                     KEA_PTRACE(lane == 0, 4, step);
-                    ++step;
-                    if (++s == S) {
-                        s = 0;
-                        ph ^= 1u;
-                    }
                 }
                 if (!ok) break;
                 if (elect_one()) mma_commit_pair(smem_u32(&bar_acc_full[buf]), (uint16_t)3);
@@ -319,9 +355,9 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
             mbar_wait(smem_u32(&bar_drain), 0u, kWaitBudget);
             __syncwarp();
         }
-    } else if (warp >= kPairExpWarp0) {
+    } else if (warp < kPairEpiWarp0) {
         // ---------------- expanders ----------------
-        // Two groups of four warps take alternate k-blocks, so one group's fence and barrier round trip overlaps the
+        // Two groups of three warps take alternate k-blocks, so one group's fence and barrier round trip overlaps the
         // other group's expansion.
         const int eg = (warp - kPairExpWarp0) / kPairExpGroupWarps;             // group
         const int e = threadIdx.x - (kPairExpWarp0 + eg * kPairExpGroupWarps) * 32;   // thread within the group
@@ -331,25 +367,27 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
         for (int tile = pair; tile < a.tiles; tile += npairs) ++my_tiles;
         const int steps = my_tiles * kbt;
         for (int step = eg; step < steps; step += kPairExpGroups) {
-            const int s = step % S;
-            const uint32_t ph = (uint32_t)((step / S) & 1);
-            const bool landed = mbar_wait(smem_u32(&bar_full[s]), ph, kWaitBudget);
-            if (!__all_sync(0xFFFFFFFFu, landed)) {
+            const int sa = step % S, sb = step % kPairBStages;
+            // the codes have landed, and the MMAs that last read B slot sb (step - kPairBStages) are done
+            bool free = mbar_wait(smem_u32(&bar_full[sa]), (uint32_t)((step / S) & 1), kWaitBudget);
+            if (step >= kPairBStages)
+                free = free && mbar_wait(smem_u32(&bar_bempty[sb]), (uint32_t)(((step / kPairBStages) & 1) ^ 1), kWaitBudget);
+            if (!__all_sync(0xFFFFFFFFu, free)) {
                 ok = false;
                 if (lane == 0) report(a.err, 1u);
                 break;
             }
             KEA_PTRACE(e == 0, 1, step);
-            const uint32_t spk = PK0 + (uint32_t)s * PKB, sb = B0 + (uint32_t)s * kPairHalfTile;
+            const uint32_t spk = PK0 + (uint32_t)sa * PKB, sbt = B0 + (uint32_t)sb * kPairHalfTile;
 #pragma unroll
-            for (int u = e; u < units; u += kPairExpGroupWarps * 32) expand_unit<WBITS>(spk, sb, 7, u);
+            for (int u = e; u < units; u += kPairExpGroupWarps * 32) expand_unit<WBITS>(spk, sbt, 7, u);
             fence_async_shared();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(ready0 + (uint32_t)s * 8u);
+            if (lane == 0) mbar_arrive_cluster(ready0 + (uint32_t)sb * 8u);
             KEA_PTRACE(e == 0, 2, step);
         }
     } else {
-        // ---------------- epilogue (warps 2-9) ----------------
+        // ---------------- epilogue (warps 8-15) ----------------
         // Warp w reads TMEM lanes 32 (w % 4) .. + 31 (its token rows) and channel half (w - 2) / 4 of every tile;
         // it finishes 32 rows x 64 bytes at a time (32 FP16 or 16 FP32 channels), staged in one of its two 2 KB
         // buffers (64-byte swizzle, as the store's tensor map) and written by one TMA store.
@@ -391,13 +429,21 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
             const float sq = t < a.M ? __ldg(a.qs + t) : 0.f;
             const uint32_t cbase = lane_base + (uint32_t)buf * kPairAccCols + (uint32_t)(half * 128);
             const uint32_t acc_empty = acc_empty0 + (uint32_t)buf * 8u;
-            if (a.y_f16) {
-                if (has_bias) pair_epilogue_tile<true, true>(a, &ymap, cbase, stg, s_al, s_bi, acc_empty, nbase, trow0, t, sq);
-                else pair_epilogue_tile<true, false>(a, &ymap, cbase, stg, s_al, s_bi, acc_empty, nbase, trow0, t, sq);
-            } else {
-                if (has_bias) pair_epilogue_tile<false, true>(a, &ymap, cbase, stg, s_al, s_bi, acc_empty, nbase, trow0, t, sq);
-                else pair_epilogue_tile<false, false>(a, &ymap, cbase, stg, s_al, s_bi, acc_empty, nbase, trow0, t, sq);
+            // one instantiation per (output type, bias, SiLU): no run-time branch inside the finishing loop
+            const int variant = (a.y_f16 ? 4 : 0) | (has_bias ? 2 : 0) | (a.flags & 1);
+#define KEA_PAIR_EPI(F16, BIAS, SILU)                                                                             \
+    pair_epilogue_tile<F16, BIAS, SILU>(a, &ymap, cbase, stg, s_al, s_bi, acc_empty, nbase, trow0, t, sq, j)
+            switch (variant) {
+                case 0: KEA_PAIR_EPI(false, false, false); break;
+                case 1: KEA_PAIR_EPI(false, false, true); break;
+                case 2: KEA_PAIR_EPI(false, true, false); break;
+                case 3: KEA_PAIR_EPI(false, true, true); break;
+                case 4: KEA_PAIR_EPI(true, false, false); break;
+                case 5: KEA_PAIR_EPI(true, false, true); break;
+                case 6: KEA_PAIR_EPI(true, true, false); break;
+                default: KEA_PAIR_EPI(true, true, true); break;
             }
+#undef KEA_PAIR_EPI
             KEA_PTRACE(ew == 0 && lane == 0, 6, j);
         }
         // The staging buffers must outlive the stores' reads of them; the global writes complete with the grid.

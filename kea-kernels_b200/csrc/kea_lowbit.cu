@@ -145,10 +145,12 @@ int max_stages(int tile_m, int tile_n, int parts, int wbits) {
 }
 
 // ---- the persistent CTA-pair kernel (gemm_pair_kernel.cuh) ---------------------------------------------------------
-// Dynamic shared memory: alignment slack + stages x (activation box + B tile + packed codes) + epilogue staging.
-int pair_stage_bytes(int wbits) { return 2 * (int)kea::kPairHalfTile + wbits * kea::kPanelSubBytes; }
+// Dynamic shared memory: alignment slack + load slots x (activation box + packed codes) + the B slots + epilogue
+// staging + channel constants.
+int pair_stage_bytes(int wbits) { return (int)kea::kPairHalfTile + wbits * kea::kPanelSubBytes; }
 int pair_smem_bytes(int wbits, int stages) {
-    return 1024 + stages * pair_stage_bytes(wbits) + (int)kea::kPairStagingBytes + (int)kea::kPairChannelBytes;
+    return 1024 + stages * pair_stage_bytes(wbits) + kea::kPairBStages * (int)kea::kPairHalfTile +
+           (int)kea::kPairStagingBytes + (int)kea::kPairChannelBytes;
 }
 int pair_max_stages(int wbits) {
     int s = kea::kPairMaxStages;
