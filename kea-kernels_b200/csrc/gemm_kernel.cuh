@@ -160,6 +160,10 @@ KEA_DEVI void expand_unit(uint32_t pk, uint32_t dst, int tn_log2, int u) {
 }
 
 // ---- epilogue ---------------------------------------------------------------------------------------------
+// SiLU behind a call: the flag is a run-time value here, and an inlined SiLU would be if-converted into predicated
+// ex2 / divide sequences that issue for every output even when the flag is off.
+__device__ __noinline__ float silu_call(float y) { return silu_approx(y); }
+
 // comb_P then alpha / bias then optional SiLU, one IEEE FP32 rounding per operation.
 KEA_DEVI float finish_value(int a0, int a1, int a2, float s0, float s1, float s2, int parts, int flags,
                             float alpha, bool has_bias, float bias) {
@@ -172,7 +176,7 @@ KEA_DEVI float finish_value(int a0, int a1, int a2, float s0, float s1, float s2
         if (parts == 3) r = __fmaf_rn(__int2float_rn(a2), s2, r);
     }
     r = has_bias ? __fmaf_rn(r, alpha, bias) : __fmul_rn(r, alpha);
-    if (flags & 1) r = silu_approx(r);
+    if (flags & 1) r = silu_call(r);
     return r;
 }
 
@@ -422,9 +426,27 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
         // ---------------- MMA issuer: the whole warp waits, lane 0 issues ----------------
         const uint32_t idesc = idesc_i8(kBM, (uint32_t)TN);
         const uint64_t a_desc0 = sw128_kmajor_desc(A0), b_desc0 = sw128_kmajor_desc(B0);
+        if (a.oneshot && nkb > 0) {
+            // Every k-block is resident and the expanders arrive on the stage barriers in order after one fence, so
+            // the last stage's barrier covers them all: one wait, then every MMA back to back (one issuing thread
+            // sustains about one tcgen05.mma per 70 clocks; a wait and a commit per stage would triple that).
+            const bool ready = mbar_wait(smem_u32(&bar_full[0]), 0u, kWaitBudget) &&
+                               mbar_wait(smem_u32(&bar_exp[nkb - 1]), 0u, kWaitBudget);
+            if (!__all_sync(0xFFFFFFFFu, ready)) {
+                ok = false;
+                if (lane == 0) report(a.err, 1u);
+            } else if (elect_one()) {
+                for (int i = 0; i < nkb; ++i) {
+                    const uint64_t ad_s = a_desc0 + (uint64_t)((i * a.a_stride) >> 4);
+                    const uint64_t bd_s = b_desc0 + (uint64_t)((i * a.b_stage) >> 4);
+                    issue_stage<P, 1, 4>(tmem, ad_s, bd_s, idesc, TN, i == 0);
+                }
+            }
+            __syncwarp();
+        }
         int s = 0;
         uint32_t ph = 0;
-        for (int i = 0; i < nkb; ++i) {
+        for (int i = 0; i < (a.oneshot ? 0 : nkb); ++i) {
             const bool ready = mbar_wait(smem_u32(&bar_full[a.oneshot ? 0 : s]), a.oneshot ? 0 : ph, kWaitBudget) &&
                                mbar_wait(smem_u32(&bar_exp[s]), ph, kWaitBudget);
             if (!__all_sync(0xFFFFFFFFu, ready)) {
