@@ -175,6 +175,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--clip-batch", type=int, default=256, help="clips in the config-3 batch (sharded over ranks)")
     ap.add_argument("--case", default=None, metavar="WBITS,N,K,M",
                     help="profiling mode: launch one GEMM case W + K times (rotating cold weights), print its timing")
     args = ap.parse_args()
@@ -300,9 +301,14 @@ def main() -> None:
     # ---- e2e through the C-ABI call with host buffers ----
     e2e = e2e_rate(torch, lowbit, dev, weights, alphas, args, world, dist if world > 1 else None, local)
 
+    # ---- the clip workloads: one 10 s clip (config 2) and a sharded batch of 256 clips (config 3) ----
+    del graphs, weights, acts, outs
+    torch.cuda.empty_cache()
+    clip = clip_workloads(torch, dev, stream, rank, world, dist if world > 1 else None, local, pdl, hbm_peak,
+                          args.clip_batch)
+
     if world > 1:
         dist.barrier(device_ids=[local])
-        del graphs
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -349,8 +355,127 @@ def main() -> None:
                        "parallelism": f"replicas x{world}", "pdl": pdl},
             "roofline": roofline, "roofline_small_m": roofline_small, "cpu_baseline": cpu, "e2e": e2e,
             "clocks": clocks, "gpu_launches": len(CASES) * args.steps, "cases": per_case,
-            "int8_peak_tops": int8_peak, "int8_peak_kind": int8_kind}
+            "int8_peak_tops": int8_peak, "int8_peak_kind": int8_kind, "clip": clip}
     print(json.dumps(line), flush=True)
+
+
+def clip_workloads(torch, dev, stream, rank, world, dist, local, pdl, hbm_peak, batch_clips):
+    """one synthetic 10 s clip (log-mel N(0, 1) [1, 128, 1000]) through the random-init 24-layer
+    1-bit FastConformer encoder and the TDT joint's greedy labels, replayed as one CUDA graph: ms per clip, cold (L2
+    flushed before every replay; the encoder's 72 MB of panels would otherwise stay in the 126 MB L2) and hot, and
+    end to end with the mel copied in from pinned host memory and the labels copied out. The low-bit path alone (the
+    192 quantize + GEMM pairs, captured on their own) gives the clip's HBM roofline: panel + scale bytes / time.
+    `batch_clips` clips sharded over the ranks (whole clips, balanced by frames), each rank runs
+    its shard as one batch (M = clips x 125 per GEMM) and the labels and timings are gathered with NCCL."""
+    from kea_kernels import batch as B
+    from kea_kernels import encoder as E
+
+    gen = torch.Generator(device=dev).manual_seed(77)
+    enc = E.FastConformerEncoder(device=dev, wbits=1, parts=1, pdl=pdl, seed=5)
+    joint = E.TDTJoint(device=dev)
+    out = {}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    with torch.cuda.stream(stream):
+        mel = torch.randn(1, 128, 1000, device=dev, generator=gen)
+        for _ in range(3):
+            labels = joint.greedy(enc(mel))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            labels = joint.greedy(enc(mel))
+        # the low-bit path alone, same shapes and order
+        xs = {k: torch.randn(1, 125, k, device=dev, generator=gen) for k in (1024, 4096)}
+        for layer in enc.layers:
+            for name in E.LAYER_LINEARS:
+                layer.lin[name](xs[layer.lin[name].in_features])
+        gl = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gl, stream=stream):
+            for layer in enc.layers:
+                for name in E.LAYER_LINEARS:
+                    layer.lin[name](xs[layer.lin[name].in_features])
+        stream.synchronize()
+
+        def timed(graph, reps, cold, pre=None, post=None):
+            evs = []
+            for i in range(reps + 3):
+                if cold:
+                    flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                if pre:
+                    pre()
+                graph.replay()
+                if post:
+                    post()
+                e1.record(stream)
+                if i >= 3:
+                    evs.append((e0, e1))
+            stream.synchronize()
+            return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+        clip_cold = timed(g, 20, True)
+        clip_hot = timed(g, 20, False)
+        lowbit_cold = timed(gl, 20, True)
+        lowbit_hot = timed(gl, 20, False)
+        host_mel = torch.randn(1, 128, 1000).pin_memory()
+        host_lab = torch.empty(1, 125, dtype=torch.int32).pin_memory()
+        clip_e2e = timed(g, 20, True, pre=lambda: mel.copy_(host_mel, non_blocking=True),
+                         post=lambda: host_lab.copy_(labels, non_blocking=True))
+    # HBM bytes a clip must stream: the panels and per-channel constants (the 125-frame activations stay in L2)
+    panel_bytes = sum(layer.lin[n].panels.numel() + 8 * layer.lin[n].out_features
+                      for layer in enc.layers for n in E.LAYER_LINEARS)
+    gops = sum(2 * 125 * layer.lin[n].out_features * layer.lin[n].in_features
+               for layer in enc.layers for n in E.LAYER_LINEARS) / 1e9
+    out["config2"] = {
+        "workload": "BASELINE config 2: one synthetic 10 s clip, log-mel N(0,1) [1,128,1000] -> 125 frames, "
+                    "random-init 24-layer 1-bit FastConformer (d 1024, 8 heads, FF 4096, conv 9) + TDT joint greedy",
+        "ms_per_clip": clip_cold, "ms_per_clip_hot": clip_hot, "ms_per_clip_e2e": clip_e2e,
+        "e2e_bytes": {"h2d": host_mel.numel() * 4, "d2h": host_lab.numel() * 4},
+        "lowbit_ms": lowbit_cold, "lowbit_ms_hot": lowbit_hot, "lowbit_gemms": 192, "lowbit_launches": 384,
+        "lowbit_gop": gops, "lowbit_tops": gops / lowbit_cold,
+        "hbm": {"bytes": panel_bytes, "achieved_gbs": panel_bytes / (lowbit_cold * 1e-3) / 1e9, "peak": hbm_peak,
+                "frac": panel_bytes / (lowbit_cold * 1e-3) / 1e9 / hbm_peak, "peak_kind": "measured"},
+        "l2": "flushed (256 MB written) before every timed replay; hot = back-to-back replays"}
+    del g, gl
+    torch.cuda.empty_cache()
+
+    # ---- config 3: the batch, sharded ----
+    n_clips = batch_clips
+    frames = [125] * n_clips
+    mine = B.shard(frames, world)[rank]
+    mels = torch.randn(len(mine), 128, 1000, device=dev, generator=gen) if mine else None
+    state = {}
+
+    def process(indices):
+        if not indices:
+            return [], 0.0
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                lab = joint.greedy(enc(mels))
+            gb = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gb, stream=stream):
+                lab = joint.greedy(enc(mels))
+            gb.replay()
+            stream.synchronize()
+            ms = timed(gb, 5, False)
+        state["graph"] = gb
+        return [lab[j] for j in range(len(indices))], ms / 1e3
+
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+    res = B.run_batch(frames, process, device=dev)
+    state.clear()
+    t = max(res.seconds)
+    m_total = 125 * n_clips
+    gop = sum(2 * m_total * layer.lin[n].out_features * layer.lin[n].in_features
+              for layer in enc.layers for n in E.LAYER_LINEARS) / 1e9
+    out["config3"] = {
+        "workload": f"BASELINE config 3: {n_clips} synthetic 10 s clips (M = {m_total} frames per GEMM over the job), "
+                    f"sharded over {world} GPU(s) as whole clips; labels and timings gathered with NCCL",
+        "clips_per_s": n_clips / t, "frames_per_s": m_total / t, "ms_per_batch": t * 1e3,
+        "per_rank_ms": [s * 1e3 for s in res.seconds], "per_rank_frames": res.frames,
+        "lowbit_gop": gop, "encoder_lowbit_tops": gop / t / 1e3,
+        "labels_gathered": len(res.tokens), "timing": "CUDA events on each rank's stream, max over ranks"}
+    return out
 
 
 def time_cases(torch, lowbit, _lib, configs, dev, stream, random_panels, alphas, pdl):

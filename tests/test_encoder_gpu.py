@@ -1,0 +1,102 @@
+"""The FastConformer call sites of the low-bit GEMM (the clip workload of BASELINE configs 2-4) against a plain
+PyTorch FP32 forward of the same layers with dense weights (codes x scale): the only differences are the residual
+INT8 activation quantization and the exact INT32 accumulation, so the relative error is set by the number of parts
+(x3: ~1e-6 per projection; x1: ~1e-2)."""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from kea_kernels import encoder as E
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _dense_linear(layer, name, x, *, norm=None, input_silu=False, silu=False):
+    w, bias = layer.weights[name]
+    if norm is not None:
+        x = F.layer_norm(x, (x.shape[-1],), norm.weight, norm.bias, norm.eps)
+    if input_silu:
+        x = F.silu(x)
+    y = F.linear(x, w.dense(), bias)
+    return F.silu(y) if silu else y
+
+
+def _dense_layer(layer, x):
+    b, t, d = x.shape
+    lin = lambda name, h, **kw: _dense_linear(layer, name, h, **kw)
+    x = x + 0.5 * lin("ff1_down", lin("ff1_up", x, norm=layer.norms["ff1"], silu=True))
+    qkv = lin("qkv", x, norm=layer.norms["att"]).view(b, t, 3, layer.heads, layer.dk)
+    q, k, v = qkv.unbind(2)
+    p = lin("linear_pos", E.rel_positions(t, d, x.device)[None])[0].view(2 * t - 1, layer.heads, layer.dk)
+    ac = torch.matmul((q + layer.pos_bias_u).transpose(1, 2), k.permute(0, 2, 3, 1))
+    bd = E.rel_shift(torch.matmul((q + layer.pos_bias_v).transpose(1, 2), p.permute(1, 2, 0)))
+    attn = torch.softmax((ac + bd) / math.sqrt(layer.dk), dim=-1)
+    x = x + lin("out", torch.matmul(attn, v.transpose(1, 2)).transpose(1, 2).reshape(b, t, d))
+    h = F.glu(lin("pw1", x, norm=layer.norms["conv"]), dim=-1).transpose(1, 2)
+    h = F.conv1d(h, layer.dw_weight, layer.dw_bias, padding=layer.kernel // 2, groups=d)
+    x = x + lin("pw2", h.transpose(1, 2), input_silu=True)
+    x = x + 0.5 * lin("ff2_down", lin("ff2_up", x, norm=layer.norms["ff2"], silu=True))
+    n = layer.norms["out"]
+    return F.layer_norm(x, (d,), n.weight, n.bias, n.eps)
+
+
+def _dense_forward(enc, mel):
+    x = enc.pre(mel)
+    for layer in enc.layers:
+        x = _dense_layer(layer, x)
+    return x
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("parts,tol", [(3, 2e-4), (1, 5e-2)])
+@torch.inference_mode()
+def test_encoder_matches_dense_fp32_forward(wbits, parts, tol):
+    enc = E.FastConformerEncoder(layers=2, wbits=wbits, parts=parts, seed=wbits, device=DEV, keep_dense=True)
+    g = torch.Generator().manual_seed(3)
+    mel = torch.randn(2, 128, 400, generator=g).to(DEV)
+    y = enc(mel)
+    assert y.shape == (2, 50, 1024) and bool(torch.isfinite(y).all())
+    ref = _dense_forward(enc, mel)
+    rel = ((y - ref).norm() / ref.norm()).item()
+    assert rel < tol, rel
+
+
+@torch.inference_mode()
+def test_clip_gemm_sequence_is_config2():
+    """One 10 s clip: 1000 log-mel frames -> 125 encoder frames; 8 low-bit GEMMs per layer at M = 125 with the
+    BASELINE config-2 shapes, and the large-M batch (config 3: 256 clips) at M = 32000 through the same layers."""
+    enc = E.FastConformerEncoder(layers=1, device=DEV)
+    shapes = enc.gemm_shapes(1, 1000)
+    assert [(n, k) for _, m, n, k in shapes] == [(4096, 1024), (1024, 4096), (3072, 1024), (1024, 1024),
+                                                (2048, 1024), (1024, 1024), (4096, 1024), (1024, 4096)]
+    assert {m for _, m, _, _ in shapes} == {125}
+    assert {m for _, m, _, _ in enc.gemm_shapes(256, 1000)} == {32000}
+    mel = torch.randn(1, 128, 1000, device=DEV)
+    assert enc(mel).shape == (1, 125, 1024)
+
+
+@torch.inference_mode()
+def test_encoder_forward_replays_in_a_cuda_graph():
+    enc = E.FastConformerEncoder(layers=2, device=DEV)
+    mel = torch.randn(1, 128, 1000, device=DEV)
+    first = enc(mel).clone()           # warm-up: one-time set-up and the linear_pos cache outside the capture
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = enc(mel)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, first)
+
+
+@torch.inference_mode()
+def test_joint_greedy_labels():
+    joint = E.TDTJoint(device=DEV)
+    enc = torch.randn(3, 125, 1024, device=DEV)
+    lab = joint.greedy(enc)
+    assert lab.shape == (3, 125) and lab.dtype == torch.int32
+    assert int(lab.min()) >= 0 and int(lab.max()) <= 1024

@@ -197,3 +197,13 @@ def test_ternary_validation_matches_the_reference_errors():
         formats.validate_ternary(torch.tensor([[0b11, 0]], dtype=torch.uint8), torch.ones(1), None, 8)
     with pytest.raises(ValueError, match="positive"):
         formats.validate_ternary(packed, torch.ones(4), None, 0)
+
+
+def test_encoder_layer_shapes_are_the_parakeet_linears():
+    """BASELINE config 2's per-layer GEMMs (QKV, out, two macaron FF pairs, conv pw1 / pw2) plus linear_pos."""
+    from kea_kernels import encoder as E
+    shapes = E.layer_linear_shapes(1024, 4096)
+    assert [shapes[n] for n in E.LAYER_LINEARS] == [(4096, 1024), (1024, 4096), (3072, 1024), (1024, 1024),
+                                                    (2048, 1024), (1024, 1024), (4096, 1024), (1024, 4096)]
+    assert shapes["linear_pos"] == (1024, 1024)
+    assert sum(n * k for n, k in (shapes[x] for x in E.LAYER_LINEARS)) == 24_117_248   # 2.875 MiB of signs per layer
