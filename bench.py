@@ -35,9 +35,9 @@ SAMPLE_MS = (1, 16, 125, 512)           # the CPU sample: every case with M <= 5
 POOL = 4                                 # distinct weight / activation sets per case in the step graphs
 COLD_BYTES = 512 << 20                   # per (wbits, N, K): distinct weights swept by the per-case cold timing
 L2_BYTES = 126 << 20
-# dram__bytes_read.sum + dram__bytes_write.sum of one cold launch, from the ncu captures summarised in
-# profiles/lowbit_gemm_<case>.md (keyed by (wbits, N, K, M)); None for a case without a capture.
-NCU_TRAFFIC = {(2, 4096, 1024, 8192): 9_564_416 + 10_128_384, (1, 4096, 1024, 125): 739_072}
+# dram__bytes_read.sum + dram__bytes_write.sum of one cold launch, from the committed ncu captures of those cases
+# (keyed by (wbits, N, K, M)); None for a case without a capture.
+NCU_TRAFFIC = {(2, 4096, 1024, 8192): 9_577_216 + 16_932_096, (1, 4096, 1024, 125): 738_816}
 
 
 def ops(m, n, k, parts=1):
@@ -176,6 +176,7 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--clip-batch", type=int, default=256, help="clips in the config-3 batch (sharded over ranks)")
+    ap.add_argument("--no-clip", action="store_true", help="skip the clip workloads (shorter profiling runs)")
     ap.add_argument("--case", default=None, metavar="WBITS,N,K,M",
                     help="profiling mode: launch one GEMM case W + K times (rotating cold weights), print its timing")
     args = ap.parse_args()
@@ -304,8 +305,8 @@ def main() -> None:
     # ---- the clip workloads: one 10 s clip (config 2) and a sharded batch of 256 clips (config 3) ----
     del graphs, weights, acts, outs
     torch.cuda.empty_cache()
-    clip = clip_workloads(torch, dev, stream, rank, world, dist if world > 1 else None, local, pdl, hbm_peak,
-                          args.clip_batch)
+    clip = None if args.no_clip else clip_workloads(torch, dev, stream, rank, world, dist if world > 1 else None,
+                                                     local, pdl, hbm_peak, args.clip_batch)
 
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -321,7 +322,7 @@ def main() -> None:
         roofline = {"bound": "tensor", "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
                     "frac": achieved / tensor_peak,
                     "traffic": NCU_TRAFFIC.get((share["wbits"], share["n"], share["k"], share["m"])),
-                    "kernel": f"lowbit_gemm_kernel<{share['wbits']}> M={share['m']} N={share['n']} K={share['k']}",
+                    "kernel": f"lowbit_gemm_pair_kernel<{share['wbits']}> M={share['m']} N={share['n']} K={share['k']}",
                     "peak_kind": int8_kind or f"2 x bf16 ({peak_kind})",
                     "note": "INT8 ops/s; peak = dense INT8 measured with torch._int_mm 8192^3 on this GPU"}
     else:
