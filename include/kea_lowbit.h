@@ -144,7 +144,8 @@ typedef struct KeaQuantizeDesc {
     int64_t xb, xt, xk;       /* strides in elements (see above) */
     int32_t t;                /* rows per batch entry (>= 1) */
     int32_t m, k, parts;
-    int8_t *q;                /* int8 [parts][m][ldq], columns k..ldq-1 written as 0 */
+    int8_t *q;                /* int8 [parts][m][ldq], columns k..ldq-1 written as 0; 4-byte aligned, ldq and the
+                                 part stride multiples of 4 (else KEA_ERR_ALIGNMENT) */
     int64_t q_part_stride;
     int32_t ldq;
     float *qs;                /* FP32 [parts][m] */
@@ -152,10 +153,13 @@ typedef struct KeaQuantizeDesc {
     const float *norm_weight; /* NULL: no LayerNorm */
     const float *norm_bias;
     float eps;
-    int32_t flags;            /* KEA_QUANT_INPUT_SILU */
+    int32_t flags;            /* KEA_QUANT_* */
 } KeaQuantizeDesc;
 
-enum { KEA_QUANT_INPUT_SILU = 1 };
+enum {
+    KEA_QUANT_INPUT_SILU = 1,
+    KEA_QUANT_PDL = 2             /* launch with programmatic dependent launch (overlap with the previous kernel) */
+};
 
 int kea_lowbit_quantize(const KeaQuantizeDesc *desc, void *stream);
 

@@ -88,68 +88,244 @@ struct QuantArgs {
 
 constexpr int kQuantThreads = 256;
 
-KEA_DEVI float block_reduce(float v, bool use_max, float *scratch) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// Sum / max over the `tpr` threads of each row group (tpr = 32, 64, 128 or 256; groups are whole warps), in a fixed
+// order, so every thread of the group gets the same value. Every thread of the CTA must call it.
+KEA_DEVI float group_reduce(float v, bool use_max, int tpr, float *scratch) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float u = __shfl_xor_sync(0xFFFFFFFFu, v, o);
         v = use_max ? fmaxf(v, u) : __fadd_rn(v, u);
     }
-    __syncthreads();  // scratch may still be read by the previous reduction
+    if (tpr == 32) return v;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wpr = tpr >> 5;
+    __syncthreads();   // scratch may still be read by the previous reduction
     if (lane == 0) scratch[warp] = v;
     __syncthreads();
-    float r = scratch[0];
-    for (int w = 1; w < kQuantThreads / 32; ++w) r = use_max ? fmaxf(r, scratch[w]) : __fadd_rn(r, scratch[w]);
+    const int w0 = warp - warp % wpr;
+    float r = scratch[w0];
+    for (int w = 1; w < wpr; ++w) r = use_max ? fmaxf(r, scratch[w0 + w]) : __fadd_rn(r, scratch[w0 + w]);
     return r;
 }
 
-// One CTA per token row; the row lives in shared memory (K floats) while the parts are peeled off.
-__global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantArgs a) {
-    extern __shared__ float xrow[];
+// rint(v / s) with the IEEE round-to-nearest quotient, without a division on the common path. Here |v| <= 127 s
+// (s is the part's amax / 127, or larger), so |v / s| <= 127 + 1e-4, and q = RN(v * RN(1 / s)) differs from v / s
+// by at most 2 * 2^-24 * 127 < 1.6e-5 while the IEEE quotient differs from v / s by at most 7.6e-6: the two round to
+// the same integer unless a half-integer lies within 2.4e-5 of q. Values within 1e-4 of a half-integer (and anything
+// non-finite or out of range) take the exact division.
+KEA_DEVI float round_quotient(float v, float s, float inv) {
+    const float q = __fmul_rn(v, inv);
+    const float f = fabsf(q - truncf(q));
+    if (fabsf(f - 0.5f) > 1.0e-4f && fabsf(q) < 128.0f) return rintf(q);
+    return rintf(__fdiv_rn(v, s));
+}
+
+// The register-resident quantizer for unit-stride rows (xk == 1, K a multiple of 4, 16-byte aligned rows): `tpr`
+// threads per row (32 .. 256, 256 / tpr rows per CTA), each holding VPT = K / tpr (rounded up to 4) values as float4
+// chunks at (c * tpr + thread) * 4, so every load and store is a coalesced 16-byte vector. LayerNorm takes two
+// group reductions (mean, then the centred variance), each part one (amax); nothing goes through shared memory but
+// the reductions' partials. This is the path of every encoder call site; other layouts take quantize_kernel.
+template <int VPT>
+__global__ void __launch_bounds__(kQuantThreads) quantize_regs_kernel(const QuantArgs a, int tpr) {
     __shared__ float scratch[kQuantThreads / 32];
-    const int m = blockIdx.x;
-    const float *x = a.x + (long long)(m / a.t) * a.xb + (long long)(m % a.t) * a.xt;
+    constexpr int C = VPT / 4;
+    const int rows = kQuantThreads / tpr;
+    const int g = threadIdx.x / tpr, gt = threadIdx.x % tpr;
+    const int m = blockIdx.x * rows + g;
+    const bool live = m < a.M;
+    const int K = a.K;
+    float4 v[C];
     grid_dependency_wait();
-    for (int k = threadIdx.x; k < a.K; k += kQuantThreads) xrow[k] = x[(long long)k * a.xk];
-    __syncthreads();
+    const float4 *src = reinterpret_cast<const float4 *>(
+        a.x + (live ? (long long)(m / a.t) * a.xb + (long long)(m % a.t) * a.xt : 0LL));
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int i = c * tpr + gt;
+        v[c] = (live && 4 * i < K) ? __ldg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     if (a.nw) {
-        float s = 0.f;
-        for (int k = threadIdx.x; k < a.K; k += kQuantThreads) s = __fadd_rn(s, xrow[k]);
-        const float mean = __fdiv_rn(block_reduce(s, false, scratch), (float)a.K);
-        float v = 0.f;
-        for (int k = threadIdx.x; k < a.K; k += kQuantThreads) {
-            const float d = __fsub_rn(xrow[k], mean);
-            v = __fmaf_rn(d, d, v);
+        float4 w[C], b[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const int i = c * tpr + gt;
+            const bool in = 4 * i < K;
+            w[c] = in ? __ldg(reinterpret_cast<const float4 *>(a.nw) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            b[c] = (in && a.nb) ? __ldg(reinterpret_cast<const float4 *>(a.nb) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        const float var = __fdiv_rn(block_reduce(v, false, scratch), (float)a.K);
-        const float inv = rsqrtf(__fadd_rn(var, a.eps));
-        for (int k = threadIdx.x; k < a.K; k += kQuantThreads)
-            xrow[k] = __fmaf_rn(__fmul_rn(__fsub_rn(xrow[k], mean), inv), a.nw[k], a.nb ? a.nb[k] : 0.f);
+        float s = 0.f;
+#pragma unroll
+        for (int c = 0; c < C; ++c) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[c].x), v[c].y), v[c].z), v[c].w);
+        const float mean = __fdiv_rn(group_reduce(s, false, tpr, scratch), (float)K);
+        float var = 0.f;
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            if (4 * (c * tpr + gt) < K) {
+                const float d0 = __fsub_rn(v[c].x, mean), d1 = __fsub_rn(v[c].y, mean);
+                const float d2 = __fsub_rn(v[c].z, mean), d3 = __fsub_rn(v[c].w, mean);
+                var = __fmaf_rn(d3, d3, __fmaf_rn(d2, d2, __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, var))));
+            }
+        }
+        const float inv = rsqrtf(__fadd_rn(__fdiv_rn(group_reduce(var, false, tpr, scratch), (float)K), a.eps));
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            v[c].x = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].x, mean), inv), w[c].x, b[c].x);
+            v[c].y = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].y, mean), inv), w[c].y, b[c].y);
+            v[c].z = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].z, mean), inv), w[c].z, b[c].z);
+            v[c].w = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].w, mean), inv), w[c].w, b[c].w);
+        }
     }
     if (a.flags & 1) {
-        for (int k = threadIdx.x; k < a.K; k += kQuantThreads) {
-            const float v = xrow[k];
-            xrow[k] = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            v[c].x = __fdiv_rn(v[c].x, __fadd_rn(1.0f, expf(-v[c].x)));
+            v[c].y = __fdiv_rn(v[c].y, __fadd_rn(1.0f, expf(-v[c].y)));
+            v[c].z = __fdiv_rn(v[c].z, __fadd_rn(1.0f, expf(-v[c].z)));
+            v[c].w = __fdiv_rn(v[c].w, __fadd_rn(1.0f, expf(-v[c].w)));
+        }
+    }
+    for (int p = 0; p < a.parts; ++p) {
+        float amax = 0.f;
+#pragma unroll
+        for (int c = 0; c < C; ++c)
+            if (4 * (c * tpr + gt) < K)
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c].x), fabsf(v[c].y)), fmaxf(fabsf(v[c].z), fabsf(v[c].w))));
+        amax = group_reduce(amax, true, tpr, scratch);
+        const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1.0e-30f);
+        const float rcp = __frcp_rn(scale);
+        if (live) {
+            uint32_t *q = reinterpret_cast<uint32_t *>(a.q + p * a.q_stride + (long long)m * a.ldq);
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+                const int i = c * tpr + gt;
+                if (4 * i < K) {
+                    float *e = reinterpret_cast<float *>(&v[c]);
+                    uint32_t word = 0;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float r = round_quotient(e[j], scale, rcp);
+                        word |= ((uint32_t)(int)r & 0xFFu) << (8 * j);
+                        e[j] = __fsub_rn(e[j], __fmul_rn(r, scale));
+                    }
+                    q[i] = word;
+                }
+            }
+            for (int i = K / 4 + gt; i < a.ldq / 4; i += tpr) q[i] = 0u;   // padding columns
+            if (gt == 0) a.qs[p * a.qs_stride + m] = scale;
+        }
+    }
+    grid_launch_dependents();
+}
+
+// `tpr` threads per token row (a power of two from 32 to 256; 256 / tpr rows per CTA): the host picks fewer threads
+// per row when there are many rows (bandwidth) and more when there are few (latency). The CTA stages its rows in
+// shared memory with loads whose consecutive threads read consecutive addresses: 16-byte vectors along k when the
+// row stride xk is 1, consecutive rows of one column in the [B, K, T] conv layout (xt == 1). Each row group then
+// normalizes (optional LayerNorm, input SiLU) and peels off the parts with group reductions; codes leave as 32-bit
+// words (four per word), the padding columns k .. ldq - 1 as zeros.
+__global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantArgs a, int tpr) {
+    extern __shared__ float xrows[];
+    __shared__ const float *bases[kQuantThreads / 32];
+    __shared__ float scratch[kQuantThreads / 32];
+    const int rows = kQuantThreads / tpr;
+    const int g = threadIdx.x / tpr, gt = threadIdx.x % tpr;    // row group, thread within the group
+    const int m0 = blockIdx.x * rows;
+    const int nrows = min(rows, a.M - m0);
+    const int K = a.K;
+    if (threadIdx.x < nrows) {
+        const int m = m0 + threadIdx.x;
+        bases[threadIdx.x] = a.x + (long long)(m / a.t) * a.xb + (long long)(m % a.t) * a.xt;
+    }
+    grid_dependency_wait();
+    __syncthreads();
+    if (a.xk == 1) {
+        if (g < nrows) {
+            const float *src = bases[g];
+            float *dst = xrows + g * K;
+            if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0 && (K & 3) == 0) {
+                const float4 *s4 = reinterpret_cast<const float4 *>(src);
+                float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll 4
+                for (int i = gt; i < K / 4; i += tpr) d4[i] = __ldg(s4 + i);
+            } else {
+#pragma unroll 4
+                for (int k = gt; k < K; k += tpr) dst[k] = __ldg(src + k);
+            }
+        }
+    } else {
+        const int per = kQuantThreads / nrows;
+        const int r = threadIdx.x % nrows, k0 = threadIdx.x / nrows;
+        if (k0 < per) {
+            const float *src = bases[r];
+            float *dst = xrows + r * K;
+#pragma unroll 4
+            for (int k = k0; k < K; k += per) dst[k] = __ldg(src + (long long)k * a.xk);
+        }
+    }
+    __syncthreads();
+    const bool live = g < nrows;
+    const int m = m0 + g;
+    float *row = xrows + (live ? g : 0) * K;
+    if (a.nw) {
+        float s = 0.f;
+        if (live)
+            for (int k = gt; k < K; k += tpr) s = __fadd_rn(s, row[k]);
+        const float mean = __fdiv_rn(group_reduce(s, false, tpr, scratch), (float)K);
+        float v = 0.f;
+        if (live)
+            for (int k = gt; k < K; k += tpr) {
+                const float d = __fsub_rn(row[k], mean);
+                v = __fmaf_rn(d, d, v);
+            }
+        const float var = __fdiv_rn(group_reduce(v, false, tpr, scratch), (float)K);
+        const float inv = rsqrtf(__fadd_rn(var, a.eps));
+        if (live)
+            for (int k = gt; k < K; k += tpr)
+                row[k] = __fmaf_rn(__fmul_rn(__fsub_rn(row[k], mean), inv), a.nw[k], a.nb ? a.nb[k] : 0.f);
+    }
+    if ((a.flags & 1) && live) {
+        for (int k = gt; k < K; k += tpr) {
+            const float v = row[k];
+            row[k] = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
         }
     }
     __syncthreads();
     for (int p = 0; p < a.parts; ++p) {
         float amax = 0.f;
-        for (int k = threadIdx.x; k < a.K; k += kQuantThreads) amax = fmaxf(amax, fabsf(xrow[k]));
-        amax = block_reduce(amax, true, scratch);
+        if (live)
+            for (int k = gt; k < K; k += tpr) amax = fmaxf(amax, fabsf(row[k]));
+        amax = group_reduce(amax, true, tpr, scratch);
         const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1.0e-30f);
-        int8_t *q = a.q + p * a.q_stride + (long long)m * a.ldq;
-        for (int k = threadIdx.x; k < a.ldq; k += kQuantThreads) {
-            int8_t code = 0;
-            if (k < a.K) {
-                const float v = xrow[k];
-                const float r = rintf(__fdiv_rn(v, scale));
-                code = (int8_t)(int)r;
-                xrow[k] = __fsub_rn(v, __fmul_rn(r, scale));
+        const float inv = __frcp_rn(scale);
+        if (live) {
+            uint32_t *q = reinterpret_cast<uint32_t *>(a.q + p * a.q_stride + (long long)m * a.ldq);
+            const bool vec = (K & 3) == 0;   // whole 16-byte groups of the row: one shared-memory vector each
+            for (int w = gt; w < a.ldq / 4; w += tpr) {   // ldq is a multiple of 4: whole words
+                uint32_t word = 0;
+                if (vec && 4 * w < K) {
+                    float4 v4 = reinterpret_cast<const float4 *>(row)[w];
+                    float *v = reinterpret_cast<float *>(&v4);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float r = round_quotient(v[j], scale, inv);
+                        word |= ((uint32_t)(int)r & 0xFFu) << (8 * j);
+                        v[j] = __fsub_rn(v[j], __fmul_rn(r, scale));
+                    }
+                    reinterpret_cast<float4 *>(row)[w] = v4;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int k = 4 * w + j;
+                        if (k < K) {
+                            const float v = row[k];
+                            const float r = round_quotient(v, scale, inv);
+                            word |= ((uint32_t)(int)r & 0xFFu) << (8 * j);
+                            row[k] = __fsub_rn(v, __fmul_rn(r, scale));
+                        }
+                    }
+                }
+                q[w] = word;
             }
-            q[k] = code;
+            if (gt == 0) a.qs[p * a.qs_stride + m] = scale;
         }
-        if (threadIdx.x == 0) a.qs[p * a.qs_stride + m] = scale;
         __syncthreads();
     }
     grid_launch_dependents();

@@ -234,6 +234,24 @@ int check_config(const KeaGemmConfig &c, int n, int k, int parts, int wbits) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// A launch configuration on `stream` with `dyn` bytes of dynamic shared memory, optionally with programmatic
+// dependent launch (the kernel may start while the previous one finishes; it waits in griddepcontrol.wait).
+cudaLaunchConfig_t launch_config(dim3 grid, size_t dyn, void *stream, cudaLaunchAttribute *attr, int pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kea::kQuantThreads, 1, 1);
+    cfg.dynamicSmemBytes = dyn;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 0;
+    if (pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 1;
+    }
+    return cfg;
+}
+
 // Launches the persistent CTA-pair kernel. KEA_ERR_UNSUPPORTED when an operand's alignment or stride rules it out
 // (the caller then runs the per-tile kernel); other codes are final.
 int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *stream) {
@@ -370,7 +388,11 @@ int kea_lowbit_quantize(const KeaQuantizeDesc *d, void *stream) {
     if (!d || !d->x || !d->q || !d->qs || d->m < 0 || d->k < 1 || d->parts < 1 || d->parts > 3 || d->t < 1 ||
         d->ldq < d->k)
         return KEA_ERR_INVALID_VALUE;
+    if (d->flags & ~(KEA_QUANT_INPUT_SILU | KEA_QUANT_PDL)) return KEA_ERR_INVALID_VALUE;
     if ((long long)d->k * 4 > 64 * 1024) return KEA_ERR_UNSUPPORTED;
+    // codes are written as 32-bit words
+    if ((reinterpret_cast<uintptr_t>(d->q) & 3u) || d->ldq % 4 || (d->parts > 1 && d->q_part_stride % 4))
+        return KEA_ERR_ALIGNMENT;
     if (d->m == 0) return KEA_OK;
     int dev = 0;
     const int st = device_setup(&dev);
@@ -392,9 +414,38 @@ int kea_lowbit_quantize(const KeaQuantizeDesc *d, void *stream) {
     a.nw = d->norm_weight;
     a.nb = d->norm_bias;
     a.eps = d->eps;
-    a.flags = d->flags;
-    kea::quantize_kernel<<<d->m, kea::kQuantThreads, d->k * sizeof(float), (cudaStream_t)stream>>>(a);
-    return cudaGetLastError() == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
+    a.flags = d->flags & KEA_QUANT_INPUT_SILU;
+    // Threads per row: enough CTAs to give every SM two (few rows: up to 256 threads on a row, for latency), as few
+    // as one warp per row when rows are many.
+    int tpr = 32;
+    while (tpr < kea::kQuantThreads && (long long)ceil_div(d->m, kea::kQuantThreads / tpr) < 2LL * g_devices[dev].sms) tpr *= 2;
+    cudaLaunchAttribute attr[1];
+    const bool unit_rows = d->xk == 1 && d->k % 4 == 0 && (reinterpret_cast<uintptr_t>(d->x) & 15u) == 0 &&
+                           d->xt % 4 == 0 && (d->t == 1 || d->xb % 4 == 0) && d->k <= 32 * kea::kQuantThreads &&
+                           (!d->norm_weight || (reinterpret_cast<uintptr_t>(d->norm_weight) & 15u) == 0) &&
+                           (!d->norm_bias || (reinterpret_cast<uintptr_t>(d->norm_bias) & 15u) == 0);
+    if (unit_rows) {
+        // registers: at most 32 values a thread
+        while (tpr < kea::kQuantThreads && d->k > 32 * tpr) tpr *= 2;
+        const int vpt = round_up(ceil_div(d->k, tpr), 4);
+        const dim3 grid((unsigned)ceil_div(d->m, kea::kQuantThreads / tpr));
+        cudaLaunchConfig_t cfg = launch_config(grid, 0, stream, attr, d->flags & KEA_QUANT_PDL);
+        cudaError_t e;
+        if (vpt <= 4) e = cudaLaunchKernelEx(&cfg, kea::quantize_regs_kernel<4>, a, tpr);
+        else if (vpt <= 8) e = cudaLaunchKernelEx(&cfg, kea::quantize_regs_kernel<8>, a, tpr);
+        else if (vpt <= 16) e = cudaLaunchKernelEx(&cfg, kea::quantize_regs_kernel<16>, a, tpr);
+        else e = cudaLaunchKernelEx(&cfg, kea::quantize_regs_kernel<32>, a, tpr);
+        if (e != cudaSuccess) cudaGetLastError();
+        return e == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
+    }
+    // shared-memory staging for other layouts; the CTA's rows must fit 64 KB
+    while (tpr < kea::kQuantThreads && (kea::kQuantThreads / tpr) * d->k * (int)sizeof(float) > 64 * 1024) tpr *= 2;
+    const int rows = kea::kQuantThreads / tpr;
+    cudaLaunchConfig_t cfg = launch_config(dim3((unsigned)ceil_div(d->m, rows)), (size_t)rows * d->k * sizeof(float),
+                                           stream, attr, d->flags & KEA_QUANT_PDL);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kea::quantize_kernel, a, tpr);
+    if (e != cudaSuccess) cudaGetLastError();
+    return e == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
 }
 
 int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {

@@ -18,7 +18,7 @@ LIB_PATH = Path(os.environ.get("KEA_LOWBIT_LIB", Path(__file__).resolve().parent
 OK, INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES, CUDA, NO_DEVICE, DEVICE_TIMEOUT, CAPTURE = range(9)
 OUT_F32, OUT_F16 = 0, 1
 FLAG_SILU, FLAG_ORDER1, FLAG_PDL, FLAG_NO_PAIR = 1, 2, 4, 8
-QUANT_INPUT_SILU = 1
+QUANT_INPUT_SILU, QUANT_PDL = 1, 2
 DEVERR_TIMEOUT, DEVERR_TAIL_BITS, DEVERR_TERNARY_11 = 1, 2, 4
 
 # Every symbol include/kea_lowbit.h declares.

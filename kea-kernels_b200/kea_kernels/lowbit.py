@@ -48,9 +48,10 @@ def prepare_panels(codes: Tensor, wbits: int, n: int, k: int) -> Tensor:
 
 
 def quantize(x: Tensor, rows: tuple[int, int, int, int], m: int, k: int, parts: int, *, ldq: int | None = None,
-             norm=None, input_silu: bool = False) -> tuple[Tensor, Tensor, int]:
+             norm=None, input_silu: bool = False, pdl: bool = False) -> tuple[Tensor, Tensor, int]:
     """x[m', kk] at x + (m' // T) * XB + (m' % T) * XT + kk * XK for rows = (XB, XT, XK, T) ->
-    (q int8 [parts, m, ldq] zero-padded past k, qs FP32 [parts, m], ldq)."""
+    (q int8 [parts, m, ldq] zero-padded past k, qs FP32 [parts, m], ldq). pdl lets the kernel start while the
+    previous kernel on the stream finishes (it waits for that kernel's results before reading x)."""
     _require_cuda(x, "x")
     if x.dtype != torch.float32:
         raise ValueError(f"expected FP32 input, got {x.dtype}")
@@ -69,7 +70,7 @@ def quantize(x: Tensor, rows: tuple[int, int, int, int], m: int, k: int, parts: 
         d.norm_weight = norm.weight.data_ptr()
         d.norm_bias = None if norm.bias is None else norm.bias.data_ptr()
         d.eps = float(norm.eps)
-    d.flags = _lib.QUANT_INPUT_SILU if input_silu else 0
+    d.flags = (_lib.QUANT_INPUT_SILU if input_silu else 0) | (_lib.QUANT_PDL if pdl else 0)
     with torch.cuda.device(x.device):
         _lib.check(_lib.lib().kea_lowbit_quantize(ctypes.byref(d), _lib.stream_handle(x.device)), "quantize")
     return q, qs, ldq

@@ -304,7 +304,7 @@ def test_pdl_launch_chain_matches():
 
 # ---- the quantizer ---------------------------------------------------------------------------------------------
 
-@pytest.mark.parametrize("m,k", [(125, 1024), (38, 4096), (7, 300), (1, 21)])
+@pytest.mark.parametrize("m,k", [(125, 1024), (38, 4096), (7, 300), (1, 21), (3000, 1024), (1500, 4096), (999, 300)])
 @pytest.mark.parametrize("parts", [1, 2, 3])
 def test_quantizer_equals_oracle_bitwise(m, k, parts):
     g = torch.Generator().manual_seed(m + k)
@@ -317,12 +317,33 @@ def test_quantizer_equals_oracle_bitwise(m, k, parts):
     assert np.array_equal(qs.cpu().numpy().view(np.uint32), want_qs.view(np.uint32))
 
 
-def test_quantizer_strided_conv_input():
+@pytest.mark.parametrize("m", [3, 700])
+def test_quantizer_half_integer_quotients_are_exact(m):
+    """Values whose quotient by the row scale lies within a few ulps of a half-integer: rint of the IEEE quotient
+    must come out bit for bit (the kernel divides exactly only where a reciprocal product could round differently)."""
+    g = torch.Generator().manual_seed(m)
+    k = 1024
+    amax = (torch.rand(m, 1, generator=g) * 3 + 0.1)
+    s = (amax / 127).float()
+    j = torch.randint(-126, 126, (m, k), generator=g).float() + 0.5
+    x = (j * s).float()
+    ulps = torch.randint(-4, 5, (m, k), generator=g).to(torch.int32)
+    x = (x.view(torch.int32) + ulps).view(torch.float32)          # a few ulps either side of (j + 1/2) s
+    x[:, 0] = amax[:, 0]
+    q, qs, ldq = lowbit.quantize(x.to(DEV), (0, x.stride(0), x.stride(1), m), m, k, 2)
+    torch.cuda.synchronize()
+    want_q, want_qs = oracle.quantize(x.numpy(), 2, ldq)
+    assert np.array_equal(qs.cpu().numpy().view(np.uint32), want_qs.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy(), want_q)
+
+
+@pytest.mark.parametrize("b,k,t", [(2, 300, 19), (16, 1024, 125)])
+def test_quantizer_strided_conv_input(b, k, t):
     g = torch.Generator().manual_seed(4)
-    x = torch.randn(2, 300, 19, generator=g)          # [B, K, T]: the conv layout, read through strides
+    x = torch.randn(b, k, t, generator=g)             # [B, K, T]: the conv layout, read through strides
     xd = x.to(DEV)
-    q, qs, ldq = lowbit.quantize(xd, (xd.stride(0), xd.stride(2), xd.stride(1), 19), 38, 300, 3)
-    want_q, want_qs = oracle.quantize(x.transpose(1, 2).reshape(38, 300).numpy(), 3, ldq)
+    q, qs, ldq = lowbit.quantize(xd, (xd.stride(0), xd.stride(2), xd.stride(1), t), b * t, k, 3)
+    want_q, want_qs = oracle.quantize(x.transpose(1, 2).reshape(b * t, k).numpy(), 3, ldq)
     assert np.array_equal(q.cpu().numpy(), want_q) and np.array_equal(qs.cpu().numpy(), want_qs)
 
 
