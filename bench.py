@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -146,6 +147,34 @@ def cpu_sample(threads: int, min_seconds: float = 10.0, max_seconds: float = 30.
         if repeats is None and (elapsed >= min_seconds or elapsed + elapsed / passes > max_seconds):
             break
     return total_ops * passes / elapsed / 1e12, elapsed, passes, total_ops
+
+
+def cpu_clip_sample(layers: int = 2) -> dict:
+    """The clip's low-bit GEMM chain on the host cores through the reference's CPU algorithm (oracle port: unpack,
+    exact integer GEMM, FP32 epilogue) for `layers` of the 24 layers (8 GEMMs each at M = 125), scaled to 24."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+    import kea_oracle as oracle
+
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(1)
+    shapes = [(4096, 1024), (1024, 4096), (3072, 1024), (1024, 1024), (2048, 1024), (1024, 1024), (4096, 1024),
+              (1024, 4096)]
+    work = []
+    for n, k in shapes * layers:
+        codes = oracle.pack_signs(rng.choice(np.array([-1, 1], dtype=np.int8), size=(n, k)))
+        q = rng.integers(-127, 128, size=(1, 125, k), dtype=np.int8)
+        qs = rng.uniform(0.005, 0.02, size=(1, 125)).astype(np.float32)
+        alpha = rng.uniform(0.01, 0.05, size=n).astype(np.float32)
+        work.append((codes, n, k, q, qs, alpha))
+    t0 = time.perf_counter()
+    for codes, n, k, q, qs, alpha in work:
+        w, status = oracle.unpack_c(codes, 1, n, k)
+        oracle.gemm(q, qs, w, alpha, threads=threads)
+    seconds = time.perf_counter() - t0
+    return {"ms_per_clip": seconds * 1e3 * 24 / layers, "cores": threads, "kind": "port",
+            "sample": f"{layers} of 24 layers ({8 * layers} GEMMs at M = 125, unpack + exact integer GEMM + FP32 "
+                      f"epilogue, oracle/kea_oracle.c), {seconds:.2f} s, scaled by 24 / {layers}"}
 
 
 def reference_arm(args) -> None:
@@ -294,9 +323,11 @@ def main() -> None:
         # ---- per-case device timing (cold: distinct weights sweep >= 4 x L2; rank 0 reports) ----
         per_case = []
         int8_peak, int8_kind = None, None
+        ref_table = None
         if rank == 0:
             per_case = time_cases(torch, lowbit, _lib, configs, dev, stream, random_panels, alphas, pdl)
             int8_peak, int8_kind = int8_peak_tops(torch, dev)
+            ref_table = reference_table(torch, lowbit, _lib, dev, stream, random_panels, pdl)
     clocks = sampler.summary()
 
     # ---- e2e through the C-ABI call with host buffers ----
@@ -356,7 +387,8 @@ def main() -> None:
                        "parallelism": f"replicas x{world}", "pdl": pdl},
             "roofline": roofline, "roofline_small_m": roofline_small, "cpu_baseline": cpu, "e2e": e2e,
             "clocks": clocks, "gpu_launches": len(CASES) * args.steps, "cases": per_case,
-            "int8_peak_tops": int8_peak, "int8_peak_kind": int8_kind, "clip": clip}
+            "int8_peak_tops": int8_peak, "int8_peak_kind": int8_kind, "reference_x3_table": ref_table,
+            "clip": clip}
     print(json.dumps(line), flush=True)
 
 
@@ -438,6 +470,8 @@ def clip_workloads(torch, dev, stream, rank, world, dist, local, pdl, hbm_peak, 
         "l2": "flushed (256 MB written) before every timed replay; hot = back-to-back replays"}
     del g, gl
     torch.cuda.empty_cache()
+    if world == 1:
+        out["config2"]["cpu_baseline"] = cpu_clip_sample()
 
     # ---- config 3: the batch, sharded ----
     n_clips = batch_clips
@@ -477,6 +511,59 @@ def clip_workloads(torch, dev, stream, rank, world, dist, local, pdl, hbm_peak, 
         "lowbit_gop": gop, "encoder_lowbit_tops": gop / t / 1e3,
         "labels_gathered": len(res.tokens), "timing": "CUDA events on each rank's stream, max over ranks"}
     return out
+
+
+# The reference's own per-GEMM times (RTX 5090, b1_dot with three residual INT8 parts, FP32 output, hot / cold):
+# the TUNED_M table comments of src/kea_kernels/binary/configs.py:17-36, keyed by (N, K, M).
+REFERENCE_X3_US = {
+    (1024, 1024, 38): (2.88, 2.92), (1024, 1024, 126): (3.53, 3.55), (1024, 1024, 256): (4.93, 5.01),
+    (1024, 1024, 368): (6.13, 6.34), (1024, 4096, 38): (5.14, 5.23), (1024, 4096, 126): (9.09, 9.20),
+    (1024, 4096, 256): (15.21, 15.45), (1024, 4096, 368): (20.84, 21.17), (2048, 1024, 38): (3.52, None),
+    (2048, 1024, 126): (4.90, None), (2048, 1024, 256): (7.58, None), (2048, 1024, 368): (10.42, None),
+    (3072, 1024, 38): (3.53, None), (3072, 1024, 126): (6.33, None), (3072, 1024, 256): (10.52, None),
+    (3072, 1024, 368): (13.31, None), (4096, 1024, 38): (4.31, 4.36), (4096, 1024, 126): (7.52, 7.63),
+    (4096, 1024, 256): (13.09, 13.30), (4096, 1024, 368): (19.24, 19.53)}
+
+
+def reference_table(torch, lowbit, _lib, dev, stream, random_panels, pdl):
+    """The reference's published b1_dot x3 shapes on this GPU: 1-bit weights, three INT8 parts, FP32 output, timed
+    hot (one weight set, as the reference's "hot") and cold (a graph of launches over >= 4 x L2 of weight sets)."""
+    rows = []
+    pools = {}
+    for (n, k, m), (ref_hot, ref_cold) in REFERENCE_X3_US.items():
+        if (n, k) not in pools:
+            pools[(n, k)] = random_panels(1, n, k, max(1, min(1024, COLD_BYTES // _lib.panel_bytes(1, n, k))))
+        pool = pools[(n, k)]
+        alpha = torch.rand(n, device=dev) * 0.02 + 0.001
+        q = torch.randint(-127, 128, (3, m, k), dtype=torch.int8, device=dev)
+        qs = torch.rand(3, m, device=dev) * 0.01 + 0.001
+        y = torch.empty(m, n, device=dev, dtype=torch.float32)
+        launches = min(len(pool), 256)
+
+        def timed(hot):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(g, stream=stream):
+                    for i in range(launches):
+                        lowbit.gemm(q, qs, k, m, pool[0 if hot else i % len(pool)], 1, n, k, alpha, None, y, parts=3,
+                                    pdl=pdl)
+                g.replay()
+                stream.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+                stream.synchronize()
+            return e0.elapsed_time(e1) * 1e3 / launches
+
+        hot, cold = timed(True), timed(False)
+        rows.append({"n": n, "k": k, "m": m, "ref_us_hot": ref_hot, "ref_us_cold": ref_cold, "us_hot": hot,
+                     "us_cold": cold, "speedup_hot": ref_hot / hot})
+    del pools
+    geo = math.exp(sum(math.log(r["speedup_hot"]) for r in rows) / len(rows))
+    return {"what": "the reference's published b1_dot x3 times (RTX 5090, src/kea_kernels/binary/configs.py:17-36) "
+                    "against this GPU on the same arithmetic (1-bit, 3 INT8 parts, FP32 out)",
+            "geomean_speedup_hot": geo, "rows": rows}
 
 
 def time_cases(torch, lowbit, _lib, configs, dev, stream, random_panels, alphas, pdl):
