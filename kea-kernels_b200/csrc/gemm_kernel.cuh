@@ -98,6 +98,10 @@ struct GemmArgs {
                                  // K = 32 step, summed in the epilogue) so back-to-back MMAs do not wait on each other
     uint32_t a_stride;           // distance between consecutive stages' activation tiles (one-shot boxes are dense:
                                  // rows * 128 bytes; the MMA's reads past a short tile only reach unstored rows)
+    int stack;                   // 1: the P parts are stacked along the rows of one 128-row tile (part p's tokens at
+                                 // rows p * mp ..), so one accumulator and one MMA per K step serve every part;
+                                 // qmap is then (k, row, part, k-block) with boxes of mp rows x P parts
+    int mp;                      // stacked rows per part: M rounded up to the 8-row swizzle atom
     uint32_t *err;
 };
 
@@ -357,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
         // lines at once (INT32 accumulation makes the order free).
         const int rot = nkb > 0 ? (int)(blockIdx.x % (unsigned)nkb) : 0;
         const int pk_copies = R == kPanelN ? ptiles : WBITS * 4;
-        const int act_copies = a.q4d ? P : TMB * P;
+        const int act_copies = a.q4d ? (a.stack ? 1 : P) : TMB * P;
         const int ncopies = pk_copies + act_copies;   // <= 14
         int issued = 0;
         if (a.oneshot) {
@@ -368,7 +372,10 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                 mbar_arrive_expect_tx(full, (uint32_t)a.kbox * tx_bytes);
                 const int plane0 = ((n0 / kPanelN) * a.kb_total + kb0) * WBITS * 4;
                 tma_load_2d(PK0, &wmap, full, (n0 % kPanelN) * 4, plane0);
-                tma_load_4d(A0, &qmap, full, 0, t0, kb0, 0);
+                if (a.stack)
+                    tma_load_4d(A0, &qmap, full, 0, t0, 0, kb0);
+                else
+                    tma_load_4d(A0, &qmap, full, 0, t0, kb0, 0);
             }
             __syncwarp();
             issued = nkb;
@@ -399,6 +406,8 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                     else                     // R rows of one word plane
                         bulk_load(spk + c * R * 4, wsrc + (size_t)kb * kblock_bytes + (size_t)c * kPanelN * 4,
                                   (uint32_t)(R * 4), full);
+                } else if (a.stack) {        // one box: mp rows of every part
+                    tma_load_4d(sa, &qmap, full, 0, t0, 0, kb);
                 } else if (a.q4d) {          // one box of 128 * TMB rows per part
                     const int p = c - pk_copies;
                     tma_load_4d(sa + p * TMB * kActTileBytes, &qmap, full, 0, t0, kb, p);
@@ -439,7 +448,10 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                 for (int i = 0; i < nkb; ++i) {
                     const uint64_t ad_s = a_desc0 + (uint64_t)((i * a.a_stride) >> 4);
                     const uint64_t bd_s = b_desc0 + (uint64_t)((i * a.b_stage) >> 4);
-                    issue_stage<P, 1, 4>(tmem, ad_s, bd_s, idesc, TN, i == 0);
+                    if (a.stack)
+                        issue_stage<1, 1, 4>(tmem, ad_s, bd_s, idesc, TN, i == 0);
+                    else
+                        issue_stage<P, 1, 4>(tmem, ad_s, bd_s, idesc, TN, i == 0);
                 }
             }
             __syncwarp();
@@ -465,7 +477,11 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
             const uint64_t ad_s = a_desc0 + (uint64_t)((s * a.a_stride) >> 4);
             const uint64_t bd_s = b_desc0 + (uint64_t)((s * a.b_stage) >> 4);
             if (elect_one()) {
-                if (TMB == 2)
+                if (a.stack && a.nacc > 1)
+                    issue_stage<1, 1, 4>(tmem, ad_s, bd_s, idesc, TN, i == 0);
+                else if (a.stack)
+                    issue_stage<1, 1, 1>(tmem, ad_s, bd_s, idesc, TN, i == 0);
+                else if (TMB == 2)
                     issue_stage<P, 2, 1>(tmem, ad_s, bd_s, idesc, TN, i == 0);
                 else if (a.nacc > 1)
                     issue_stage<P, 1, 4>(tmem, ad_s, bd_s, idesc, TN, i == 0);
@@ -561,7 +577,45 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
         if (!done && ok && lane == 0) report(a.err, 1u);
         KEA_TRACE_POINT(threadIdx.x == 64, 9);
         tc_fence_after();
-        if (a.splits == 1 && a.tma_store) {
+        if (a.stack && a.splits == 1) {
+            // Stacked parts: part p of token t sits in TMEM lane p * mp + t, so the lanes of one token live in
+            // different warps. Every row goes to shared memory (the stage area, dead now: all MMAs completed),
+            // then each (token, 4-channel group) combines its parts: comb_P, alpha / bias, SiLU, store.
+            const uint32_t xs = base;
+            const int ld = TN + 4;   // int32 row stride: 16 bytes of padding keep a warp's row stores bank-spread
+            if (done) {
+                for (int ch = sub; ch < chunks; ch += 4) {
+                    uint32_t v[16];
+                    load_acc16(lane_addr, 0, a.nacc, TN, ch * 16, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        st_shared_v4(xs + (uint32_t)((row * ld + ch * 16 + 4 * q) * 4), v[4 * q], v[4 * q + 1],
+                                     v[4 * q + 2], v[4 * q + 3]);
+                }
+            }
+            named_barrier_sync(3, kEpiThreads);
+            if (done) {
+                const int e = threadIdx.x - 64, g_log2 = tn_log2 - 2;   // TN / 4 groups (a power of two)
+                for (int i = e; i < (a.mp << g_log2); i += kEpiThreads) {
+                    const int tl = i >> g_log2, g = i & ((1 << g_log2) - 1);
+                    const int t = t0 + tl;
+                    if (t >= a.M || n0 + 4 * g >= a.N) continue;
+                    int accv[P][4];
+                    float sc[P];
+#pragma unroll
+                    for (int p = 0; p < P; ++p) {
+                        const uint4 u = ld_shared_v4(xs + (uint32_t)(((p * a.mp + tl) * ld + 4 * g) * 4));
+                        accv[p][0] = (int)u.x;
+                        accv[p][1] = (int)u.y;
+                        accv[p][2] = (int)u.z;
+                        accv[p][3] = (int)u.w;
+                        sc[p] = s_qs[p * TMB * kBM + tl];
+                    }
+                    finish_store<P, 4>(a, t, n0 + 4 * g, 4 * g, accv, sc, s_alpha, s_bias);
+                }
+            }
+        } else if (a.splits == 1 && a.tma_store) {
             // Each warp stages its 32 token rows x W = TN / 4 channels of y (64 or 128 bytes a row, swizzled like the
             // store's tensor map) in the free stage area, then one lane stores the box with TMA: a few bulk stores
             // instead of thousands of scattered 16-byte ones.
@@ -659,13 +713,14 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
             const int per = (groups + a.splits - 1) / a.splits;
             // owner = g / per by a reciprocal (exact for g < 1024, per <= 64): no division per group
             const uint32_t inv_per = (65536u + (uint32_t)per - 1u) / (uint32_t)per;
-            const int blocks = TMB * P;
+            const int blocks = a.stack ? 1 : TMB * P;
             if (a.recv_aliases_stages) {   // peers may still be in their main loops: wait until every CTA is done
                 cluster_arrive();
                 cluster_wait();
             }
             for (int blk = 0; blk < blocks; ++blk) {
-                const bool live = t0 + (blk / P) * kBM + row < a.M;   // rows past M are never read by the owner
+                // rows past M (or past the stacked parts) are never read by the owner
+                const bool live = a.stack ? (row < P * a.mp && t0 + row % a.mp < a.M) : t0 + (blk / P) * kBM + row < a.M;
                 for (int ch = sub; ch < chunks; ch += 4) {
                     uint32_t v[16];
                     if (done) {
@@ -698,7 +753,46 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
     if (a.splits > 1) {
         cluster_sync_all();  // every partial has landed in its owner's shared memory
         KEA_TRACE_POINT(threadIdx.x == 64, 11);
-        if (warp >= 2) {
+        if (warp >= 2 && a.stack) {
+            // Stacked parts: sum the splits per stacked row into the first source slot, then combine each token's
+            // parts (rows p * mp + t) for this rank's channel groups.
+            const int groups = TN / 4;
+            const int per = (groups + a.splits - 1) / a.splits;
+            const int g_lo = rank * per, g_hi = min(groups, g_lo + per);
+            if (row < P * a.mp) {
+                for (int g = g_lo + sub; g < g_hi; g += 4) {
+                    int4 sum = make_int4(0, 0, 0, 0);
+                    for (int src = 0; src < a.splits; ++src) {
+                        const uint4 u = ld_shared_v4(recv + (uint32_t)(((src * per + (g - g_lo)) * kBM + row) * 16));
+                        sum.x += (int)u.x;
+                        sum.y += (int)u.y;
+                        sum.z += (int)u.z;
+                        sum.w += (int)u.w;
+                    }
+                    st_shared_v4(recv + (uint32_t)(((g - g_lo) * kBM + row) * 16), (uint32_t)sum.x, (uint32_t)sum.y,
+                                 (uint32_t)sum.z, (uint32_t)sum.w);
+                }
+            }
+            named_barrier_sync(3, kEpiThreads);
+            const int e = threadIdx.x - 64, own = g_hi - g_lo;
+            for (int i = e; i < a.mp * own; i += kEpiThreads) {
+                const int tl = i / own, gl = i - tl * own;
+                const int t = t0 + tl, g = g_lo + gl;
+                if (t >= a.M || n0 + 4 * g >= a.N) continue;
+                int accv[P][4];
+                float sc[P];
+#pragma unroll
+                for (int p = 0; p < P; ++p) {
+                    const uint4 u = ld_shared_v4(recv + (uint32_t)((gl * kBM + p * a.mp + tl) * 16));
+                    accv[p][0] = (int)u.x;
+                    accv[p][1] = (int)u.y;
+                    accv[p][2] = (int)u.z;
+                    accv[p][3] = (int)u.w;
+                    sc[p] = s_qs[p * TMB * kBM + tl];
+                }
+                finish_store<P, 4>(a, t, n0 + 4 * g, 4 * g, accv, sc, s_alpha, s_bias);
+            }
+        } else if (warp >= 2) {
             const int groups = TN / 4;
             const int per = (groups + a.splits - 1) / a.splits;
             const int blocks = TMB * P;

@@ -167,13 +167,23 @@ bool pair_shape(int m, int n, int k, int parts) {
 
 // The M-bucketed split-K dispatch table (B200, 148 SMs).
 //  * M <= 128 (one token block): narrow channel tiles, so the grid covers the SMs with little or no split-K
-//    (each CTA then reads the whole K of its channels and needs no partial exchange); split K only while the
-//    tile grid is below the SM count.
+//    (each CTA then reads the whole K of its channels and needs no partial exchange); split K only as far as the
+//    one-shot mode needs (<= 8 k-blocks per CTA) and while the tile grid is below the SM count.
 //  * 128 < M <= 512: 128-channel tiles, 256 tokens per CTA when one part (the weight expansion serves both
 //    token blocks), split K up to the SM count.
 //  * larger M: 256 tokens x 256 channels per CTA when the tile count allows (fewest operand bytes per MMA).
-KeaGemmConfig choose_tile(int m, int n, int k, int wbits, int parts, int sms) {
+// Stacked parts: with P > 1 and P x (M rounded up to 8) <= 128 the parts share one 128-row token tile (part p's
+// tokens at rows p * mp ..), so the MMAs, tensor memory and shared memory are those of one part. Needs the 4-D
+// activation view (K a multiple of 128).
+int stack_rows(int m, int parts, int k) { return round_up(std::max(m, 1), 8); }
+bool stackable(int m, int parts, int k) {
+    return parts > 1 && k % kea::kBK == 0 && m <= kea::kBM && parts * stack_rows(m, parts, k) <= kea::kBM;
+}
+
+KeaGemmConfig choose_tile(int m, int n, int k, int wbits, int parts_in, int sms, bool allow_stack = true) {
     KeaGemmConfig c{};
+    // the tile's footprint: stacked parts act as one
+    const int parts = allow_stack && stackable(m, parts_in, k) ? 1 : parts_in;
     const int kb = ceil_div(k, kea::kBK), nt128 = ceil_div(n, kea::kPanelN);
     int tile_m, tile_n;
     if (m <= kea::kBM) {
@@ -192,6 +202,10 @@ KeaGemmConfig choose_tile(int m, int n, int k, int wbits, int parts, int sms) {
     const int tiles = ceil_div(std::max(m, 1), tile_m) * ceil_div(n, tile_n);
     int splits = 1;
     if (tiles < sms) splits = std::max(1, sms / tiles);
+    // One token block: split K only as far as needed for each CTA's K range to arrive in one shot (<= 8 k-blocks);
+    // more splits fill more SMs, but the partial exchange costs more than the idle SMs (measured: K = 1024 runs
+    // fastest unsplit on 32-64 CTAs, K = 4096 with 4 splits).
+    if (m <= kea::kBM) splits = std::min(splits, ceil_div(kb, 8));
     splits = std::min({splits, kb, kMaxPortableCluster});
     while (splits > 1 && exchange_bytes(tile_m, tile_n, parts, splits) + 1024 > kMaxDynSmem) --splits;
     const int per = ceil_div(kb, splits);
@@ -220,6 +234,7 @@ KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
 }
 
 int check_config(const KeaGemmConfig &c, int n, int k, int parts, int wbits) {
+    // parts here is the tile footprint: 1 for stacked parts
     const int kb = ceil_div(k, kea::kBK), nt = ceil_div(n, kea::kPanelN);
     if (c.tile_m != 128 && c.tile_m != 256) return KEA_ERR_UNSUPPORTED;
     if (!valid_tile_n(c.tile_n)) return KEA_ERR_UNSUPPORTED;
@@ -472,19 +487,30 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
         if (ps != KEA_ERR_UNSUPPORTED) return ps;
     }
     if (c.pair) c = choose_tile(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms);
+    // Stacked parts (one 128-row tile holds every part's tokens): pe is the parts the tile's footprint counts.
+    int pe = stackable(d->m, d->parts, d->k) ? 1 : d->parts;
     if (forced) {
         if (d->tile_m) c.tile_m = d->tile_m;
         if (d->tile_n) c.tile_n = d->tile_n;
         if (d->splits) c.splits = d->splits;
+        if (c.tile_m != kea::kBM) pe = d->parts;
         if (d->stages) {
             c.stages = d->stages;
         } else {
             const int per = ceil_div(ceil_div(d->k, kea::kBK), std::max(1, c.splits));
-            c.stages = std::max(1, std::min(per, max_stages(c.tile_m, c.tile_n, d->parts, d->wbits)));
+            c.stages = std::max(1, std::min(per, max_stages(c.tile_m, c.tile_n, pe, d->wbits)));
         }
-        c.smem_bytes = dyn_smem_bytes(c.tile_m, c.tile_n, d->parts, d->wbits, c.splits, c.stages);
+        c.smem_bytes = dyn_smem_bytes(c.tile_m, c.tile_n, pe, d->wbits, c.splits, c.stages);
     }
-    const int cs = check_config(c, d->n, d->k, d->parts, d->wbits);
+    // the single-tile stacked epilogue stages every TMEM row (TN + 4 words) in the stage area
+    const bool stack = pe == 1 && d->parts > 1 && c.tile_m == kea::kBM &&
+                       (c.splits > 1 || kea::kBM * (c.tile_n + 4) * 4 <= c.stages * stage_bytes(c.tile_m, c.tile_n, 1, d->wbits));
+    if (!stack && pe == 1 && d->parts > 1) {   // footprint sized for stacking that cannot be used: size for the parts
+        pe = d->parts;
+        if (!forced) c = choose_tile(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms, false);
+        else c.smem_bytes = dyn_smem_bytes(c.tile_m, c.tile_n, pe, d->wbits, c.splits, c.stages);
+    }
+    const int cs = check_config(c, d->n, d->k, pe, d->wbits);
     if (cs != KEA_OK) return cs;
 
     // Activations. When K is a multiple of 128: a 4-D view (k within a 128-block, row, k-block, part) whose boxes are
@@ -498,7 +524,7 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     const int R = std::min(c.tile_n, kea::kPanelN);
     // One-shot: the CTA's whole K range fits in the stages and arrives in two TMA boxes (one token block, one
     // part, narrow channel tile so the panel box is at most 256 bytes wide).
-    const bool oneshot = q4d && tmb * d->parts == 1 && c.tile_n <= 64 && nkb_max <= c.stages && nkb_max <= 8;
+    const bool oneshot = q4d && tmb * pe == 1 && c.tile_n <= 64 && nkb_max <= c.stages && nkb_max <= 8;
     const int kbox = oneshot ? nkb_max : 1;
     CUtensorMap qmap;
     const long long pstride = d->parts > 1 ? d->q_part_stride : (long long)d->m * d->ldq;
@@ -507,7 +533,19 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     const int box_rows4 = std::min(kea::kBM * tmb, round_up(d->m, 8));
     const int box_rows3 = std::min(kea::kBM, round_up(d->m, 8));
     uint32_t act_tx;
-    if (q4d) {
+    if (q4d && stack) {
+        // (k in block, row, part, k-block): one box = box_rows4 rows of every part for kbox k-blocks, landing as
+        // [k-block][part][row][128 bytes], i.e. the parts stacked along the tile's rows
+        act_tx = (uint32_t)(d->parts * box_rows4 * kea::kBK);
+        const cuuint64_t dims[4] = {(cuuint64_t)kea::kBK, (cuuint64_t)d->m, (cuuint64_t)d->parts, (cuuint64_t)kb_total};
+        const cuuint64_t strides[3] = {(cuuint64_t)d->ldq, (cuuint64_t)std::max<long long>(pstride, 16), (cuuint64_t)kea::kBK};
+        const cuuint32_t box[4] = {(cuuint32_t)kea::kBK, (cuuint32_t)box_rows4, (cuuint32_t)d->parts, (cuuint32_t)kbox};
+        const cuuint32_t estr[4] = {1, 1, 1, 1};
+        if (g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t *>(d->q), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return KEA_ERR_CUDA;
+    } else if (q4d) {
         act_tx = (uint32_t)(d->parts * box_rows4 * kea::kBK);
         const cuuint64_t dims[4] = {(cuuint64_t)kea::kBK, (cuuint64_t)d->m, (cuuint64_t)kb_total, (cuuint64_t)d->parts};
         const cuuint64_t strides[3] = {(cuuint64_t)d->ldq, (cuuint64_t)kea::kBK, (cuuint64_t)std::max<long long>(pstride, 16)};
@@ -554,7 +592,7 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     const int staging_bytes = (c.tile_m / kea::kBM) * kea::kEpiWarps * 32 * warp_row_bytes;   // reuses the stages
     bool tma_store = c.splits == 1 && aligned16(d->y) && (d->ldy * out_esize) % 16 == 0 &&
                      (warp_row_bytes == 64 || warp_row_bytes == 128) &&
-                     staging_bytes <= c.stages * stage_bytes(c.tile_m, c.tile_n, d->parts, d->wbits);
+                     staging_bytes <= c.stages * stage_bytes(c.tile_m, c.tile_n, pe, d->wbits);
     if (tma_store) {
         const cuuint64_t ydims[2] = {(cuuint64_t)d->n, (cuuint64_t)d->m};
         const cuuint64_t ystrides[1] = {(cuuint64_t)(d->ldy * out_esize)};
@@ -591,8 +629,8 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     a.kb_total = ceil_div(d->k, kea::kBK);
     a.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
     a.pdl = (d->flags & KEA_FLAG_PDL) ? 1 : 0;
-    a.tmem_cols = tmem_columns(c.tile_m, c.tile_n, d->parts);
-    a.a_stage = (uint32_t)a_stage_bytes(c.tile_m, d->parts);
+    a.tmem_cols = tmem_columns(c.tile_m, c.tile_n, pe);
+    a.a_stage = (uint32_t)a_stage_bytes(c.tile_m, pe);
     a.b_stage = (uint32_t)b_stage_bytes(c.tile_n);
     a.pk_stage = (uint32_t)pk_stage_bytes(c.tile_n, d->wbits);
     a.b_region = (uint32_t)c.stages * a.a_stage;
@@ -601,10 +639,12 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     a.oneshot = oneshot ? 1 : 0;
     a.kbox = kbox;
     a.act_tx = act_tx;
-    a.nacc = accumulators(c.tile_m, c.tile_n, d->parts);
-    a.a_stride = oneshot ? (uint32_t)(box_rows4 * kea::kBK) : a.a_stage;
-    a.recv_aliases_stages = exchange_aliases(c.tile_m, c.tile_n, d->parts, d->wbits, c.splits, c.stages) ? 1 : 0;
-    a.recv_off = a.recv_aliases_stages ? 0u : (uint32_t)(c.stages * stage_bytes(c.tile_m, c.tile_n, d->parts, d->wbits));
+    a.nacc = accumulators(c.tile_m, c.tile_n, pe);
+    a.a_stride = oneshot ? (uint32_t)((stack ? d->parts : 1) * box_rows4 * kea::kBK) : a.a_stage;
+    a.recv_aliases_stages = exchange_aliases(c.tile_m, c.tile_n, pe, d->wbits, c.splits, c.stages) ? 1 : 0;
+    a.recv_off = a.recv_aliases_stages ? 0u : (uint32_t)(c.stages * stage_bytes(c.tile_m, c.tile_n, pe, d->wbits));
+    a.stack = stack ? 1 : 0;
+    a.mp = box_rows4;
     const int esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
     a.vec_y = aligned16(d->y) && ((d->ldy * esize) % 16 == 0);
     a.vec_acc = d->acc && aligned16(d->acc) && ((d->ld_acc * 4) % 16 == 0) && ((d->acc_part_stride * 4) % 16 == 0);

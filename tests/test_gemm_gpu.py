@@ -157,6 +157,37 @@ def test_gemm_parts_and_order(wbits, parts, n, k, m, flags):
     _check(y, acc, want, want_acc, flags)
 
 
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("parts", [2, 3])
+@pytest.mark.parametrize("n,k,m", [(1024, 1024, 38), (4096, 1024, 40), (3072, 1024, 17), (2048, 1024, 64),
+                                   (1024, 4096, 1), (1024, 1024, 5), (512, 256, 33)])
+@pytest.mark.parametrize("flags", [0, 2, 1])
+def test_stacked_parts_small_m(wbits, parts, n, k, m, flags):
+    """Small M with 2 or 3 parts: the parts are stacked along one 128-row tile (one MMA per K step for all parts)
+    whenever P x round_up(M, 8) <= 128, with and without split-K; results are those of the oracle bit for bit."""
+    seed = wbits * 31 + parts * 7 + n + k + m + flags
+    codes, w = _codes(wbits, n, k, seed)
+    q, qs = _activations(parts, m, k, seed)
+    alpha, bias = _channel(n, seed, flags != 2)
+    out = torch.float16 if flags == 2 else torch.float32
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags, out=out)
+    want, want_acc = oracle.reference(q, qs, w, alpha, bias, flags)
+    _check(y, acc, want, want_acc, flags)
+
+
+@pytest.mark.parametrize("config", [(128, 32, 1, 8), (128, 64, 2, 4), (128, 128, 4, 2), (128, 32, 4, 2),
+                                    (128, 256, 8, 1), (128, 64, 1, 1)])
+@pytest.mark.parametrize("parts", [2, 3])
+def test_stacked_parts_forced_configs(config, parts):
+    n, k, m = 512, 2048, 38
+    codes, w = _codes(1, n, k, 13)
+    q, qs = _activations(parts, m, k, 13)
+    alpha, bias = _channel(n, 13, True)
+    y, acc = _run(codes, 1, n, k, q, qs, alpha, bias, config=configs.DotConfig(*config))
+    want, want_acc = oracle.reference(q, qs, w, alpha, bias)
+    _check(y, acc, want, want_acc, 0)
+
+
 @pytest.mark.parametrize("out", [torch.float32, torch.float16])
 @pytest.mark.parametrize("parts", [1, 3])
 def test_gemm_silu_epilogue(out, parts):
