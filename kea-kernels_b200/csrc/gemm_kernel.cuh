@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
     const uint32_t base = (raw + 1023u) & ~1023u;   // 128-byte swizzle atoms need 1024-byte alignment
     const int TN = a.tile_n, TMB = a.tm_blocks;
     const int tn_log2 = 31 - __clz(TN);
-    const int n0 = blockIdx.x * TN, t0 = blockIdx.y * (TMB * kBM);
+    const int n0 = blockIdx.x * TN, t0 = blockIdx.y * (a.stack ? a.mp : TMB * kBM);
     const int rank = a.splits > 1 ? (int)cluster_ctarank() : 0;
     const int kb0 = (int)((long long)a.kb_total * rank / a.splits);
     const int kb1 = (int)((long long)a.kb_total * (rank + 1) / a.splits);

@@ -175,21 +175,40 @@ bool pair_shape(int m, int n, int k, int parts) {
 // Stacked parts: with P > 1 and P x (M rounded up to 8) <= 128 the parts share one 128-row token tile (part p's
 // tokens at rows p * mp ..), so the MMAs, tensor memory and shared memory are those of one part. Needs the 4-D
 // activation view (K a multiple of 128).
-int stack_rows(int m, int parts, int k) { return round_up(std::max(m, 1), 8); }
-bool stackable(int m, int parts, int k) {
-    return parts > 1 && k % kea::kBK == 0 && m <= kea::kBM && parts * stack_rows(m, parts, k) <= kea::kBM;
+// Up to 512 tokens the tokens are cut into stacked tiles of mp tokens (P x mp <= 128 rows; mp a multiple of 8).
+constexpr int kStackMaxM = 512;
+int stack_rows(int m, int parts, int k) {
+    return std::min(round_up(std::max(m, 1), 8), (kea::kBM / (8 * std::max(parts, 1))) * 8);
+}
+bool stackable(int m, int parts, int k) { return parts > 1 && k % kea::kBK == 0 && m <= kStackMaxM; }
+// The table's choice: one stacked tile always; above one token block only while unstacked tiles (128 tokens x 128
+// channels, P accumulators) would leave half the SMs idle; several stacked tiles run unsplit, so at M <= 128 with
+// long K the split unstacked tile wins (measured on the reference's x3 shapes).
+bool use_stack(int m, int n, int k, int parts, int sms) {
+    if (!stackable(m, parts, k)) return false;
+    const bool one_tile = parts * round_up(std::max(m, 1), 8) <= kea::kBM;
+    return (m <= kea::kBM || 2 * ceil_div(m, kea::kBM) * ceil_div(n, kea::kPanelN) < sms) &&
+           (one_tile || ceil_div(k, kea::kBK) <= 8 || m > kea::kBM);
 }
 
 KeaGemmConfig choose_tile(int m, int n, int k, int wbits, int parts_in, int sms, bool allow_stack = true) {
     KeaGemmConfig c{};
     // the tile's footprint: stacked parts act as one
-    const int parts = allow_stack && stackable(m, parts_in, k) ? 1 : parts_in;
+    const bool stacked = allow_stack && use_stack(m, n, k, parts_in, sms);
+    const int parts = stacked ? 1 : parts_in;
     const int kb = ceil_div(k, kea::kBK), nt128 = ceil_div(n, kea::kPanelN);
+    // token tiles: stacked tiles of mp tokens, else blocks of 128 (or 256) tokens
+    const int tok_tiles = stacked ? ceil_div(std::max(m, 1), stack_rows(m, parts_in, k)) : 1;
     int tile_m, tile_n;
-    if (m <= kea::kBM) {
+    if (stacked && tok_tiles > 1) {
+        // several stacked token tiles: split K only for one-shot loading, widen the channel tile until one wave
         tile_m = kea::kBM;
         tile_n = 32;
-        while (tile_n < 128 && ceil_div(n, tile_n * 2) * 2 >= sms) tile_n *= 2;   // keep >= sms / 2 CTAs
+        while (tile_n < 128 && tok_tiles * ceil_div(n, tile_n) > sms) tile_n *= 2;
+    } else if (m <= kea::kBM || stacked) {
+        tile_m = kea::kBM;
+        tile_n = 32;
+        while (tile_n < 128 && tok_tiles * ceil_div(n, tile_n * 2) * 2 >= sms) tile_n *= 2;   // keep >= sms / 2 CTAs
     } else if (m <= 512) {
         tile_m = parts == 1 ? 256 : kea::kBM;
         tile_n = 128;
@@ -199,13 +218,14 @@ KeaGemmConfig choose_tile(int m, int n, int k, int wbits, int parts_in, int sms,
         const int tiles256 = ceil_div(n, tile_n) * ceil_div(m, tile_m);
         if (tiles256 < sms && tile_n == 256) tile_n = 128;                  // too few tiles: narrower channels
     }
-    const int tiles = ceil_div(std::max(m, 1), tile_m) * ceil_div(n, tile_n);
+    const int tiles = (stacked ? tok_tiles : ceil_div(std::max(m, 1), tile_m)) * ceil_div(n, tile_n);
     int splits = 1;
     if (tiles < sms) splits = std::max(1, sms / tiles);
+    if (stacked && tok_tiles > 1) splits = 1;
     // One token block: split K only as far as needed for each CTA's K range to arrive in one shot (<= 8 k-blocks);
     // more splits fill more SMs, but the partial exchange costs more than the idle SMs (measured: K = 1024 runs
     // fastest unsplit on 32-64 CTAs, K = 4096 with 4 splits).
-    if (m <= kea::kBM) splits = std::min(splits, ceil_div(kb, 8));
+    if (m <= kea::kBM || stacked) splits = std::min(splits, ceil_div(kb, 8));
     splits = std::min({splits, kb, kMaxPortableCluster});
     while (splits > 1 && exchange_bytes(tile_m, tile_n, parts, splits) + 1024 > kMaxDynSmem) --splits;
     const int per = ceil_div(kb, splits);
@@ -488,7 +508,9 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     }
     if (c.pair) c = choose_tile(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms);
     // Stacked parts (one 128-row tile holds every part's tokens): pe is the parts the tile's footprint counts.
-    int pe = stackable(d->m, d->parts, d->k) ? 1 : d->parts;
+    // forced tiles may stack whenever the shape allows; the table stacks where it chose to
+    int pe = (forced ? stackable(d->m, d->parts, d->k) : use_stack(d->m, d->n, d->k, d->parts, g_devices[dev].sms))
+                 ? 1 : d->parts;
     if (forced) {
         if (d->tile_m) c.tile_m = d->tile_m;
         if (d->tile_n) c.tile_n = d->tile_n;
@@ -530,7 +552,7 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     const long long pstride = d->parts > 1 ? d->q_part_stride : (long long)d->m * d->ldq;
     // Rows past m only feed accumulator rows that are never stored, so a single token tile loads just the rows
     // that exist (rounded up to the 8-row swizzle atom) instead of zero-filling the rest.
-    const int box_rows4 = std::min(kea::kBM * tmb, round_up(d->m, 8));
+    const int box_rows4 = stack ? stack_rows(d->m, d->parts, d->k) : std::min(kea::kBM * tmb, round_up(d->m, 8));
     const int box_rows3 = std::min(kea::kBM, round_up(d->m, 8));
     uint32_t act_tx;
     if (q4d && stack) {
@@ -651,7 +673,8 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     a.err = d->error_word;
 
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)ceil_div(d->n, c.tile_n), (unsigned)ceil_div(d->m, c.tile_m), (unsigned)c.splits);
+    cfg.gridDim = dim3((unsigned)ceil_div(d->n, c.tile_n),
+                       (unsigned)(stack ? ceil_div(d->m, box_rows4) : ceil_div(d->m, c.tile_m)), (unsigned)c.splits);
     cfg.blockDim = dim3(kea::kThreads, 1, 1);
     cfg.dynamicSmemBytes = (size_t)c.smem_bytes;
     cfg.stream = (cudaStream_t)stream;

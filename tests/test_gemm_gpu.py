@@ -160,11 +160,12 @@ def test_gemm_parts_and_order(wbits, parts, n, k, m, flags):
 @pytest.mark.parametrize("wbits", [1, 2])
 @pytest.mark.parametrize("parts", [2, 3])
 @pytest.mark.parametrize("n,k,m", [(1024, 1024, 38), (4096, 1024, 40), (3072, 1024, 17), (2048, 1024, 64),
-                                   (1024, 4096, 1), (1024, 1024, 5), (512, 256, 33)])
+                                   (1024, 4096, 1), (1024, 1024, 5), (512, 256, 33), (1024, 1024, 126),
+                                   (4096, 1024, 368), (1024, 4096, 257), (640, 512, 511)])
 @pytest.mark.parametrize("flags", [0, 2, 1])
 def test_stacked_parts_small_m(wbits, parts, n, k, m, flags):
-    """Small M with 2 or 3 parts: the parts are stacked along one 128-row tile (one MMA per K step for all parts)
-    whenever P x round_up(M, 8) <= 128, with and without split-K; results are those of the oracle bit for bit."""
+    """M <= 512 with 2 or 3 parts: the tokens are cut into tiles of mp tokens whose parts are stacked along one
+    128-row tile (one MMA per K step for all parts), with and without split-K; bit for bit the oracle's results."""
     seed = wbits * 31 + parts * 7 + n + k + m + flags
     codes, w = _codes(wbits, n, k, seed)
     q, qs = _activations(parts, m, k, seed)
