@@ -135,6 +135,8 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_regs_kernel(const Quan
     const int K = a.K;
     float4 v[C];
     grid_dependency_wait();
+    // the next kernel may launch now: it loads its static operands, then waits for this grid to complete
+    grid_launch_dependents();
     const float4 *src = reinterpret_cast<const float4 *>(
         a.x + (live ? (long long)(m / a.t) * a.xb + (long long)(m % a.t) * a.xt : 0LL));
 #pragma unroll
@@ -235,6 +237,8 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantArgs
         bases[threadIdx.x] = a.x + (long long)(m / a.t) * a.xb + (long long)(m % a.t) * a.xt;
     }
     grid_dependency_wait();
+    // the next kernel may launch now: it loads its static operands, then waits for this grid to complete
+    grid_launch_dependents();
     __syncthreads();
     if (a.xk == 1) {
         if (g < nrows) {

@@ -91,7 +91,10 @@ struct GemmArgs {
     uint32_t a_stage, b_stage, pk_stage;   // bytes per stage of the activation / expanded-weight / packed regions
     uint32_t b_region, pk_region;         // region offsets in dynamic shared memory (the activation region is at 0)
     int q4d;                     // qmap is 4-D (k in block, row, k-block, part) with 128 * tm_blocks-row boxes
-    int oneshot;                 // the whole K range of the CTA arrives at once on bar_full[0] (two TMA boxes)
+    int oneshot;                 // the whole K range of the CTA arrives at once, in `chunks` pairs of TMA boxes of
+                                 // kbox k-blocks each, chunk c on bar_full[c] (expansion and MMAs of chunk 0 overlap
+                                 // the landing of chunk 1)
+    int chunks;
     int kbox;                    // k-blocks per activation / panel box in one-shot mode
     uint32_t act_tx;             // activation bytes one stage receives (boxes shrink to the rows that exist)
     int nacc;                    // independent accumulators per (token block, part): 1, or 4 for narrow tiles (one per
@@ -300,6 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
     __shared__ __align__(8) uint64_t bar_exp[kMaxStages];
     __shared__ __align__(8) uint64_t bar_empty[kMaxStages];
     __shared__ __align__(8) uint64_t bar_acc;
+    __shared__ __align__(8) uint64_t bar_w;      // one-shot with programmatic dependent launch: the packed codes
     __shared__ uint32_t tmem_slot;
     __shared__ float s_qs[3 * 2 * kBM];
     __shared__ float s_alpha[kMaxTileN];
@@ -332,6 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
             mbar_init(smem_u32(&bar_empty[s]), 1);
         }
         mbar_init(smem_u32(&bar_acc), 1);
+        mbar_init(smem_u32(&bar_w), 1);
         fence_barrier_init();
         prefetch_tensormap(&qmap);
         if (a.tma_store) prefetch_tensormap(&ymap);
@@ -347,8 +352,11 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
     const uint32_t tmem = tmem_slot;
     KEA_TRACE_POINT(threadIdx.x == 0, 1);
 
-    // With programmatic dependent launch, everything below may read what the previous kernel wrote.
-    if (a.pdl) grid_dependency_wait();
+    // With programmatic dependent launch, everything below may read what the previous kernel wrote. In one-shot
+    // mode the packed codes (static weights) are loaded and expanded first, while the previous kernel finishes:
+    // only the producer's activation boxes and the expanders' token-scale loads wait for it.
+    const bool early_w = a.pdl && a.oneshot;
+    if (a.pdl && !early_w) grid_dependency_wait();
 
     bool ok = true;
     if (warp == 0) {
@@ -368,14 +376,29 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
             // Every k-block of this CTA at once: one TMA box of the panels (kbox k-blocks x wbits x 4 word planes
             // of this CTA's R rows) and one 4-D box of activations (128 rows x kbox k-blocks), both on bar_full[0].
             if (lane == 0) {
-                const uint32_t full = smem_u32(&bar_full[0]);
-                mbar_arrive_expect_tx(full, (uint32_t)a.kbox * tx_bytes);
-                const int plane0 = ((n0 / kPanelN) * a.kb_total + kb0) * WBITS * 4;
-                tma_load_2d(PK0, &wmap, full, (n0 % kPanelN) * 4, plane0);
-                if (a.stack)
-                    tma_load_4d(A0, &qmap, full, 0, t0, 0, kb0);
-                else
-                    tma_load_4d(A0, &qmap, full, 0, t0, kb0, 0);
+                if (early_w) {   // every chunk's codes on bar_w now; the activations once the previous kernel is done
+                    const uint32_t wbar = smem_u32(&bar_w);
+                    mbar_arrive_expect_tx(wbar, (uint32_t)(a.chunks * a.kbox) * a.pk_stage);
+                    for (int c = 0; c < a.chunks; ++c) {
+                        const int plane0 = ((n0 / kPanelN) * a.kb_total + kb0 + c * a.kbox) * WBITS * 4;
+                        tma_load_2d(PK0 + (uint32_t)(c * a.kbox) * a.pk_stage, &wmap, wbar, (n0 % kPanelN) * 4, plane0);
+                    }
+                    grid_dependency_wait();
+                }
+                for (int c = 0; c < a.chunks; ++c) {
+                    const uint32_t full = smem_u32(&bar_full[c]);
+                    const int kbc = kb0 + c * a.kbox;
+                    mbar_arrive_expect_tx(full, (uint32_t)a.kbox * (early_w ? a.act_tx : tx_bytes));
+                    if (!early_w) {
+                        const int plane0 = ((n0 / kPanelN) * a.kb_total + kbc) * WBITS * 4;
+                        tma_load_2d(PK0 + (uint32_t)(c * a.kbox) * a.pk_stage, &wmap, full, (n0 % kPanelN) * 4, plane0);
+                    }
+                    const uint32_t adst = A0 + (uint32_t)(c * a.kbox) * a.a_stride;
+                    if (a.stack)
+                        tma_load_4d(adst, &qmap, full, 0, t0, 0, kbc);
+                    else
+                        tma_load_4d(adst, &qmap, full, 0, t0, kbc, 0);
+                }
             }
             __syncwarp();
             issued = nkb;
@@ -428,33 +451,41 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
         KEA_TRACE_POINT(lane == 0, 3);
         if (!ok) {
             if (lane == 0) report(a.err, 1u);
-            for (int i = (issued > S ? issued - S : 0); i < issued; ++i)   // let issued copies land first
-                mbar_wait(smem_u32(&bar_full[a.oneshot ? 0 : i % S]), a.oneshot ? 0 : (i / S) & 1, kWaitBudget);
+            if (a.oneshot) {
+                if (early_w) mbar_wait(smem_u32(&bar_w), 0u, kWaitBudget);
+                for (int c = 0; c < a.chunks; ++c) mbar_wait(smem_u32(&bar_full[c]), 0u, kWaitBudget);
+            } else {
+                for (int i = (issued > S ? issued - S : 0); i < issued; ++i)   // let issued copies land first
+                    mbar_wait(smem_u32(&bar_full[i % S]), (i / S) & 1, kWaitBudget);
+            }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer: the whole warp waits, lane 0 issues ----------------
         const uint32_t idesc = idesc_i8(kBM, (uint32_t)TN);
         const uint64_t a_desc0 = sw128_kmajor_desc(A0), b_desc0 = sw128_kmajor_desc(B0);
         if (a.oneshot && nkb > 0) {
-            // Every k-block is resident and the expanders arrive on the stage barriers in order after one fence, so
-            // the last stage's barrier covers them all: one wait, then every MMA back to back (one issuing thread
-            // sustains about one tcgen05.mma per 70 clocks; a wait and a commit per stage would triple that).
-            const bool ready = mbar_wait(smem_u32(&bar_full[0]), 0u, kWaitBudget) &&
-                               mbar_wait(smem_u32(&bar_exp[nkb - 1]), 0u, kWaitBudget);
-            if (!__all_sync(0xFFFFFFFFu, ready)) {
-                ok = false;
-                if (lane == 0) report(a.err, 1u);
-            } else if (elect_one()) {
-                for (int i = 0; i < nkb; ++i) {
-                    const uint64_t ad_s = a_desc0 + (uint64_t)((i * a.a_stride) >> 4);
-                    const uint64_t bd_s = b_desc0 + (uint64_t)((i * a.b_stage) >> 4);
-                    if (a.stack)
-                        issue_stage<1, 1, 4>(tmem, ad_s, bd_s, idesc, TN, i == 0);
-                    else
-                        issue_stage<P, 1, 4>(tmem, ad_s, bd_s, idesc, TN, i == 0);
+            // Every k-block of a chunk is resident and the expanders arrive on its stage barriers in order after one
+            // fence, so the chunk's last stage barrier covers it: one wait per chunk, then its MMAs back to back.
+            for (int c = 0; c < a.chunks && ok; ++c) {
+                const int i0 = c * a.kbox, i1 = min(nkb, i0 + a.kbox);
+                if (i0 >= i1) break;
+                const bool ready = mbar_wait(smem_u32(&bar_full[c]), 0u, kWaitBudget) &&
+                                   mbar_wait(smem_u32(&bar_exp[i1 - 1]), 0u, kWaitBudget);
+                if (!__all_sync(0xFFFFFFFFu, ready)) {
+                    ok = false;
+                    if (lane == 0) report(a.err, 1u);
+                } else if (elect_one()) {
+                    for (int i = i0; i < i1; ++i) {
+                        const uint64_t ad_s = a_desc0 + (uint64_t)((i * a.a_stride) >> 4);
+                        const uint64_t bd_s = b_desc0 + (uint64_t)((i * a.b_stage) >> 4);
+                        if (a.stack)
+                            issue_stage<1, 1, 4>(tmem, ad_s, bd_s, idesc, TN, i == 0);
+                        else
+                            issue_stage<P, 1, 4>(tmem, ad_s, bd_s, idesc, TN, i == 0);
+                    }
                 }
+                __syncwarp();
             }
-            __syncwarp();
         }
         int s = 0;
         uint32_t ph = 0;
@@ -501,9 +532,11 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
     } else {
         // ---------------- expanders ----------------
         const int e = threadIdx.x - 64;   // 0 .. 511
-        for (int i = e; i < P * TMB * kBM; i += kEpiThreads) {
-            const int p = i / (TMB * kBM), t = t0 + (i - p * TMB * kBM);
-            s_qs[i] = t < a.M ? a.qs[p * a.qs_stride + t] : 0.f;
+        if (!early_w) {
+            for (int i = e; i < P * TMB * kBM; i += kEpiThreads) {
+                const int p = i / (TMB * kBM), t = t0 + (i - p * TMB * kBM);
+                s_qs[i] = t < a.M ? a.qs[p * a.qs_stride + t] : 0.f;
+            }
         }
         for (int i = e; i < TN; i += kEpiThreads) {
             const int n = n0 + i;
@@ -512,10 +545,10 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
         }
         const int units = TN * (WBITS == 1 ? 4 : 8);
         const int units_log2 = tn_log2 + (WBITS == 1 ? 2 : 3);
-        if (a.oneshot) {
-            // Every k-block is already resident: spread all of them over the 512 threads, then one proxy fence and
-            // the stage arrivals (a fence per stage would put its latency into every stage of the MMA chain).
-            const bool landed = mbar_wait(smem_u32(&bar_full[0]), 0u, kWaitBudget);
+        if (a.oneshot && early_w) {
+            // The codes of every chunk arrive on bar_w, ahead of the activations: expand them all behind one fence,
+            // then wait for the previous kernel and read this tile's token scales.
+            const bool landed = mbar_wait(smem_u32(&bar_w), 0u, kWaitBudget);
             if (!__all_sync(0xFFFFFFFFu, landed)) {
                 ok = false;
                 if (lane == 0) report(a.err, 1u);
@@ -531,6 +564,35 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                 __syncwarp();
                 if (lane == 0)
                     for (int st = 0; st < nkb; ++st) mbar_arrive(smem_u32(&bar_exp[st]));
+            }
+            grid_dependency_wait();
+            for (int i = e; i < P * TMB * kBM; i += kEpiThreads) {
+                const int p = i / (TMB * kBM), t = t0 + (i - p * TMB * kBM);
+                s_qs[i] = t < a.M ? a.qs[p * a.qs_stride + t] : 0.f;
+            }
+        } else if (a.oneshot) {
+            // Each chunk's k-blocks are resident at once: spread them over the 512 threads, then one proxy fence and
+            // the chunk's stage arrivals (a fence per stage would put its latency into every stage of the MMA chain).
+            for (int c = 0; c < a.chunks && ok; ++c) {
+                const int i0 = c * a.kbox, i1 = min(nkb, i0 + a.kbox);
+                if (i0 >= i1) break;
+                const bool landed = mbar_wait(smem_u32(&bar_full[c]), 0u, kWaitBudget);
+                if (!__all_sync(0xFFFFFFFFu, landed)) {
+                    ok = false;
+                    if (lane == 0) report(a.err, 1u);
+                } else {
+                    KEA_TRACE_POINT(threadIdx.x == 64 && c == 0, 4);
+                    for (int f = e + (i0 << units_log2); f < (i1 << units_log2); f += kEpiThreads) {
+                        const int st = f >> units_log2;
+                        expand_unit<WBITS>(PK0 + (uint32_t)st * a.pk_stage, B0 + (uint32_t)st * a.b_stage, tn_log2,
+                                           f & (units - 1));
+                    }
+                    fence_async_shared();
+                    KEA_TRACE_POINT(threadIdx.x == 64 && c == 0, 5);
+                    __syncwarp();
+                    if (lane == 0)
+                        for (int st = i0; st < i1; ++st) mbar_arrive(smem_u32(&bar_exp[st]));
+                }
             }
         }
         int s = 0;

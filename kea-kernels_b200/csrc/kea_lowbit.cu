@@ -547,7 +547,9 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     // One-shot: the CTA's whole K range fits in the stages and arrives in two TMA boxes (one token block, one
     // part, narrow channel tile so the panel box is at most 256 bytes wide).
     const bool oneshot = q4d && tmb * pe == 1 && c.tile_n <= 64 && nkb_max <= c.stages && nkb_max <= 8;
-    const int kbox = oneshot ? nkb_max : 1;
+    // two chunks when they fit the stages: the second lands while the first is expanded and multiplied
+    const int chunks = oneshot && nkb_max >= 4 && 2 * ceil_div(nkb_max, 2) <= c.stages ? 2 : 1;
+    const int kbox = oneshot ? ceil_div(nkb_max, chunks) : 1;
     CUtensorMap qmap;
     const long long pstride = d->parts > 1 ? d->q_part_stride : (long long)d->m * d->ldq;
     // Rows past m only feed accumulator rows that are never stored, so a single token tile loads just the rows
@@ -659,6 +661,7 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     a.pk_region = a.b_region + (uint32_t)c.stages * a.b_stage;
     a.q4d = q4d ? 1 : 0;
     a.oneshot = oneshot ? 1 : 0;
+    a.chunks = chunks;
     a.kbox = kbox;
     a.act_tx = act_tx;
     a.nacc = accumulators(c.tile_m, c.tile_n, pe);
