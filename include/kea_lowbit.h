@@ -94,9 +94,11 @@ typedef struct KeaGemmDesc {
     int64_t acc_part_stride;  /* elements between parts of acc */
     int32_t m;                /* tokens (rows of q and y); 0 is a no-op */
     int32_t flags;            /* KEA_FLAG_* */
-    int32_t tile_m;           /* 0: dispatch table; else tokens per CTA (128 or 256); any forced field selects the
-                                 per-tile kernel */
-    int32_t tile_n;           /* 0: dispatch table; else channels per CTA (32, 64, 128 or 256) */
+    int32_t tile_m;           /* 0: dispatch table; 128 or 256: tokens per CTA of the per-tile tcgen05 kernel (any
+                                 forced field selects it); 1..16: the CUDA-core kernel (m <= 16, splits and stages
+                                 0 or 1) */
+    int32_t tile_n;           /* 0: dispatch table; else channels per CTA (32, 64, 128 or 256; 8, 16 or 32 for the
+                                 CUDA-core kernel) */
     int32_t splits;           /* 0: dispatch table; else split-K ways = cluster size (1..16) */
     int32_t stages;           /* 0: dispatch table; else pipeline stages (1..8) */
     uint32_t *error_word;     /* device word OR-ed with KEA_DEVERR_* bits, or NULL for the library's own */
@@ -109,8 +111,9 @@ typedef struct KeaGemmConfig {
     int32_t splits;           /* K split across a thread-block cluster of this size */
     int32_t stages;           /* smem pipeline depth (k128 blocks in flight) */
     int32_t smem_bytes;       /* dynamic shared memory per CTA */
-    int32_t pair;             /* 1: the persistent CTA-pair kernel (tcgen05 cta_group::2, 256 x 256 tiles per pair of
-                                 SMs, double-buffered accumulators); 0: the per-tile kernel */
+    int32_t kernel;           /* 0: the per-tile tcgen05 kernel; 1: the persistent CTA-pair kernel (tcgen05
+                                 cta_group::2, 256 x 256 tiles per pair of SMs, double-buffered accumulators); 2: the
+                                 CUDA-core kernel for M <= 16 (tile_n = channels per CTA) */
 } KeaGemmConfig;
 
 int kea_lowbit_gemm(const KeaGemmDesc *desc, void *stream);

@@ -11,6 +11,7 @@
 #include "kea_lowbit.h"
 #include "gemm_kernel.cuh"
 #include "gemm_pair_kernel.cuh"
+#include "gemv_kernel.cuh"
 #include "aux_kernels.cuh"
 
 namespace {
@@ -85,6 +86,15 @@ int device_setup(int *device_out) {
         if (cudaFuncSetAttribute((const void *)kea::quantize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  64 * 1024) != cudaSuccess)
             status = KEA_ERR_CUDA;
+        const void *gemv_kernels[18] = {
+#define KEA_GEMV_MT(W, P) (const void *)kea::lowbit_gemv_kernel<W, P, 1>, (const void *)kea::lowbit_gemv_kernel<W, P, 4>, \
+                          (const void *)kea::lowbit_gemv_kernel<W, P, 16>
+            KEA_GEMV_MT(1, 1), KEA_GEMV_MT(1, 2), KEA_GEMV_MT(1, 3), KEA_GEMV_MT(2, 1), KEA_GEMV_MT(2, 2), KEA_GEMV_MT(2, 3)
+#undef KEA_GEMV_MT
+        };
+        for (const void *k : gemv_kernels)
+            if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kea::kGemvMaxSmem) != cudaSuccess)
+                status = KEA_ERR_CUDA;
     }
     st.status = status;
     st.sms = sms > 0 ? sms : kSmsB200;
@@ -235,11 +245,28 @@ KeaGemmConfig choose_tile(int m, int n, int k, int wbits, int parts_in, int sms,
     c.splits = splits;
     c.stages = std::max(stages, 1);
     c.smem_bytes = dyn_smem_bytes(tile_m, tile_n, parts, wbits, splits, c.stages);
-    c.pair = 0;
+    c.kernel = 0;
     return c;
 }
 
-// The full table: the pair kernel where its shape rule holds, else the per-tile kernel's entry.
+// The CUDA-core kernel: 8 channels per CTA (32 K slices per channel) spreads even 1024-channel layers over the SMs.
+// 16 (fewer, longer slices) measured faster for small weights (N x K <= 1M: the whole job is a few CTAs per SM) and
+// for wide layers (N > 3072) with several activation rows, unless the rows are the tokens of one 2-bit part (its
+// words carry half the codes, so its slices are already twice as long). The table takes the kernel up to
+// kGemvTableRows activation rows (tokens x parts), where it beat the tensor-core kernel on every Parakeet shape;
+// from 6 rows on the tensor-core kernel is as fast or faster.
+constexpr int kGemvTableRows = 4;
+int gemv_channels(int n, int k, int wbits, int m, int parts) {
+    if ((long long)n * k <= (1LL << 20)) return 16;
+    if (n > 3072 && m * parts >= 2 && (wbits == 1 || parts > 1)) return 16;
+    return 8;
+}
+bool gemv_fits(int m, int parts, int ch) {
+    return m >= 1 && m <= kea::kGemvMaxM && kea::gemv_smem_bytes(m * parts, ch) <= kea::kGemvMaxSmem;
+}
+
+// The full table: the CUDA-core kernel for M <= 16, the pair kernel where its shape rule holds, else the per-tile
+// kernel's entry.
 KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
     KeaGemmConfig c = choose_tile(m, n, k, wbits, parts, sms);
     if (pair_shape(m, n, k, parts)) {
@@ -248,7 +275,15 @@ KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
         c.splits = 1;
         c.stages = pair_max_stages(wbits);
         c.smem_bytes = pair_smem_bytes(wbits, c.stages);
-        c.pair = 1;
+        c.kernel = 1;
+    }
+    if (m * parts <= kGemvTableRows && gemv_fits(m, parts, gemv_channels(n, k, wbits, m, parts))) {
+        c.kernel = 2;
+        c.tile_m = m;
+        c.tile_n = gemv_channels(n, k, wbits, m, parts);
+        c.splits = 1;
+        c.stages = 1;
+        c.smem_bytes = kea::gemv_smem_bytes(m * parts, c.tile_n);
     }
     return c;
 }
@@ -285,6 +320,65 @@ cudaLaunchConfig_t launch_config(dim3 grid, size_t dyn, void *stream, cudaLaunch
         cfg.numAttrs = 1;
     }
     return cfg;
+}
+
+// Launches the CUDA-core kernel for M <= 16 (any wbits / parts / layout the per-tile kernel takes).
+template <int W, int P>
+cudaError_t launch_gemv_p(cudaLaunchConfig_t *cfg, const kea::GemvArgs &a) {
+    if (a.M <= 1) return cudaLaunchKernelEx(cfg, kea::lowbit_gemv_kernel<W, P, 1>, a);
+    if (a.M <= 4) return cudaLaunchKernelEx(cfg, kea::lowbit_gemv_kernel<W, P, 4>, a);
+    return cudaLaunchKernelEx(cfg, kea::lowbit_gemv_kernel<W, P, 16>, a);
+}
+
+int launch_gemv(const KeaGemmDesc *d, const KeaGemmConfig &c, void *stream) {
+    kea::GemvArgs a{};
+    a.q = d->q;
+    a.q_stride = d->parts > 1 ? d->q_part_stride : 0;
+    a.ldq = d->ldq;
+    a.qs = d->qs;
+    a.qs_stride = d->qs_part_stride;
+    a.panels = d->panels;
+    a.alpha = d->alpha;
+    a.bias = d->bias;
+    a.y = d->y;
+    a.ldy = d->ldy;
+    a.y_f16 = d->y_dtype == KEA_OUT_F16;
+    a.acc = d->acc;
+    a.ld_acc = d->ld_acc;
+    a.acc_stride = d->acc_part_stride;
+    a.M = d->m;
+    a.N = d->n;
+    a.K = d->k;
+    a.kb_total = ceil_div(d->k, kea::kBK);
+    a.ch = c.tile_n;
+    a.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
+    a.err = d->error_word;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ceil_div(d->n, c.tile_n), 1, 1);
+    cfg.blockDim = dim3(kea::kGemvThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)kea::gemv_smem_bytes(d->m * d->parts, c.tile_n);
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    if (d->flags & KEA_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e;
+    switch (d->wbits * 4 + d->parts) {
+        case 5: e = launch_gemv_p<1, 1>(&cfg, a); break;
+        case 6: e = launch_gemv_p<1, 2>(&cfg, a); break;
+        case 7: e = launch_gemv_p<1, 3>(&cfg, a); break;
+        case 9: e = launch_gemv_p<2, 1>(&cfg, a); break;
+        case 10: e = launch_gemv_p<2, 2>(&cfg, a); break;
+        default: e = launch_gemv_p<2, 3>(&cfg, a); break;
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return KEA_ERR_CUDA;
+    }
+    return KEA_OK;
 }
 
 // Launches the persistent CTA-pair kernel. KEA_ERR_UNSUPPORTED when an operand's alignment or stride rules it out
@@ -502,11 +596,22 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
 
     KeaGemmConfig c = choose(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms);
     const bool forced = d->tile_m || d->tile_n || d->splits || d->stages;
-    if (c.pair && !forced && !(d->flags & KEA_FLAG_NO_PAIR)) {
+    if (c.kernel == 2 && !forced) return launch_gemv(d, c, stream);
+    if (forced && d->tile_m >= 1 && d->tile_m <= kea::kGemvMaxM) {   // the CUDA-core kernel, forced
+        if ((d->tile_n != 8 && d->tile_n != 16 && d->tile_n != 32) || !gemv_fits(d->m, d->parts, d->tile_n) ||
+            d->splits > 1 || d->stages > 1)
+            return KEA_ERR_UNSUPPORTED;
+        KeaGemmConfig g = c;
+        g.kernel = 2;
+        g.tile_m = d->m;
+        g.tile_n = d->tile_n;
+        return launch_gemv(d, g, stream);
+    }
+    if (c.kernel == 1 && !forced && !(d->flags & KEA_FLAG_NO_PAIR)) {
         const int ps = launch_pair(d, c, g_devices[dev].sms, stream);
         if (ps != KEA_ERR_UNSUPPORTED) return ps;
     }
-    if (c.pair) c = choose_tile(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms);
+    if (c.kernel) c = choose_tile(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms);
     // Stacked parts (one 128-row tile holds every part's tokens): pe is the parts the tile's footprint counts.
     // forced tiles may stack whenever the shape allows; the table stacks where it chose to
     int pe = (forced ? stackable(d->m, d->parts, d->k) : use_stack(d->m, d->n, d->k, d->parts, g_devices[dev].sms))

@@ -42,7 +42,7 @@ class GemmDesc(ctypes.Structure):
 
 class GemmConfig(ctypes.Structure):
     _fields_ = [("tile_m", ctypes.c_int32), ("tile_n", ctypes.c_int32), ("splits", ctypes.c_int32),
-                ("stages", ctypes.c_int32), ("smem_bytes", ctypes.c_int32), ("pair", ctypes.c_int32)]
+                ("stages", ctypes.c_int32), ("smem_bytes", ctypes.c_int32), ("kernel", ctypes.c_int32)]
 
 
 class QuantizeDesc(ctypes.Structure):

@@ -16,28 +16,44 @@ from kea_kernels import _lib
 SMS = 148
 
 
+PER_TILE, PAIR, GEMV = 0, 1, 2
+
+
 @dataclasses.dataclass(frozen=True)
 class DotConfig:
-    """CTA = `tile_m` tokens x `tile_n` channels over 1/`splits` of K, `stages` k128 blocks in flight. With `pair`,
-    the persistent CTA-pair kernel: 256 x 256 tiles per pair of SMs (tcgen05 cta_group::2), walked by at most
-    SMS / 2 pairs, two accumulator buffers in tensor memory."""
+    """CTA = `tile_m` tokens x `tile_n` channels over 1/`splits` of K, `stages` k128 blocks in flight (the per-tile
+    tcgen05 kernel). kernel == PAIR: the persistent CTA-pair kernel, 256 x 256 tiles per pair of SMs (tcgen05
+    cta_group::2), walked by at most SMS / 2 pairs, two accumulator buffers in tensor memory. kernel == GEMV: the
+    CUDA-core kernel for M <= 16, `tile_n` channels per CTA. Passing a PER_TILE config forces those tiles."""
     tile_m: int
     tile_n: int
     splits: int
     stages: int
-    pair: int = 0
+    kernel: int = PER_TILE
+
+    @property
+    def pair(self) -> bool:
+        return self.kernel == PAIR
 
     def label(self) -> str:
-        if self.pair:
+        if self.kernel == PAIR:
             return f"pair{self.tile_m}x{self.tile_n}_s{self.stages}"
+        if self.kernel == GEMV:
+            return f"gemv_n{self.tile_n}"
         return f"m{self.tile_m}_n{self.tile_n}_c{self.splits}_s{self.stages}"
 
     def validate(self, parts: int = 1) -> None:
+        if self.kernel == GEMV:
+            if not (1 <= self.tile_m <= 16 and self.tile_n in (8, 16, 32)):
+                raise ValueError(f"invalid config {self}")
+            return
         if not (self.tile_m in (128, 256) and self.tile_n in (32, 64, 128, 256) and 1 <= self.splits <= 16
                 and 1 <= self.stages <= 8 and (self.tile_m // 128) * parts * self.tile_n <= 512):
             raise ValueError(f"invalid config {self}")
 
     def grid(self, m: int, n: int) -> tuple[int, int, int]:
+        if self.kernel == GEMV:
+            return (-(-n // self.tile_n), 1, 1)
         if self.pair:
             tiles = -(-n // self.tile_n) * -(-m // self.tile_m)
             return (2 * min(tiles, SMS // 2), 1, 1)
@@ -47,4 +63,4 @@ class DotConfig:
 def choose(m: int, n: int, k: int, wbits: int = 1, parts: int = 1) -> DotConfig:
     """The configuration the library uses for this shape (the C table)."""
     c = _lib.choose_config(max(m, 0), n, k, wbits, parts)
-    return DotConfig(c.tile_m, c.tile_n, c.splits, c.stages, c.pair)
+    return DotConfig(c.tile_m, c.tile_n, c.splits, c.stages, c.kernel)

@@ -81,8 +81,9 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
          config=None, pdl: bool = False, error_word: Tensor | None = None, pair: bool = True) -> None:
     """y[:m] (row stride y.stride(0); FP32 or FP16) from q int8 [parts, m, ldq] and qs FP32 [parts, m].
     acc, when given, receives the exact INT32 accumulators as int32 [parts, m, n] (any row / part strides).
-    `config` forces the per-tile kernel's tiles (a pair config from the table forces nothing); pair=False keeps the
-    dispatch table away from the persistent CTA-pair kernel."""
+    `config` forces the per-tile kernel's tiles, or (tile_m <= 16, m <= 16) the CUDA-core kernel's channels per CTA;
+    a pair config from the table forces nothing. pair=False keeps the dispatch table away from the persistent
+    CTA-pair kernel."""
     if m == 0:
         return
     if parts not in (1, 2, 3):
@@ -119,7 +120,7 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
     d.m = m
     d.flags = (_lib.FLAG_SILU if silu else 0) | (_lib.FLAG_ORDER1 if order else 0) | (_lib.FLAG_PDL if pdl else 0) \
         | (0 if pair else _lib.FLAG_NO_PAIR)
-    if config is not None and not getattr(config, "pair", 0):
+    if config is not None and getattr(config, "kernel", 0) != 1:   # a pair config from the table forces nothing
         d.tile_m, d.tile_n, d.splits, d.stages = config.tile_m, config.tile_n, config.splits, config.stages
     if error_word is not None:
         d.error_word = error_word.data_ptr()

@@ -176,6 +176,93 @@ def test_stacked_parts_small_m(wbits, parts, n, k, m, flags):
     _check(y, acc, want, want_acc, flags)
 
 
+def _gemv_fits(rows: int, ch: int = 8) -> bool:
+    """The CUDA-core kernel's slice sums ([8 warps][rows][channels] INT32) fit its 48 KB of shared memory."""
+    return 8 * rows * ch * 4 <= 48 * 1024
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("parts", [1, 2, 3])
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 13, 16])
+@pytest.mark.parametrize("n,k,flags", [(4096, 1024, 0), (1024, 4096, 2), (3072, 1024, 1), (200, 300, 0),
+                                       (1000, 21, 2), (130, 4097, 1), (8, 129, 0)])
+def test_gemv_small_m_equals_oracle(wbits, parts, m, n, k, flags):
+    """The CUDA-core kernel (dp4a over expanded codes), forced for every M <= 16 (the table takes it up to 4
+    activation rows = tokens x parts): bit for bit the oracle's results, for every token-count bucket (1, <= 4,
+    <= 16), part count, epilogue and ragged K / N."""
+    rows, fits = m * parts, _gemv_fits(m * parts)
+    assert (configs.choose(m, n, k, wbits, parts).kernel == configs.GEMV) == (rows <= 4 and fits)
+    seed = wbits * 53 + parts * 11 + m + n + k + flags
+    codes, w = _codes(wbits, n, k, seed)
+    q, qs = _activations(parts, m, k, seed)
+    alpha, bias = _channel(n, seed, flags != 2)
+    out = torch.float16 if flags == 2 else torch.float32
+    config = configs.DotConfig(m, 8, 1, 1, configs.GEMV)
+    if not fits:
+        with pytest.raises(ValueError, match="unsupported"):
+            _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags, out=out, config=config)
+        return
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags, out=out, config=config)
+    want, want_acc = oracle.reference(q, qs, w, alpha, bias, flags)
+    _check(y, acc, want, want_acc, flags)
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("parts", [1, 3])
+@pytest.mark.parametrize("flags", [0, 1, 2])
+def test_gemv_equals_tensor_core_kernel_bitwise(wbits, parts, flags):
+    """The CUDA-core and tensor-core kernels give the same bits, SiLU included (same epilogue code)."""
+    n, k, m = 2048, 1024, 7
+    codes, _ = _codes(wbits, n, k, 77 + flags)
+    q, qs = _activations(parts, m, k, 78)
+    alpha, bias = _channel(n, 79, True)
+    y0, acc0 = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags)
+    y1, acc1 = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags, config=configs.DotConfig(128, 64, 2, 4))
+    assert np.array_equal(acc0, acc1)
+    assert np.array_equal(y0.numpy().view(np.uint32), y1.numpy().view(np.uint32))
+    for ch in (8, 16, 32):   # every forced channels-per-CTA width of the CUDA-core kernel
+        y2, acc2 = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags,
+                        config=configs.DotConfig(m, ch, 1, 1, configs.GEMV))
+        assert np.array_equal(acc0, acc2)
+        assert np.array_equal(y0.numpy().view(np.uint32), y2.numpy().view(np.uint32))
+
+
+def test_forced_gemv_config_is_refused_above_16_tokens():
+    codes, _ = _codes(1, 512, 1024, 3)
+    q, qs = _activations(1, 17, 1024, 3)
+    alpha, _ = _channel(512, 3, False)
+    with pytest.raises(ValueError, match="unsupported"):
+        _run(codes, 1, 512, 1024, q, qs, alpha, None, config=configs.DotConfig(16, 32, 1, 1, configs.GEMV))
+    q, qs = _activations(1, 16, 1024, 3)
+    with pytest.raises(ValueError, match="unsupported"):        # channels per CTA: 8, 16 or 32
+        _run(codes, 1, 512, 1024, q, qs, alpha, None, config=configs.DotConfig(16, 64, 1, 1, configs.GEMV))
+
+
+def test_gemv_pdl_chain_matches():
+    """Back-to-back CUDA-core launches with programmatic dependent launch: the second reads the first's output."""
+    n, k, m = 1024, 1024, 4
+    codes, w = _codes(1, n, k, 91)
+    q, qs = _activations(1, m, k, 92)
+    alpha, _ = _channel(n, 93, False)
+    panels = lowbit.prepare_panels(torch.from_numpy(codes).to(DEV), 1, n, k)
+    qd, qsd, ad = (torch.from_numpy(v).to(DEV) for v in (q, qs, alpha))
+    ref = None
+    for pdl in (False, True):
+        outs = []
+        for _ in range(3):
+            y = torch.empty(m, n, device=DEV)
+            acc = torch.empty(1, m, n, device=DEV, dtype=torch.int32)
+            lowbit.gemm(qd, qsd, q.shape[2], m, panels, 1, n, k, ad, None, y, parts=1, acc=acc, pdl=pdl)
+            outs.append((y, acc))
+        torch.cuda.synchronize()
+        got = [(y.cpu().numpy(), a.cpu().numpy()) for y, a in outs]
+        ref = ref or got[0]
+        for y, a in got:
+            assert np.array_equal(a, ref[1]) and np.array_equal(y.view(np.uint32), ref[0].view(np.uint32))
+    want, want_acc = oracle.reference(q, qs, w, alpha)
+    _check(torch.from_numpy(ref[0]), ref[1], want, want_acc, 0)
+
+
 @pytest.mark.parametrize("config", [(128, 32, 1, 8), (128, 64, 2, 4), (128, 128, 4, 2), (128, 32, 4, 2),
                                     (128, 256, 8, 1), (128, 64, 1, 1)])
 @pytest.mark.parametrize("parts", [2, 3])
@@ -279,7 +366,7 @@ PAIR_SHAPES = [(256, 128, 257), (512, 2048, 300), (768, 136, 513), (256, 200, 70
 @pytest.mark.parametrize("out", [torch.float32, torch.float16])
 def test_pair_kernel_equals_oracle(wbits, n, k, m, out):
     """Ragged K (zero-filled boxes), ragged M (clipped stores), one to several tiles per pair of SMs."""
-    assert configs.choose(m, n, k, wbits, 1).pair == 1
+    assert configs.choose(m, n, k, wbits, 1).kernel == configs.PAIR
     seed = wbits * 977 + n + k + m
     codes, w = _codes(wbits, n, k, seed)
     q, qs = _activations(1, m, k, seed)

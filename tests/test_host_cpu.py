@@ -45,6 +45,14 @@ def test_every_shape_has_a_valid_config(n, k, wbits, parts):
     kb = -(-k // 128)
     for m in (1, 16, 38, 125, 126, 249, 256, 368, 400, 512, 1500, 2048, 8192, 32000):
         c = _lib.choose_config(m, n, k, wbits, parts)
+        assert (c.kernel == configs.GEMV) == (m * parts <= 4)
+        if c.kernel == configs.GEMV:   # the CUDA-core kernel: tile_m = the tokens, tile_n = channels per CTA
+            assert c.tile_m == m and c.tile_n in (8, 16, 32)
+            assert c.splits == 1 and 0 < c.smem_bytes <= 48 * 1024
+            cfg = configs.choose(m, n, k, wbits, parts)
+            cfg.validate(parts)
+            assert cfg.grid(m, n)[0] * cfg.tile_n >= n
+            continue
         assert c.tile_m in (128, 256) and c.tile_n in (32, 64, 128, 256)
         assert (c.tile_m // 128) * parts * c.tile_n <= 512
         assert 1 <= c.splits <= min(kb, 16) and 1 <= c.stages <= 8
