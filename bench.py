@@ -206,6 +206,8 @@ def main() -> None:
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--clip-batch", type=int, default=256, help="clips in the config-3 batch (sharded over ranks)")
     ap.add_argument("--no-clip", action="store_true", help="skip the clip workloads (shorter profiling runs)")
+    ap.add_argument("--kea-t-clips", type=int, default=1024,
+                    help="clips in the config-4 batch (2-bit, two parts, 2-30 s; 0 skips it)")
     ap.add_argument("--case", default=None, metavar="WBITS,N,K,M",
                     help="profiling mode: launch one GEMM case W + K times (rotating cold weights), print its timing")
     args = ap.parse_args()
@@ -338,6 +340,9 @@ def main() -> None:
     torch.cuda.empty_cache()
     clip = None if args.no_clip else clip_workloads(torch, dev, stream, rank, world, dist if world > 1 else None,
                                                      local, pdl, hbm_peak, args.clip_batch)
+    if clip is not None and args.kea_t_clips > 0:
+        clip["config4"] = kea_t_batch(torch, dev, stream, world, dist if world > 1 else None, local, pdl,
+                                      args.kea_t_clips)
 
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -511,6 +516,79 @@ def clip_workloads(torch, dev, stream, rank, world, dist, local, pdl, hbm_peak, 
         "lowbit_gop": gop, "encoder_lowbit_tops": gop / t / 1e3,
         "labels_gathered": len(res.tokens), "timing": "CUDA events on each rank's stream, max over ranks"}
     return out
+
+
+KEA_T_FRAMES_CAP = 32000   # padded encoder frames per forward (bounds the subsampling activations to ~10 GB)
+KEA_T_BUCKET = 32          # length-bucket width in encoder frames
+
+
+def kea_t_batch(torch, dev, stream, world, dist, local, pdl, n_clips):
+    """a Kea-T-shaped encoder (the same 24-layer FastConformer, 2-bit ternary weights, two
+    residual INT8 parts: Kea-T's default x2 mode) over `n_clips` synthetic clips whose lengths are uniform in
+    2-30 s (log-mel at 100 frames/s, N(0, 1)). Whole clips are sharded over the ranks by frame count; each rank sorts
+    its clips into length buckets KEA_T_BUCKET encoder frames wide, pads each bucket to its longest clip (masked as
+    attention keys and before the depthwise convolution) and runs it in forwards of at most KEA_T_FRAMES_CAP padded
+    frames. One untimed pass fills the per-length position-projection cache; the timed pass is bracketed by CUDA
+    events on the rank's stream, labels and timings gathered with NCCL, max over ranks."""
+    from kea_kernels import batch as B
+    from kea_kernels import encoder as E
+
+    g = torch.Generator().manual_seed(2024)
+    mel_frames = [int(v) for v in (200 + torch.rand(n_clips, generator=g) * 2800).long()]   # 2-30 s at 100 frames/s
+    enc = E.FastConformerEncoder(device=dev, wbits=2, parts=2, pdl=pdl, seed=9)
+    joint = E.TDTJoint(device=dev)
+    enc_frames = [enc.frames(t) for t in mel_frames]
+    dgen = torch.Generator(device=dev).manual_seed(4242)
+
+    def process(indices):
+        if not indices:
+            return [], 0.0
+        fr = [enc_frames[i] for i in indices]
+        work = []
+        for bucket in B.buckets(fr, range(KEA_T_BUCKET, max(fr) + KEA_T_BUCKET, KEA_T_BUCKET)):
+            if not bucket:
+                continue
+            ids = [indices[j] for j in bucket]                      # longest first
+            t_mel = mel_frames[ids[0]]
+            per = max(1, KEA_T_FRAMES_CAP // enc.frames(t_mel))
+            for s0 in range(0, len(ids), per):
+                sub = ids[s0:s0 + per]
+                mel = torch.zeros(len(sub), 128, t_mel, device=dev)
+                for j, i in enumerate(sub):
+                    mel[j, :, :mel_frames[i]].normal_(generator=dgen)
+                lengths = torch.tensor([enc_frames[i] for i in sub], device=dev)
+                work.append((sub, mel, lengths))
+        labels = {}
+        with torch.cuda.stream(stream):
+            for sub, mel, lengths in work:                          # untimed: position cache, allocator
+                joint.greedy(enc(mel, lengths))
+            stream.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            outs = [joint.greedy(enc(mel, lengths)) for _, mel, lengths in work]
+            e1.record(stream)
+            stream.synchronize()
+        for (sub, _, _), lab in zip(work, outs):
+            for j, i in enumerate(sub):
+                labels[i] = lab[j, :enc_frames[i]]
+        return [labels[i] for i in indices], e0.elapsed_time(e1) / 1e3
+
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+    res = B.run_batch(enc_frames, process, device=dev)
+    t = max(res.seconds)
+    total = sum(enc_frames)
+    ops = sum(2 * layer.lin[n].out_features * layer.lin[n].in_features * enc.parts
+              for layer in enc.layers for n in E.LAYER_LINEARS) * total / 1e9
+    return {"workload": f"BASELINE config 4: {n_clips} synthetic clips, lengths U[2, 30] s ({total} encoder frames, "
+                        f"{min(enc_frames)}-{max(enc_frames)} per clip), Kea-T-shaped random-init encoder (2-bit "
+                        f"ternary, x2 residual parts), sharded over {world} GPU(s) by frames, length buckets "
+                        f"{KEA_T_BUCKET} frames wide padded per bucket, <= {KEA_T_FRAMES_CAP} padded frames per "
+                        "forward; labels and timings gathered with NCCL",
+            "clips_per_s": n_clips / t, "frames_per_s": total / t, "ms_per_batch": t * 1e3,
+            "per_rank_ms": [v * 1e3 for v in res.seconds], "per_rank_frames": res.frames,
+            "lowbit_gop_unpadded": ops, "encoder_lowbit_tops_unpadded": ops / t / 1e3,
+            "labels_gathered": len(res.tokens), "timing": "CUDA events on each rank's stream, max over ranks"}
 
 
 # The reference's own per-GEMM times (RTX 5090, b1_dot with three residual INT8 parts, FP32 output, hot / cold):

@@ -146,7 +146,8 @@ class ConformerLayer(nn.Module):
             self._pos_cache[t] = p
         return p
 
-    def attention(self, x: Tensor) -> Tensor:
+    def attention(self, x: Tensor, keys: Tensor | None = None) -> Tensor:
+        """keys: optional bool [b, 1, 1, t], False at padded frames (masked out as keys)."""
         b, t, _ = x.shape
         qkv = self.lin["qkv"](x, norm=self.norms["att"]).view(b, t, 3, self.heads, self.dk)
         q, k, v = qkv.unbind(2)                                         # [b, t, h, dk]
@@ -155,20 +156,27 @@ class ConformerLayer(nn.Module):
         q_v = (q + self.pos_bias_v).transpose(1, 2)
         ac = torch.matmul(q_u, k.permute(0, 2, 3, 1))                   # [b, h, t, t]
         bd = rel_shift(torch.matmul(q_v, p.permute(1, 2, 0)))           # [b, h, t, t]
-        attn = torch.softmax((ac + bd) * (1.0 / math.sqrt(self.dk)), dim=-1)
+        scores = (ac + bd) * (1.0 / math.sqrt(self.dk))
+        if keys is not None:
+            scores = scores.masked_fill(~keys, float("-inf"))
+        attn = torch.softmax(scores, dim=-1)
         ctx = torch.matmul(attn, v.transpose(1, 2)).transpose(1, 2).reshape(b, t, self.d)
         return self.lin["out"](ctx)
 
-    def conv(self, x: Tensor) -> Tensor:
+    def conv(self, x: Tensor, frames: Tensor | None = None) -> Tensor:
+        """frames: optional [b, t, 1] of 1 at real frames, 0 at padding (zeroed before the depthwise conv)."""
         h = self.lin["pw1"](x, norm=self.norms["conv"])                 # [b, t, 2d]
-        h = F.glu(h, dim=-1).transpose(1, 2)                            # [b, d, t]
+        h = F.glu(h, dim=-1)
+        if frames is not None:
+            h = h * frames
+        h = h.transpose(1, 2)                                           # [b, d, t]
         h = F.conv1d(h, self.dw_weight, self.dw_bias, padding=self.kernel // 2, groups=self.d)
         return self.lin["pw2"](h.transpose(1, 2), input_silu=True)      # SiLU fused into the quantizer
 
-    def forward(self, x: Tensor) -> Tensor:
+    def forward(self, x: Tensor, keys: Tensor | None = None, frames: Tensor | None = None) -> Tensor:
         x = x + 0.5 * self.lin["ff1_down"](self.lin["ff1_up"](x, norm=self.norms["ff1"], silu=True))
-        x = x + self.attention(x)
-        x = x + self.conv(x)
+        x = x + self.attention(x, keys)
+        x = x + self.conv(x, frames)
         x = x + 0.5 * self.lin["ff2_down"](self.lin["ff2_up"](x, norm=self.norms["ff2"], silu=True))
         return self.norms["out"](x)
 
@@ -225,11 +233,19 @@ class FastConformerEncoder(nn.Module):
         return t
 
     @torch.inference_mode()
-    def forward(self, mel: Tensor) -> Tensor:
-        """mel FP32 [B, 128, T] -> encoder states FP32 [B, frames(T), d_model]."""
+    def forward(self, mel: Tensor, lengths: Tensor | None = None) -> Tensor:
+        """mel FP32 [B, 128, T] -> encoder states FP32 [B, frames(T), d_model]. With `lengths` (int [B], encoder
+        frames of each clip; the rest of its row is padding) padded frames are masked out as attention keys and
+        zeroed before the depthwise convolution, so a clip's real frames do not depend on the padding (the
+        length-bucketed batches of mixed-length clips)."""
         x = self.pre(mel)
+        keys = frames = None
+        if lengths is not None:
+            t = x.shape[1]
+            live = torch.arange(t, device=x.device)[None, :] < lengths.to(x.device)[:, None]   # [b, t]
+            keys, frames = live[:, None, None, :], live[:, :, None].to(x.dtype)
         for layer in self.layers:
-            x = layer(x)
+            x = layer(x, keys, frames)
         return x
 
     def gemm_shapes(self, batch: int, t: int) -> list[tuple[str, int, int, int]]:

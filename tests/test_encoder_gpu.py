@@ -100,3 +100,22 @@ def test_joint_greedy_labels():
     lab = joint.greedy(enc)
     assert lab.shape == (3, 125) and lab.dtype == torch.int32
     assert int(lab.min()) >= 0 and int(lab.max()) <= 1024
+
+
+@torch.inference_mode()
+def test_padded_bucket_matches_clip_alone():
+    """Config 4's length buckets: a short clip padded to its bucket's longest clip (padding masked as attention
+    keys and zeroed before the depthwise conv) gives its own frames as when run alone."""
+    enc = E.FastConformerEncoder(layers=2, wbits=2, parts=3, seed=4, device=DEV)
+    g = torch.Generator().manual_seed(5)
+    long_mel, short_mel = torch.randn(1, 128, 400, generator=g), torch.randn(1, 128, 288, generator=g)
+    batch = torch.zeros(2, 128, 400)
+    batch[0], batch[1, :, :288] = long_mel[0], short_mel[0]
+    lengths = torch.tensor([enc.frames(400), enc.frames(288)])
+    y = enc(batch.to(DEV), lengths.to(DEV))
+    alone_short, alone_long = enc(short_mel.to(DEV))[0], enc(long_mel.to(DEV))[0]
+    n = int(lengths[1])
+    assert alone_short.shape[0] == n
+    for got, want in ((y[1, :n], alone_short), (y[0], alone_long)):
+        rel = ((got - want).norm() / want.norm()).item()
+        assert rel < 2e-4, rel
