@@ -119,6 +119,26 @@ KEA_DEVI float round_quotient(float v, float s, float inv) {
     return rintf(__fdiv_rn(v, s));
 }
 
+// Four codes rint(e[j] / s) (the IEEE quotient, as round_quotient) packed little-endian into a word; r[j] gets the
+// codes as floats. Branch-free on the common path: the four products e[j] * RN(1 / s) are rounded together and one
+// flag records whether any lies within 1e-4 of a half-integer (or is not a number); only then are the four redone
+// with the exact division.
+KEA_DEVI uint32_t quantize4(const float *e, float s, float inv, float (&r)[4]) {
+    bool odd = false;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float t = __fmul_rn(e[j], inv);
+        r[j] = rintf(t);
+        odd |= !(fabsf(__fsub_rn(t, r[j])) < 0.4999f);
+    }
+    if (odd) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) r[j] = rintf(__fdiv_rn(e[j], s));
+    }
+    const int b0 = __float2int_rn(r[0]), b1 = __float2int_rn(r[1]), b2 = __float2int_rn(r[2]), b3 = __float2int_rn(r[3]);
+    return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
 // The register-resident quantizer for unit-stride rows (xk == 1, K a multiple of 4, 16-byte aligned rows): `tpr`
 // threads per row (32 .. 256, 256 / tpr rows per CTA), each holding VPT = K / tpr (rounded up to 4) values as float4
 // chunks at (c * tpr + thread) * 4, so every load and store is a coalesced 16-byte vector. LayerNorm takes two
@@ -145,14 +165,6 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_regs_kernel(const Quan
         v[c] = (live && 4 * i < K) ? __ldg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (a.nw) {
-        float4 w[C], b[C];
-#pragma unroll
-        for (int c = 0; c < C; ++c) {
-            const int i = c * tpr + gt;
-            const bool in = 4 * i < K;
-            w[c] = in ? __ldg(reinterpret_cast<const float4 *>(a.nw) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-            b[c] = (in && a.nb) ? __ldg(reinterpret_cast<const float4 *>(a.nb) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
         float s = 0.f;
 #pragma unroll
         for (int c = 0; c < C; ++c) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[c].x), v[c].y), v[c].z), v[c].w);
@@ -167,12 +179,18 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_regs_kernel(const Quan
             }
         }
         const float inv = rsqrtf(__fadd_rn(__fdiv_rn(group_reduce(var, false, tpr, scratch), (float)K), a.eps));
+        // the affine parameters are read here, chunk by chunk, not held for the whole row (registers)
 #pragma unroll
         for (int c = 0; c < C; ++c) {
-            v[c].x = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].x, mean), inv), w[c].x, b[c].x);
-            v[c].y = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].y, mean), inv), w[c].y, b[c].y);
-            v[c].z = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].z, mean), inv), w[c].z, b[c].z);
-            v[c].w = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].w, mean), inv), w[c].w, b[c].w);
+            const int i = c * tpr + gt;
+            if (4 * i < K) {
+                const float4 w = __ldg(reinterpret_cast<const float4 *>(a.nw) + i);
+                const float4 b = a.nb ? __ldg(reinterpret_cast<const float4 *>(a.nb) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[c].x = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].x, mean), inv), w.x, b.x);
+                v[c].y = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].y, mean), inv), w.y, b.y);
+                v[c].z = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].z, mean), inv), w.z, b.z);
+                v[c].w = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].w, mean), inv), w.w, b.w);
+            }
         }
     }
     if (a.flags & 1) {
@@ -184,35 +202,37 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_regs_kernel(const Quan
             v[c].w = __fdiv_rn(v[c].w, __fadd_rn(1.0f, expf(-v[c].w)));
         }
     }
-    for (int p = 0; p < a.parts; ++p) {
-        float amax = 0.f;
+    float amax = 0.f;
 #pragma unroll
-        for (int c = 0; c < C; ++c)
-            if (4 * (c * tpr + gt) < K)
-                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c].x), fabsf(v[c].y)), fmaxf(fabsf(v[c].z), fabsf(v[c].w))));
+    for (int c = 0; c < C; ++c)
+        if (4 * (c * tpr + gt) < K)
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c].x), fabsf(v[c].y)), fmaxf(fabsf(v[c].z), fabsf(v[c].w))));
+    for (int p = 0; p < a.parts; ++p) {
         amax = group_reduce(amax, true, tpr, scratch);
         const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1.0e-30f);
         const float rcp = __frcp_rn(scale);
-        if (live) {
-            uint32_t *q = reinterpret_cast<uint32_t *>(a.q + p * a.q_stride + (long long)m * a.ldq);
+        float next = 0.f;   // the residual's amax: the next part's scale
+        uint32_t *q = reinterpret_cast<uint32_t *>(a.q + p * a.q_stride + (long long)m * a.ldq);
 #pragma unroll
-            for (int c = 0; c < C; ++c) {
-                const int i = c * tpr + gt;
-                if (4 * i < K) {
-                    float *e = reinterpret_cast<float *>(&v[c]);
-                    uint32_t word = 0;
+        for (int c = 0; c < C; ++c) {
+            const int i = c * tpr + gt;
+            if (4 * i < K) {
+                float *e = reinterpret_cast<float *>(&v[c]);
+                float r[4];
+                const uint32_t word = quantize4(e, scale, rcp, r);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float r = round_quotient(e[j], scale, rcp);
-                        word |= ((uint32_t)(int)r & 0xFFu) << (8 * j);
-                        e[j] = __fsub_rn(e[j], __fmul_rn(r, scale));
-                    }
-                    q[i] = word;
+                for (int j = 0; j < 4; ++j) {
+                    e[j] = __fsub_rn(e[j], __fmul_rn(r[j], scale));
+                    next = fmaxf(next, fabsf(e[j]));
                 }
+                if (live) q[i] = word;
             }
+        }
+        if (live) {
             for (int i = K / 4 + gt; i < a.ldq / 4; i += tpr) q[i] = 0u;   // padding columns
             if (gt == 0) a.qs[p * a.qs_stride + m] = scale;
         }
+        amax = next;
     }
     grid_launch_dependents();
 }
@@ -307,12 +327,10 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantArgs
                 if (vec && 4 * w < K) {
                     float4 v4 = reinterpret_cast<const float4 *>(row)[w];
                     float *v = reinterpret_cast<float *>(&v4);
+                    float r[4];
+                    word = quantize4(v, scale, inv, r);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float r = round_quotient(v[j], scale, inv);
-                        word |= ((uint32_t)(int)r & 0xFFu) << (8 * j);
-                        v[j] = __fsub_rn(v[j], __fmul_rn(r, scale));
-                    }
+                    for (int j = 0; j < 4; ++j) v[j] = __fsub_rn(v[j], __fmul_rn(r[j], scale));
                     reinterpret_cast<float4 *>(row)[w] = v4;
                 } else {
 #pragma unroll
