@@ -262,6 +262,10 @@ KEA_DEVI void load_acc16(uint32_t lane_addr, int blk, int nacc, int TN, int c, u
         tmem_ld16(lane_addr + col + (uint32_t)(2 * TN), w2);
         tmem_ld16(lane_addr + col + (uint32_t)(3 * TN), w3);
         tmem_wait_ld();
+        tmem_regs_ready(v);
+        tmem_regs_ready(w1);
+        tmem_regs_ready(w2);
+        tmem_regs_ready(w3);
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = v[j] + w1[j] + w2[j] + w3[j];
     }
@@ -650,6 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                     uint32_t v[16];
                     load_acc16(lane_addr, 0, a.nacc, TN, ch * 16, v);
                     tmem_wait_ld();
+                    tmem_regs_ready(v);
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
                         st_shared_v4(xs + (uint32_t)((row * ld + ch * 16 + 4 * q) * 4), v[4 * q], v[4 * q + 1],
@@ -698,6 +703,8 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
 #pragma unroll
                         for (int p = 0; p < P; ++p) load_acc16(lane_addr, tb * P + p, a.nacc, TN, c, v[p]);
                         tmem_wait_ld();
+#pragma unroll
+                        for (int p = 0; p < P; ++p) tmem_regs_ready(v[p]);
                         float f[16];
 #pragma unroll
                         for (int j = 0; j < 16; ++j)
@@ -756,6 +763,8 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
 #pragma unroll
                         for (int p = 0; p < P; ++p) load_acc16(lane_addr, tb * P + p, a.nacc, TN, c, v[p]);
                         tmem_wait_ld();
+#pragma unroll
+                        for (int p = 0; p < P; ++p) tmem_regs_ready(v[p]);
                         if (t < a.M && n0 + c < a.N) {
                             int accv[P][16];
 #pragma unroll
@@ -788,6 +797,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                     if (done) {
                         load_acc16(lane_addr, blk, a.nacc, TN, ch * 16, v);
                         tmem_wait_ld();
+                        tmem_regs_ready(v);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 16; ++j) v[j] = 0;

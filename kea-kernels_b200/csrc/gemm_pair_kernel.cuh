@@ -1,5 +1,5 @@
 // gemm_pair_kernel.cuh - the large-M low-bit GEMM for sm_100a: a persistent kernel on CTA pairs (tcgen05
-// cta_group::2), one INT8 activation part.
+// cta_group::2), one or two residual INT8 activation parts.
 //
 // A pair tile is 256 tokens x 256 channels. The even CTA of a thread-block cluster of two holds tokens 0-127 of the
 // tile and channel rows 0-127 (one panel tile); the odd CTA holds tokens 128-255 and channel rows 128-255. Each CTA
@@ -9,20 +9,23 @@
 // which keeps shared memory under its bandwidth at the INT8 rate. The even CTA issues tcgen05.mma.cta_group::2
 // (M = 256, N = 256) for both; each CTA's tensor memory receives its 128 token rows x 256 channels.
 //
-// The pairs walk the tile list persistently (pair p takes tiles p, p + pairs, ...). Tensor memory holds two
-// 256-column accumulator buffers, so the epilogue of tile i (8 warps per CTA) runs while the MMAs of tile i + 1
-// accumulate into the other buffer.
+// The pairs walk the tile list persistently (pair p takes tiles p, p + pairs, ...). With one part, tensor memory
+// holds two 256-column accumulator buffers, so the epilogue of tile i (8 warps per CTA) runs while the MMAs of tile
+// i + 1 accumulate into the other buffer. With two parts (P = 2) every load slot holds both parts' activation boxes,
+// each expanded weight tile serves both parts' MMAs (one accumulator of 256 columns per part), and the 512 columns
+// are one buffer: the next tile's MMAs wait for the epilogue. (A 128-channel tile would keep two buffers, but its
+// operand traffic per MAC would take shared memory past its bandwidth.)
 //
 // Warps per CTA (512 threads):
-//   warp 0       producer: per k-block one TMA box of activations (128 tokens x 128 k, 128-byte swizzle) and one bulk
-//                copy of the packed codes (128 channel rows x 128 k), on this CTA's `full` barrier;
+//   warp 0       producer: per k-block P TMA boxes of activations (128 tokens x 128 k of each part, 128-byte
+//                swizzle) and one bulk copy of the packed codes (128 channel rows x 128 k), on this CTA's `full` barrier;
 //   warp 1       allocates tensor memory for the pair; in the even CTA one elected lane issues the MMAs, frees each
 //                stage in both CTAs (tcgen05.commit to both CTAs' `empty`) and hands finished accumulators to both
 //                CTAs' epilogues (`acc_full`);
 //   warps 2-7    expanders, two groups of three warps taking alternate k-blocks: packed codes -> INT8 +-1 / -1 0 +1
 //                in the 128-byte-swizzled K-major B tile, then arrive on the even CTA's `ready` barrier (6 warp
 //                arrivals: the stage is complete in both CTAs);
-//   warps 8-15   epilogue: TMEM -> comb_1 * alpha (+ bias) (SiLU) -> FP32 / FP16, staged in shared memory and written
+//   warps 8-15   epilogue: TMEM -> comb_P * alpha (+ bias) (SiLU) -> FP32 / FP16, staged in shared memory and written
 //                with TMA stores; then release the buffer (`acc_empty` of the even CTA, 16 warp arrivals).
 // Every wait is bounded (kWaitBudget); on expiry the kernel reports KEA_DEVERR_TIMEOUT, lets its copies and MMAs
 // drain, and returns.
@@ -50,14 +53,15 @@ constexpr uint32_t kPairChannelBytes = kPairEpiWarps * 1024;                // a
 
 struct PairArgs {
     const uint8_t *panels;
-    const float *qs;             // FP32 [m] token scales
+    const float *qs;             // FP32 [P][m] token scales
+    long long qs_stride;         // elements between parts of qs
     const float *alpha;          // FP32 [n]
     const float *bias;           // FP32 [n] or null
-    int *acc;                    // optional INT32 [m][ld_acc]
-    long long ld_acc;
+    int *acc;                    // optional INT32 [P][m][ld_acc]
+    long long ld_acc, acc_stride;
     int M, N, K, kb_total;
     int n_tiles, tiles;          // 256-channel tiles, pair tiles in all
-    int flags;                   // KEA_FLAG_SILU
+    int flags;                   // KEA_FLAG_SILU, KEA_FLAG_ORDER1
     int pdl;
     int y_f16;
     int stages;
@@ -92,6 +96,16 @@ KEA_DEVI float finish1(int acc, float s, float alpha, float bias) {
     return y;
 }
 
+// comb_2 (order 0: fma(a0, s0, a1 * s1); order 1: fma(a1, s1, a0 * s0), the caller passing the parts swapped),
+// alpha / bias, optional SiLU: one IEEE FP32 rounding per operation.
+template <bool BIAS, bool SILU>
+KEA_DEVI float finish2(int lo, int hi, float s_lo, float s_hi, float alpha, float bias) {
+    const float r = __fmaf_rn(int_to_float_exact(lo), s_lo, __fmul_rn(int_to_float_exact(hi), s_hi));
+    float y = BIAS ? __fmaf_rn(r, alpha, bias) : __fmul_rn(r, alpha);
+    if constexpr (SILU) y = silu_approx(y);
+    return y;
+}
+
 // One epilogue warp's share of a finished tile: its 32 token rows x 128 channels of tensor memory in four chunks of
 // 32 columns. The TMEM load of chunk i + 1 is in flight while chunk i is finished in registers (alpha / bias from the
 // warp's shared-memory copy). A chunk is 2 KB of FP16 output (one 32 x 64-byte box) or 4 KB of FP32 (two boxes);
@@ -117,6 +131,31 @@ KEA_DEVI void pair_finish_chunk(uint32_t (&v)[32], uint32_t s_al, uint32_t s_bi,
             v[jj + 1] = __float_as_uint(f1);
             v[jj + 2] = __float_as_uint(f2);
             v[jj + 3] = __float_as_uint(f3);
+        }
+    }
+}
+
+// comb_2 of one chunk: the order-0 lower part in lo, the other in hi (swapped by the caller for order 1); the
+// results replace lo as in pair_finish_chunk.
+template <bool F16, bool BIAS, bool SILU>
+KEA_DEVI void pair_finish_chunk2(uint32_t (&lo)[32], const uint32_t (&hi)[32], uint32_t s_al, uint32_t s_bi, int c,
+                                 float s_lo, float s_hi) {
+#pragma unroll
+    for (int jj = 0; jj < 32; jj += 4) {
+        const uint4 alu = ld_shared_v4(s_al + (uint32_t)(c + jj) * 4u);
+        uint4 biu = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (BIAS) biu = ld_shared_v4(s_bi + (uint32_t)(c + jj) * 4u);
+        float f[4];
+        const float al[4] = {__uint_as_float(alu.x), __uint_as_float(alu.y), __uint_as_float(alu.z), __uint_as_float(alu.w)};
+        const float bi[4] = {__uint_as_float(biu.x), __uint_as_float(biu.y), __uint_as_float(biu.z), __uint_as_float(biu.w)};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) f[u] = finish2<BIAS, SILU>((int)lo[jj + u], (int)hi[jj + u], s_lo, s_hi, al[u], bi[u]);
+        if constexpr (F16) {
+            lo[jj / 2] = pack_half2(f[0], f[1]);
+            lo[jj / 2 + 1] = pack_half2(f[2], f[3]);
+        } else {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) lo[jj + u] = __float_as_uint(f[u]);
         }
     }
 }
@@ -170,6 +209,7 @@ KEA_DEVI void pair_epilogue_tile(const PairArgs &a, const CUtensorMap *ymap, uin
         // chunk ci in va; chunk ci + 1 into vb while va is finished
         KEA_PTRACE(tr, 10, j * 4 + ci);
         tmem_wait_ld();
+        tmem_regs_ready(va);
         KEA_PTRACE(tr, 11, j * 4 + ci);
         pair_load32(cbase + (uint32_t)(32 * (ci + 1)), vb);
         if (a.acc && t < a.M) {
@@ -183,6 +223,7 @@ KEA_DEVI void pair_epilogue_tile(const PairArgs &a, const CUtensorMap *ymap, uin
         KEA_PTRACE(tr, 13, j * 4 + ci);
         // chunk ci + 1 in vb; chunk ci + 2 into va
         tmem_wait_ld();
+        tmem_regs_ready(vb);
         if (ci + 2 < 4) {
             pair_load32(cbase + (uint32_t)(32 * (ci + 2)), va);
         } else {   // every TMEM read of the buffer is done: hand it back to the MMA warp
@@ -200,7 +241,45 @@ KEA_DEVI void pair_epilogue_tile(const PairArgs &a, const CUtensorMap *ymap, uin
     }
 }
 
-template <int WBITS>
+// Two parts: per chunk both parts' 32 columns are loaded together (part 1 lies 256 columns on), finished and stored;
+// the buffer is released after the last chunk's loads.
+template <bool F16, bool BIAS, bool SILU>
+KEA_DEVI void pair_epilogue_tile2(const PairArgs &a, const CUtensorMap *ymap, uint32_t cbase, uint32_t stg,
+                                  uint32_t s_al, uint32_t s_bi, uint32_t acc_empty, int nbase, int trow0, int t,
+                                  float s0, float s1, bool order1) {
+    const int lane = threadIdx.x & 31;
+    // lo = the part whose product is the fma's first operand (part 0 for order 0, part 1 for order 1)
+    const uint32_t col_lo = order1 ? kPairAccCols : 0u, col_hi = order1 ? 0u : kPairAccCols;
+    const long long acc_lo = order1 ? a.acc_stride : 0LL, acc_hi = order1 ? 0LL : a.acc_stride;
+    const float s_lo = order1 ? s1 : s0, s_hi = order1 ? s0 : s1;
+    uint32_t v0[32], v1[32];
+#pragma unroll 1
+    for (int ci = 0; ci < 4; ++ci) {
+        pair_load32(cbase + col_lo + (uint32_t)(32 * ci), v0);
+        pair_load32(cbase + col_hi + (uint32_t)(32 * ci), v1);
+        tmem_wait_ld();
+        tmem_regs_ready(v0);
+        tmem_regs_ready(v1);
+        if (ci == 3) {   // every TMEM read of the buffer is done: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc_empty);
+        }
+        if (a.acc && t < a.M) {
+            int4 *d0 = reinterpret_cast<int4 *>(a.acc + acc_lo + (long long)t * a.ld_acc + nbase + 32 * ci);
+            int4 *d1 = reinterpret_cast<int4 *>(a.acc + acc_hi + (long long)t * a.ld_acc + nbase + 32 * ci);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                d0[q] = make_int4((int)v0[4 * q], (int)v0[4 * q + 1], (int)v0[4 * q + 2], (int)v0[4 * q + 3]);
+                d1[q] = make_int4((int)v1[4 * q], (int)v1[4 * q + 1], (int)v1[4 * q + 2], (int)v1[4 * q + 3]);
+            }
+        }
+        pair_finish_chunk2<F16, BIAS, SILU>(v0, v1, s_al, s_bi, 32 * ci, s_lo, s_hi);
+        pair_stage_and_store<F16>(ymap, v0, stg, ci, nbase + 32 * ci, trow0);
+    }
+}
+
+template <int WBITS, int P>
 __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                           const __grid_constant__ CUtensorMap ymap,
                                                                           const PairArgs a) {
@@ -219,12 +298,14 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
     const uint32_t rank = cluster_ctarank();
     const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
     const uint32_t base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
-    // Shared memory: [activation boxes: S x 16 KB][B tiles: kPairBStages x 16 KB][packed codes: S x PKB][epilogue
+    // Shared memory: [activation boxes: S x P x 16 KB][B tiles: kPairBStages x 16 KB][packed codes: S x PKB][epilogue
     // staging][channel constants]. Load slot s (activations + codes) and B slot b turn over independently: a k-block
     // step i uses load slot i % S and B slot i % kPairBStages, so the loads run S steps ahead of the MMAs while only
     // a few expanded tiles are kept.
+    constexpr uint32_t ASLOT = (uint32_t)P * kPairHalfTile;
+    constexpr int NBUF = P == 1 ? 2 : 1;   // accumulator buffers
     const int S = a.stages;
-    const uint32_t A0 = base, B0 = base + (uint32_t)S * kPairHalfTile;
+    const uint32_t A0 = base, B0 = base + (uint32_t)S * ASLOT;
     const uint32_t PK0 = B0 + (uint32_t)kPairBStages * kPairHalfTile;
     const uint32_t STG0 = (PK0 + (uint32_t)S * PKB + 1023u) & ~1023u;
     const int kbt = a.kb_total;
@@ -275,7 +356,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
             int s = 0;
             uint32_t ph = 0;
             long long issued = 0;
-            const uint32_t tx = kPairHalfTile + PKB;
+            const uint32_t tx = ASLOT + PKB;
             for (int tile = pair; tile < a.tiles && ok; tile += npairs) {
                 const int mt = tile / a.n_tiles, nt = tile - mt * a.n_tiles;
                 const int t0 = mt * kPairTileM + (int)rank * kBM;
@@ -288,7 +369,9 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                     KEA_PTRACE(true, 0, issued);
                     const uint32_t full = smem_u32(&bar_full[s]);
                     mbar_arrive_expect_tx(full, tx);
-                    tma_load_2d(A0 + (uint32_t)s * kPairHalfTile, &qmap, full, kb * kBK, t0);
+#pragma unroll
+                    for (int p = 0; p < P; ++p)   // (k, token, part) boxes
+                        tma_load_3d(A0 + (uint32_t)s * ASLOT + (uint32_t)p * kPairHalfTile, &qmap, full, kb * kBK, t0, p);
                     bulk_load(PK0 + (uint32_t)s * PKB, wsrc + (size_t)kb * PKB, PKB, full);
                     ++issued;
                     if (++s == S) {
@@ -311,9 +394,9 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
             const uint64_t ad0 = sw128_kmajor_desc(A0), bd0 = sw128_kmajor_desc(B0);
             int j = 0, step = 0;
             for (int tile = pair; tile < a.tiles; tile += npairs, ++j) {
-                const int buf = j & 1;
-                const uint32_t use = (uint32_t)(j >> 1);
-                if (j >= 2) {
+                const int buf = j % NBUF;
+                const uint32_t use = (uint32_t)(j / NBUF);
+                if (j >= NBUF) {
                     const bool drained = mbar_wait_cluster(smem_u32(&bar_acc_empty[buf]), (use & 1u) ^ 1u, kWaitBudget);
                     if (!__all_sync(0xFFFFFFFFu, drained)) {
                         ok = false;
@@ -331,13 +414,16 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                         break;
                     }
                     KEA_PTRACE(lane == 0, 3, step);
-                    const uint64_t ad = ad0 + (uint64_t)(((uint32_t)sa * kPairHalfTile) >> 4);
+                    const uint64_t ad = ad0 + (uint64_t)(((uint32_t)sa * ASLOT) >> 4);
                     const uint64_t bd = bd0 + (uint64_t)(((uint32_t)sb * kPairHalfTile) >> 4);
                     if (elect_one()) {
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)   // K = 32 per MMA: + 32 bytes = 2 descriptor units
-                            mma_i8_pair(dcol, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                        (kb > 0 || kk > 0) ? 1u : 0u);
+                        for (int p = 0; p < P; ++p)       // part p: its box, its 256 accumulator columns
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk)   // K = 32 per MMA: + 32 bytes = 2 descriptor units
+                                mma_i8_pair(dcol + (uint32_t)p * kPairAccCols,
+                                            ad + (uint64_t)((p * kPairHalfTile) >> 4) + (uint64_t)(kk * 2),
+                                            bd + (uint64_t)(kk * 2), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                         mma_commit_pair(smem_u32(&bar_empty[sa]), (uint16_t)3);
                         mma_commit_pair(smem_u32(&bar_bempty[sb]), (uint16_t)3);
                     }
@@ -368,10 +454,14 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
         const int steps = my_tiles * kbt;
         for (int step = eg; step < steps; step += kPairExpGroups) {
             const int sa = step % S, sb = step % kPairBStages;
-            // the codes have landed, and the MMAs that last read B slot sb (step - kPairBStages) are done
-            bool free = mbar_wait(smem_u32(&bar_full[sa]), (uint32_t)((step / S) & 1), kWaitBudget);
+            // The MMAs that last read B slot sb (step - kPairBStages) are done, then the codes have landed. The order
+            // matters: a parity wait on `full` is unambiguous only once the slot's previous fill (step - S) has
+            // completed. The MMAs of step - kPairBStages imply every fill up to that step, which covers step - S
+            // when S >= kPairBStages; otherwise step - S was this group's own earlier step (S = 2), already waited.
+            bool free = true;
             if (step >= kPairBStages)
-                free = free && mbar_wait(smem_u32(&bar_bempty[sb]), (uint32_t)(((step / kPairBStages) & 1) ^ 1), kWaitBudget);
+                free = mbar_wait(smem_u32(&bar_bempty[sb]), (uint32_t)(((step / kPairBStages) & 1) ^ 1), kWaitBudget);
+            free = free && mbar_wait(smem_u32(&bar_full[sa]), (uint32_t)((step / S) & 1), kWaitBudget);
             if (!__all_sync(0xFFFFFFFFu, free)) {
                 ok = false;
                 if (lane == 0) report(a.err, 1u);
@@ -400,8 +490,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
         const bool has_bias = a.bias != nullptr;
         int j = 0;
         for (int tile = pair; tile < a.tiles; tile += npairs, ++j) {
-            const int buf = j & 1;
-            const uint32_t use = (uint32_t)(j >> 1);
+            const int buf = j % NBUF;
+            const uint32_t use = (uint32_t)(j / NBUF);
             const int mt = tile / a.n_tiles, nt = tile - mt * a.n_tiles;
             const int trow0 = mt * kPairTileM + (int)rank * kBM + quad * 32;
             const int t = trow0 + lane;
@@ -427,12 +517,17 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
             tc_fence_after();
             KEA_PTRACE(ew == 0 && lane == 0, 5, j);
             const float sq = t < a.M ? __ldg(a.qs + t) : 0.f;
+            const float sq1 = (P > 1 && t < a.M) ? __ldg(a.qs + a.qs_stride + t) : 0.f;
             const uint32_t cbase = lane_base + (uint32_t)buf * kPairAccCols + (uint32_t)(half * 128);
             const uint32_t acc_empty = acc_empty0 + (uint32_t)buf * 8u;
             // one instantiation per (output type, bias, SiLU): no run-time branch inside the finishing loop
             const int variant = (a.y_f16 ? 4 : 0) | (has_bias ? 2 : 0) | (a.flags & 1);
 #define KEA_PAIR_EPI(F16, BIAS, SILU)                                                                             \
-    pair_epilogue_tile<F16, BIAS, SILU>(a, &ymap, cbase, stg, s_al, s_bi, acc_empty, nbase, trow0, t, sq, j)
+    if constexpr (P == 1)                                                                                         \
+        pair_epilogue_tile<F16, BIAS, SILU>(a, &ymap, cbase, stg, s_al, s_bi, acc_empty, nbase, trow0, t, sq, j); \
+    else                                                                                                          \
+        pair_epilogue_tile2<F16, BIAS, SILU>(a, &ymap, cbase, stg, s_al, s_bi, acc_empty, nbase, trow0, t, sq, sq1, \
+                                             (a.flags & 2) != 0)
             switch (variant) {
                 case 0: KEA_PAIR_EPI(false, false, false); break;
                 case 1: KEA_PAIR_EPI(false, false, true); break;

@@ -78,8 +78,10 @@ int device_setup(int *device_out) {
                 cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
                 status = KEA_ERR_CUDA;
         }
-        const void *pair_kernels[2] = {(const void *)kea::lowbit_gemm_pair_kernel<1>,
-                                       (const void *)kea::lowbit_gemm_pair_kernel<2>};
+        const void *pair_kernels[4] = {(const void *)kea::lowbit_gemm_pair_kernel<1, 1>,
+                                       (const void *)kea::lowbit_gemm_pair_kernel<2, 1>,
+                                       (const void *)kea::lowbit_gemm_pair_kernel<1, 2>,
+                                       (const void *)kea::lowbit_gemm_pair_kernel<2, 2>};
         for (const void *k : pair_kernels)
             if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairMaxDynSmem) != cudaSuccess)
                 status = KEA_ERR_CUDA;
@@ -157,22 +159,23 @@ int max_stages(int tile_m, int tile_n, int parts, int wbits) {
 // ---- the persistent CTA-pair kernel (gemm_pair_kernel.cuh) ---------------------------------------------------------
 // Dynamic shared memory: alignment slack + load slots x (activation box + packed codes) + the B slots + epilogue
 // staging + channel constants.
-int pair_stage_bytes(int wbits) { return (int)kea::kPairHalfTile + wbits * kea::kPanelSubBytes; }
-int pair_smem_bytes(int wbits, int stages) {
-    return 1024 + stages * pair_stage_bytes(wbits) + kea::kPairBStages * (int)kea::kPairHalfTile +
+int pair_stage_bytes(int wbits, int parts) { return parts * (int)kea::kPairHalfTile + wbits * kea::kPanelSubBytes; }
+int pair_smem_bytes(int wbits, int parts, int stages) {
+    return 1024 + stages * pair_stage_bytes(wbits, parts) + kea::kPairBStages * (int)kea::kPairHalfTile +
            (int)kea::kPairStagingBytes + (int)kea::kPairChannelBytes;
 }
-int pair_max_stages(int wbits) {
+int pair_max_stages(int wbits, int parts) {
     int s = kea::kPairMaxStages;
-    while (s > 2 && pair_smem_bytes(wbits, s) > kPairMaxDynSmem) --s;
+    while (s > 2 && pair_smem_bytes(wbits, parts, s) > kPairMaxDynSmem) --s;
     return s;
 }
-// The pair kernel takes one activation part and whole 256-channel tiles; above this many tokens it replaces the
-// per-tile kernel (its 256 x 256 pair tiles keep the shared-memory traffic per MAC at half the per-tile kernel's).
+// The pair kernel takes one or two activation parts and whole 256-channel tiles; above this many tokens it replaces
+// the per-tile kernel (its 256 x 256 pair tiles keep the shared-memory traffic per MAC at half the per-tile
+// kernel's).
 constexpr int kPairMinM = 257;
 // K <= 32768 keeps |acc| <= 127 K below 2^22, where the epilogue's two-operation INT32 -> FP32 conversion is exact.
 bool pair_shape(int m, int n, int k, int parts) {
-    return parts == 1 && n % kea::kPairTileN == 0 && m >= kPairMinM && k <= 32768;
+    return parts <= 2 && n % kea::kPairTileN == 0 && m >= kPairMinM && k <= 32768;
 }
 
 // The M-bucketed split-K dispatch table (B200, 148 SMs).
@@ -273,8 +276,8 @@ KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
         c.tile_m = kea::kPairTileM;
         c.tile_n = kea::kPairTileN;
         c.splits = 1;
-        c.stages = pair_max_stages(wbits);
-        c.smem_bytes = pair_smem_bytes(wbits, c.stages);
+        c.stages = pair_max_stages(wbits, parts);
+        c.smem_bytes = pair_smem_bytes(wbits, parts, c.stages);
         c.kernel = 1;
     }
     if (m * parts <= kGemvTableRows && gemv_fits(m, parts, gemv_channels(n, k, wbits, m, parts))) {
@@ -386,16 +389,18 @@ int launch_gemv(const KeaGemmDesc *d, const KeaGemmConfig &c, void *stream) {
 int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *stream) {
     const int esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
     if (!aligned16(d->y) || (d->ldy * esize) % 16 || !aligned16(d->alpha) || (d->bias && !aligned16(d->bias)) ||
-        (d->acc && (!aligned16(d->acc) || d->ld_acc % 4)))
+        (d->acc && (!aligned16(d->acc) || d->ld_acc % 4 || (d->parts > 1 && d->acc_part_stride % 4))))
         return KEA_ERR_UNSUPPORTED;
-    // Activations: 2-D (k, row) with 128 x 128 boxes in the 128-byte swizzle; columns >= k and rows >= m read as 0.
+    // Activations: 3-D (k, row, part) with 128 x 128 x 1 boxes in the 128-byte swizzle; columns >= k and rows >= m
+    // read as 0.
     CUtensorMap qmap, ymap;
     {
-        const cuuint64_t dims[2] = {(cuuint64_t)d->k, (cuuint64_t)d->m};
-        const cuuint64_t strides[1] = {(cuuint64_t)d->ldq};
-        const cuuint32_t box[2] = {(cuuint32_t)kea::kBK, (cuuint32_t)kea::kBM};
-        const cuuint32_t estr[2] = {1, 1};
-        if (g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(d->q), dims, strides, box, estr,
+        const long long pstride = d->parts > 1 ? d->q_part_stride : (long long)d->m * d->ldq;
+        const cuuint64_t dims[3] = {(cuuint64_t)d->k, (cuuint64_t)d->m, (cuuint64_t)d->parts};
+        const cuuint64_t strides[2] = {(cuuint64_t)d->ldq, (cuuint64_t)pstride};
+        const cuuint32_t box[3] = {(cuuint32_t)kea::kBK, (cuuint32_t)kea::kBM, 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        if (g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t *>(d->q), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return KEA_ERR_CUDA;
@@ -414,17 +419,19 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
     kea::PairArgs a{};
     a.panels = d->panels;
     a.qs = d->qs;
+    a.qs_stride = d->qs_part_stride;
     a.alpha = d->alpha;
     a.bias = d->bias;
     a.acc = d->acc;
     a.ld_acc = d->ld_acc;
+    a.acc_stride = d->acc_part_stride;
     a.M = d->m;
     a.N = d->n;
     a.K = d->k;
     a.kb_total = ceil_div(d->k, kea::kBK);
     a.n_tiles = d->n / kea::kPairTileN;
     a.tiles = a.n_tiles * ceil_div(d->m, kea::kPairTileM);
-    a.flags = d->flags & KEA_FLAG_SILU;
+    a.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
     a.pdl = (d->flags & KEA_FLAG_PDL) ? 1 : 0;
     a.y_f16 = esize == 2;
     a.stages = c.stages;
@@ -450,8 +457,13 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
     }
     cfg.attrs = attrs;
     cfg.numAttrs = na;
-    const cudaError_t e = d->wbits == 1 ? cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<1>, qmap, ymap, a)
-                                        : cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<2>, qmap, ymap, a);
+    cudaError_t e;
+    switch (d->wbits * 4 + d->parts) {
+        case 5: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<1, 1>, qmap, ymap, a); break;
+        case 6: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<1, 2>, qmap, ymap, a); break;
+        case 9: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<2, 1>, qmap, ymap, a); break;
+        default: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<2, 2>, qmap, ymap, a); break;
+    }
     if (e != cudaSuccess) {
         cudaGetLastError();
         return KEA_ERR_CUDA;

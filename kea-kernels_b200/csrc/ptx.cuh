@@ -155,6 +155,21 @@ KEA_DEVI void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "memory");
 }
 KEA_DEVI void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// tcgen05.ld fills its destination registers asynchronously, but to the compiler they are written when the load
+// statement executes: arithmetic on them could be scheduled above tcgen05.wait::ld and read registers that have not
+// landed. After the wait, this empty volatile statement (ordered after it, as every volatile asm) rewrites the
+// registers, so each later use depends on a statement that follows the wait.
+KEA_DEVI void tmem_regs_ready(uint32_t (&r)[16]) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+KEA_DEVI void tmem_regs_ready(uint32_t (&r)[32]) {
+    tmem_regs_ready(*reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+    tmem_regs_ready(*reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+}
 
 // Shared-memory matrix descriptor of a K-major operand stored in the 128-byte swizzle layout:
 // rows of 128 bytes, 8-row (1024 B) swizzle atoms stacked along M/N (stride 1024 B), atom base 1024-aligned.

@@ -401,6 +401,38 @@ def test_pair_kernel_equals_per_tile_kernel_bitwise(wbits, n, k, m):
     assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
 
 
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("n,k,m", [(256, 128, 257), (512, 2048, 300), (768, 136, 513), (1024, 4096, 1000),
+                                   (2048, 1024, 611)])
+@pytest.mark.parametrize("flags,out", [(0, torch.float32), (2, torch.float32), (0, torch.float16),
+                                       (2, torch.float16), (1, torch.float32)])
+def test_pair_kernel_two_parts_equals_oracle(wbits, n, k, m, flags, out):
+    """Two residual parts on the pair kernel (both parts' boxes per load slot, one accumulator per part): both
+    combination orders, SiLU, bias, both output types, the accumulators of both parts, ragged K and M."""
+    assert configs.choose(m, n, k, wbits, 2).kernel == configs.PAIR
+    seed = wbits * 433 + n + k + m + flags
+    codes, w = _codes(wbits, n, k, seed)
+    q, qs = _activations(2, m, k, seed)
+    alpha, bias = _channel(n, seed, m % 2 == 1)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags, out=out)
+    want, want_acc = oracle.reference(q, qs, w, alpha, bias, flags)
+    _check(y, acc, want, want_acc, flags)
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("flags", [0, 2])
+def test_pair_kernel_two_parts_equals_per_tile_kernel_bitwise(wbits, flags):
+    """Kea-T's x2 mode at config-4 size (M = 32000 frames): pair and per-tile kernels agree bit for bit."""
+    n, k, m = 4096, 1024, 32000
+    codes, _ = _codes(wbits, n, k, 31 + flags)
+    q, qs = _activations(2, m, k, 32)
+    alpha, bias = _channel(n, 33, True)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags, out=torch.float16)
+    y2, acc2 = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags, out=torch.float16, pair=False)
+    assert np.array_equal(acc, acc2)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+
+
 def test_pair_kernel_pdl_chain_matches():
     n, k, m = 1024, 1024, 1024
     codes, w = _codes(1, n, k, 8)

@@ -53,6 +53,10 @@ def test_every_shape_has_a_valid_config(n, k, wbits, parts):
             cfg.validate(parts)
             assert cfg.grid(m, n)[0] * cfg.tile_n >= n
             continue
+        if c.kernel == configs.PAIR:   # 256 x 256 pair tiles, one 256-column accumulator per part
+            assert c.tile_m == 256 and c.tile_n == 256 and parts <= 2 and c.splits == 1
+            assert c.smem_bytes <= 227 * 1024
+            continue
         assert c.tile_m in (128, 256) and c.tile_n in (32, 64, 128, 256)
         assert (c.tile_m // 128) * parts * c.tile_n <= 512
         assert 1 <= c.splits <= min(kb, 16) and 1 <= c.stages <= 8
