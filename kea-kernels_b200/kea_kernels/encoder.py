@@ -113,13 +113,21 @@ def rel_positions(t: int, d: int, device) -> Tensor:
 
 class ConformerLayer(nn.Module):
     def __init__(self, d: int, heads: int, ff: int, kernel: int, wbits: int, parts: int, gen: torch.Generator,
-                 device: torch.device, pdl: bool, keep_dense: bool):
+                 device: torch.device, pdl: bool, keep_dense: bool,
+                 projections: dict[str, LowBitLinear] | None = None):
+        """`projections`: loaded low-bit projections by this module's names (an export); the others are random."""
         super().__init__()
         self.d, self.heads, self.dk = d, heads, d // heads
         self.lin = nn.ModuleDict()
         self.weights = {}
         rnd = lambda *shape: torch.randn(*shape, generator=gen, device=device)
         for name, (n, k) in layer_linear_shapes(d, ff).items():
+            if projections is not None and name in projections:
+                lin = projections[name]
+                if (lin.out_features, lin.in_features) != (n, k):
+                    raise ValueError(f"{name}: projection is {lin.out_features} x {lin.in_features}, expected {n} x {k}")
+                self.lin[name] = lin
+                continue
             w = RandomLowBitWeights(n, k, wbits, gen, keep_dense=keep_dense)
             bias = rnd(n) * 0.02 if name != "linear_pos" else None
             self.weights[name] = (w, bias)
@@ -216,7 +224,9 @@ class FastConformerEncoder(nn.Module):
 
     def __init__(self, *, layers: int = 24, d_model: int = 1024, heads: int = 8, ff: int = 4096, conv_kernel: int = 9,
                  n_mels: int = 128, sub_channels: int = 256, wbits: int = 1, parts: int = 1, seed: int = 0,
-                 device=None, pdl: bool = True, keep_dense: bool = False):
+                 device=None, pdl: bool = True, keep_dense: bool = False,
+                 projections: list[dict[str, LowBitLinear]] | None = None):
+        """`projections`: per layer, loaded low-bit projections (kea_kernels.export); random weights otherwise."""
         super().__init__()
         device = torch.device(device if device is not None else "cuda")
         if device.type == "cuda" and device.index is None:
@@ -224,8 +234,11 @@ class FastConformerEncoder(nn.Module):
         gen = torch.Generator(device=device).manual_seed(seed)
         self.d_model, self.wbits, self.parts = d_model, wbits, parts
         self.pre = Subsampling(n_mels, d_model, sub_channels, gen, device)
+        if projections is not None and len(projections) != layers:
+            raise ValueError(f"projections for {len(projections)} layers, expected {layers}")
         self.layers = nn.ModuleList(ConformerLayer(d_model, heads, ff, conv_kernel, wbits, parts, gen, device, pdl,
-                                                   keep_dense) for _ in range(layers))
+                                                   keep_dense, None if projections is None else projections[i])
+                                    for i in range(layers))
 
     def frames(self, t: int) -> int:
         for _ in range(3):
