@@ -51,7 +51,9 @@ enum {
     KEA_FLAG_SILU = 1,
     KEA_FLAG_ORDER1 = 2,
     KEA_FLAG_PDL = 4,           /* launch with programmatic dependent launch (overlap with the previous kernel) */
-    KEA_FLAG_NO_PAIR = 8        /* never use the persistent CTA-pair kernel (the per-tile kernel runs instead) */
+    KEA_FLAG_NO_PAIR = 8,       /* never use the persistent CTA-pair kernel (the per-tile kernel runs instead) */
+    KEA_FLAG_FORCE_PAIR = 16    /* the pair kernel wherever its shape allows (1-2 parts, N % 256 == 0, m > 256,
+                                   k <= 32768), also where the table would take the per-tile kernel */
 };
 
 /* Device error word bits (written by kernels into `error_word`, or into the library's own device word). */
@@ -102,6 +104,11 @@ typedef struct KeaGemmDesc {
     int32_t splits;           /* 0: dispatch table; else split-K ways = cluster size (1..16) */
     int32_t stages;           /* 0: dispatch table; else pipeline stages (1..8) */
     uint32_t *error_word;     /* device word OR-ed with KEA_DEVERR_* bits, or NULL for the library's own */
+    const float *residual;    /* NULL, or FP32 [m][ld_residual]: y = residual + residual_scale * (the epilogue's
+                                 value), two IEEE roundings as `residual + scale * y` in PyTorch; FP32 y only. May be
+                                 y itself: every element is read before it is written, by the same thread */
+    int64_t ld_residual;
+    float residual_scale;
 } KeaGemmDesc;
 
 /* Tile configuration picked for a shape (the M-bucketed split-K dispatch table). */
@@ -165,6 +172,26 @@ enum {
 };
 
 int kea_lowbit_quantize(const KeaQuantizeDesc *desc, void *stream);
+
+/* The convolution module's middle between its pointwise GEMMs, in one pass over pw1's output:
+ *   g[b, t, c] = h[b, t, c] * sigmoid(h[b, t, C + c]), zero where t >= lengths[b] (padding);
+ *   y[b, t, c] = bias[c] + sum_j w[c, j] * g[b, t + j - kw / 2, c]   (zero padding in time),
+ * h FP32 [B][T][2C] and y FP32 [B][T][C] contiguous, w FP32 [C][kw] (BatchNorm folded in), kw odd <= 31.
+ * No reference C counterpart: replaces the reference's Triton glu_pad + torch depthwise conv + batch norm
+ * (src/kea_kernels/ternary/layer_fusions4.py:52-77). */
+typedef struct KeaConvDesc {
+    const float *h;
+    float *y;
+    const float *weight;      /* [C][kw] */
+    const float *bias;        /* [C] or NULL */
+    const int32_t *lengths;   /* [B] frames per clip, or NULL */
+    int32_t b, t, c, kw;
+    int32_t flags;            /* KEA_CONV_PDL */
+} KeaConvDesc;
+
+enum { KEA_CONV_PDL = 1 };
+
+int kea_lowbit_glu_depthwise(const KeaConvDesc *desc, void *stream);
 
 /* Reads and clears the library's own device error word on the current device. Synchronizes the device. */
 int kea_lowbit_read_error(uint32_t *out);

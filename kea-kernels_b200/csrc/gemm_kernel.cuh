@@ -101,6 +101,9 @@ struct GemmArgs {
                                  // K = 32 step, summed in the epilogue) so back-to-back MMAs do not wait on each other
     uint32_t a_stride;           // distance between consecutive stages' activation tiles (one-shot boxes are dense:
                                  // rows * 128 bytes; the MMA's reads past a short tile only reach unstored rows)
+    const float *res;            // residual FP32 [M][ld_res] or null: y = res + res_scale * value (FP32 y)
+    long long ld_res;
+    float res_scale;
     int stack;                   // 1: the P parts are stacked along the rows of one 128-row tile (part p's tokens at
                                  // rows p * mp ..), so one accumulator and one MMA per K step serve every part;
                                  // qmap is then (k, row, part, k-block) with boxes of mp rows x P parts
@@ -204,8 +207,14 @@ KEA_DEVI void finish_store(const GemmArgs &a, int t, int n, int c, const int (&a
         v[j] = finish_value(acc[0][j], P > 1 ? acc[P > 1 ? 1 : 0][j] : 0, P > 2 ? acc[P > 2 ? 2 : 0][j] : 0, s[0],
                             P > 1 ? s[P > 1 ? 1 : 0] : 0.f, P > 2 ? s[P > 2 ? 2 : 0] : 0.f, P, a.flags,
                             s_alpha[c + j], has_bias, has_bias ? s_bias[c + j] : 0.f);
-    const long long off = (long long)t * a.ldy + n;
     const bool full = n + CNT <= a.N;
+    if (a.res) {   // residual + scale * value: the two roundings of the unfused `x + s * y`
+        const float *r = a.res + (long long)t * a.ld_res + n;
+#pragma unroll
+        for (int j = 0; j < CNT; ++j)
+            if (full || n + j < a.N) v[j] = __fadd_rn(__ldg(r + j), __fmul_rn(a.res_scale, v[j]));
+    }
+    const long long off = (long long)t * a.ldy + n;
     if (a.y_f16) {
         __half *y = reinterpret_cast<__half *>(a.y) + off;
         if (full && a.vec_y) {

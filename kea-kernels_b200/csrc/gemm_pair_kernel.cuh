@@ -62,6 +62,9 @@ struct PairArgs {
     int M, N, K, kb_total;
     int n_tiles, tiles;          // 256-channel tiles, pair tiles in all
     int flags;                   // KEA_FLAG_SILU, KEA_FLAG_ORDER1
+    const float *res;            // residual FP32 [M][ld_res] (16-byte rows) or null: y = res + res_scale * value
+    long long ld_res;
+    float res_scale;
     int pdl;
     int y_f16;
     int stages;
@@ -160,6 +163,18 @@ KEA_DEVI void pair_finish_chunk2(uint32_t (&lo)[32], const uint32_t (&hi)[32], u
     }
 }
 
+// residual + scale * value for one chunk of FP32 outputs (bit patterns in v), 32 channels of token row `row`.
+KEA_DEVI void pair_add_residual(uint32_t (&v)[32], const float *row, float scale) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const float4 r = __ldg(reinterpret_cast<const float4 *>(row) + q);
+        v[4 * q] = __float_as_uint(__fadd_rn(r.x, __fmul_rn(scale, __uint_as_float(v[4 * q]))));
+        v[4 * q + 1] = __float_as_uint(__fadd_rn(r.y, __fmul_rn(scale, __uint_as_float(v[4 * q + 1]))));
+        v[4 * q + 2] = __float_as_uint(__fadd_rn(r.z, __fmul_rn(scale, __uint_as_float(v[4 * q + 2]))));
+        v[4 * q + 3] = __float_as_uint(__fadd_rn(r.w, __fmul_rn(scale, __uint_as_float(v[4 * q + 3]))));
+    }
+}
+
 template <bool F16>
 KEA_DEVI void pair_stage_and_store(const CUtensorMap *ymap, const uint32_t (&v)[32], uint32_t stg, int ci, int n,
                                    int trow0) {
@@ -218,6 +233,8 @@ KEA_DEVI void pair_epilogue_tile(const PairArgs &a, const CUtensorMap *ymap, uin
             for (int q = 0; q < 8; ++q) dst[q] = make_int4((int)va[4 * q], (int)va[4 * q + 1], (int)va[4 * q + 2], (int)va[4 * q + 3]);
         }
         pair_finish_chunk<F16, BIAS, SILU>(va, s_al, s_bi, 32 * ci, sq);
+        if constexpr (!F16)
+            if (a.res && t < a.M) pair_add_residual(va, a.res + (long long)t * a.ld_res + nbase + 32 * ci, a.res_scale);
         KEA_PTRACE(tr, 12, j * 4 + ci);
         pair_stage_and_store<F16>(ymap, va, stg, ci, nbase + 32 * ci, trow0);
         KEA_PTRACE(tr, 13, j * 4 + ci);
@@ -237,6 +254,9 @@ KEA_DEVI void pair_epilogue_tile(const PairArgs &a, const CUtensorMap *ymap, uin
             for (int q = 0; q < 8; ++q) dst[q] = make_int4((int)vb[4 * q], (int)vb[4 * q + 1], (int)vb[4 * q + 2], (int)vb[4 * q + 3]);
         }
         pair_finish_chunk<F16, BIAS, SILU>(vb, s_al, s_bi, 32 * (ci + 1), sq);
+        if constexpr (!F16)
+            if (a.res && t < a.M)
+                pair_add_residual(vb, a.res + (long long)t * a.ld_res + nbase + 32 * (ci + 1), a.res_scale);
         pair_stage_and_store<F16>(ymap, vb, stg, ci + 1, nbase + 32 * (ci + 1), trow0);
     }
 }
@@ -275,6 +295,8 @@ KEA_DEVI void pair_epilogue_tile2(const PairArgs &a, const CUtensorMap *ymap, ui
             }
         }
         pair_finish_chunk2<F16, BIAS, SILU>(v0, v1, s_al, s_bi, 32 * ci, s_lo, s_hi);
+        if constexpr (!F16)
+            if (a.res && t < a.M) pair_add_residual(v0, a.res + (long long)t * a.ld_res + nbase + 32 * ci, a.res_scale);
         pair_stage_and_store<F16>(ymap, v0, stg, ci, nbase + 32 * ci, trow0);
     }
 }

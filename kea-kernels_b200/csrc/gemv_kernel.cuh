@@ -46,6 +46,9 @@ struct GemvArgs {
     int M, N, K, kb_total;
     int ch;                      // channels per CTA: 32, 16 or 8
     int flags;
+    const float *res;            // residual FP32 [M][ld_res] or null: y = res + res_scale * value
+    long long ld_res;
+    float res_scale;
     uint32_t *err;
 };
 
@@ -179,8 +182,9 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) lowbit_gemv_kern
             s[p] = __ldg(a.qs + p * a.qs_stride + m);
         }
         const bool has_bias = a.bias != nullptr;
-        const float v = finish_value(tot[0], tot[1], tot[2], s[0], s[1], s[2], P, a.flags, __ldg(a.alpha + nn), has_bias,
-                                     has_bias ? __ldg(a.bias + nn) : 0.f);
+        float v = finish_value(tot[0], tot[1], tot[2], s[0], s[1], s[2], P, a.flags, __ldg(a.alpha + nn), has_bias,
+                               has_bias ? __ldg(a.bias + nn) : 0.f);
+        if (a.res) v = __fadd_rn(__ldg(a.res + (long long)m * a.ld_res + nn), __fmul_rn(a.res_scale, v));
         if (a.y_f16)
             reinterpret_cast<__half *>(a.y)[(long long)m * a.ldy + nn] = __float2half_rn(v);
         else

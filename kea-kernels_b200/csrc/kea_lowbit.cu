@@ -12,6 +12,7 @@
 #include "gemm_kernel.cuh"
 #include "gemm_pair_kernel.cuh"
 #include "gemv_kernel.cuh"
+#include "conv_kernels.cuh"
 #include "aux_kernels.cuh"
 
 namespace {
@@ -173,9 +174,26 @@ int pair_max_stages(int wbits, int parts) {
 // the per-tile kernel (its 256 x 256 pair tiles keep the shared-memory traffic per MAC at half the per-tile
 // kernel's).
 constexpr int kPairMinM = 257;
+// With two parts the tile's two accumulators fill tensor memory (no overlap of epilogue and MMAs), which costs
+// where a few tiles are all the work: below kPairMinTiles2 pair tiles the per-tile kernel measured as fast or faster.
+constexpr int kPairMinTiles2 = 32;
 // K <= 32768 keeps |acc| <= 127 K below 2^22, where the epilogue's two-operation INT32 -> FP32 conversion is exact.
-bool pair_shape(int m, int n, int k, int parts) {
+bool pair_fits(int m, int n, int k, int parts) {
     return parts <= 2 && n % kea::kPairTileN == 0 && m >= kPairMinM && k <= 32768;
+}
+bool pair_shape(int m, int n, int k, int parts) {
+    return pair_fits(m, n, k, parts) &&
+           (parts == 1 || ceil_div(m, kea::kPairTileM) * (n / kea::kPairTileN) >= kPairMinTiles2);
+}
+KeaGemmConfig pair_config(int wbits, int parts) {
+    KeaGemmConfig c{};
+    c.tile_m = kea::kPairTileM;
+    c.tile_n = kea::kPairTileN;
+    c.splits = 1;
+    c.stages = pair_max_stages(wbits, parts);
+    c.smem_bytes = pair_smem_bytes(wbits, parts, c.stages);
+    c.kernel = 1;
+    return c;
 }
 
 // The M-bucketed split-K dispatch table (B200, 148 SMs).
@@ -272,14 +290,7 @@ bool gemv_fits(int m, int parts, int ch) {
 // kernel's entry.
 KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
     KeaGemmConfig c = choose_tile(m, n, k, wbits, parts, sms);
-    if (pair_shape(m, n, k, parts)) {
-        c.tile_m = kea::kPairTileM;
-        c.tile_n = kea::kPairTileN;
-        c.splits = 1;
-        c.stages = pair_max_stages(wbits, parts);
-        c.smem_bytes = pair_smem_bytes(wbits, parts, c.stages);
-        c.kernel = 1;
-    }
+    if (pair_shape(m, n, k, parts)) c = pair_config(wbits, parts);
     if (m * parts <= kGemvTableRows && gemv_fits(m, parts, gemv_channels(n, k, wbits, m, parts))) {
         c.kernel = 2;
         c.tile_m = m;
@@ -356,6 +367,9 @@ int launch_gemv(const KeaGemmDesc *d, const KeaGemmConfig &c, void *stream) {
     a.ch = c.tile_n;
     a.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
     a.err = d->error_word;
+    a.res = d->residual;
+    a.ld_res = d->ld_residual;
+    a.res_scale = d->residual_scale;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ceil_div(d->n, c.tile_n), 1, 1);
@@ -389,7 +403,8 @@ int launch_gemv(const KeaGemmDesc *d, const KeaGemmConfig &c, void *stream) {
 int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *stream) {
     const int esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
     if (!aligned16(d->y) || (d->ldy * esize) % 16 || !aligned16(d->alpha) || (d->bias && !aligned16(d->bias)) ||
-        (d->acc && (!aligned16(d->acc) || d->ld_acc % 4 || (d->parts > 1 && d->acc_part_stride % 4))))
+        (d->acc && (!aligned16(d->acc) || d->ld_acc % 4 || (d->parts > 1 && d->acc_part_stride % 4))) ||
+        (d->residual && (!aligned16(d->residual) || d->ld_residual % 4)))
         return KEA_ERR_UNSUPPORTED;
     // Activations: 3-D (k, row, part) with 128 x 128 x 1 boxes in the 128-byte swizzle; columns >= k and rows >= m
     // read as 0.
@@ -432,6 +447,9 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
     a.n_tiles = d->n / kea::kPairTileN;
     a.tiles = a.n_tiles * ceil_div(d->m, kea::kPairTileM);
     a.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
+    a.res = d->residual;
+    a.ld_res = d->ld_residual;
+    a.res_scale = d->residual_scale;
     a.pdl = (d->flags & KEA_FLAG_PDL) ? 1 : 0;
     a.y_f16 = esize == 2;
     a.stages = c.stages;
@@ -472,6 +490,11 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
 }
 
 }  // namespace
+
+template <int KW>
+cudaError_t launch_glu_dw(cudaLaunchConfig_t *cfg, const kea::ConvArgs &a) {
+    return cudaLaunchKernelEx(cfg, kea::glu_depthwise_kernel<KW>, a);
+}
 
 extern "C" {
 
@@ -523,6 +546,46 @@ int kea_lowbit_prepare(const uint8_t *codes, int32_t wbits, int32_t n, int32_t k
     kea::prepare_panels_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(codes, row_bytes, wbits, n, k, kb, rows,
                                                                           panels, error_word);
     return cudaGetLastError() == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
+}
+
+int kea_lowbit_glu_depthwise(const KeaConvDesc *d, void *stream) {
+    if (!d || !d->h || !d->y || !d->weight || d->b < 0 || d->t < 0 || d->c < 1 || d->kw < 1 || d->kw % 2 == 0 ||
+        d->kw > kea::kConvMaxKw || (d->flags & ~KEA_CONV_PDL))
+        return KEA_ERR_INVALID_VALUE;
+    if (d->kw != 9 && d->kw != 3 && d->kw != 31) return KEA_ERR_UNSUPPORTED;   // the built widths
+    if (d->b == 0 || d->t == 0) return KEA_OK;
+    if (d->b > 65535) return KEA_ERR_UNSUPPORTED;
+    int dev = 0;
+    const int st = device_setup(&dev);
+    if (st != KEA_OK) return st;
+    kea::ConvArgs a{};
+    a.h = d->h;
+    a.y = d->y;
+    a.w = d->weight;
+    a.bias = d->bias;
+    a.lengths = d->lengths;
+    a.B = d->b;
+    a.T = d->t;
+    a.C = d->c;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ceil_div(d->c, kea::kConvThreads), (unsigned)ceil_div(d->t, kea::kConvChunk),
+                       (unsigned)d->b);
+    cfg.blockDim = dim3(kea::kConvThreads, 1, 1);
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    if (d->flags & KEA_CONV_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 1;
+    }
+    const cudaError_t e = d->kw == 9 ? launch_glu_dw<9>(&cfg, a) : d->kw == 3 ? launch_glu_dw<3>(&cfg, a)
+                                                                             : launch_glu_dw<31>(&cfg, a);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return KEA_ERR_CUDA;
+    }
+    return KEA_OK;
 }
 
 int kea_lowbit_quantize(const KeaQuantizeDesc *d, void *stream) {
@@ -598,9 +661,12 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     if (!d->q || !d->qs || !d->panels || !d->alpha || !d->y || d->ldy < d->n || d->ldq < d->k) return KEA_ERR_INVALID_VALUE;
     if (d->acc && (d->ld_acc < d->n || (d->parts > 1 && d->acc_part_stride < (int64_t)d->m * d->ld_acc)))
         return KEA_ERR_INVALID_VALUE;
+    if (d->residual && (d->y_dtype != KEA_OUT_F32 || d->ld_residual < d->n)) return KEA_ERR_INVALID_VALUE;
     if (!aligned16(d->q) || d->ldq % 16 || !aligned16(d->panels)) return KEA_ERR_ALIGNMENT;
     if (d->parts > 1 && (d->q_part_stride % 16 || d->q_part_stride < (int64_t)d->m * d->ldq)) return KEA_ERR_ALIGNMENT;
-    if (d->flags & ~(KEA_FLAG_SILU | KEA_FLAG_ORDER1 | KEA_FLAG_PDL | KEA_FLAG_NO_PAIR)) return KEA_ERR_INVALID_VALUE;
+    if (d->flags & ~(KEA_FLAG_SILU | KEA_FLAG_ORDER1 | KEA_FLAG_PDL | KEA_FLAG_NO_PAIR | KEA_FLAG_FORCE_PAIR))
+        return KEA_ERR_INVALID_VALUE;
+    if ((d->flags & KEA_FLAG_NO_PAIR) && (d->flags & KEA_FLAG_FORCE_PAIR)) return KEA_ERR_INVALID_VALUE;
 
     int dev = 0;
     const int st = device_setup(&dev);
@@ -619,6 +685,8 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
         g.tile_n = d->tile_n;
         return launch_gemv(d, g, stream);
     }
+    if (!forced && (d->flags & KEA_FLAG_FORCE_PAIR) && pair_fits(d->m, d->n, d->k, d->parts))
+        c = pair_config(d->wbits, d->parts);
     if (c.kernel == 1 && !forced && !(d->flags & KEA_FLAG_NO_PAIR)) {
         const int ps = launch_pair(d, c, g_devices[dev].sms, stream);
         if (ps != KEA_ERR_UNSUPPORTED) return ps;
@@ -731,7 +799,8 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     const int out_esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
     const int warp_row_bytes = (c.tile_n / 4) * out_esize;
     const int staging_bytes = (c.tile_m / kea::kBM) * kea::kEpiWarps * 32 * warp_row_bytes;   // reuses the stages
-    bool tma_store = c.splits == 1 && aligned16(d->y) && (d->ldy * out_esize) % 16 == 0 &&
+    // (a residual is added by the direct-store epilogue, which reads it next to the value it finishes)
+    bool tma_store = c.splits == 1 && !d->residual && aligned16(d->y) && (d->ldy * out_esize) % 16 == 0 &&
                      (warp_row_bytes == 64 || warp_row_bytes == 128) &&
                      staging_bytes <= c.stages * stage_bytes(c.tile_m, c.tile_n, pe, d->wbits);
     if (tma_store) {
@@ -769,6 +838,9 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     a.stages = c.stages;
     a.kb_total = ceil_div(d->k, kea::kBK);
     a.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
+    a.res = d->residual;
+    a.ld_res = d->ld_residual;
+    a.res_scale = d->residual_scale;
     a.pdl = (d->flags & KEA_FLAG_PDL) ? 1 : 0;
     a.tmem_cols = tmem_columns(c.tile_m, c.tile_n, pe);
     a.a_stage = (uint32_t)a_stage_bytes(c.tile_m, pe);
@@ -787,6 +859,9 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     a.recv_off = a.recv_aliases_stages ? 0u : (uint32_t)(c.stages * stage_bytes(c.tile_m, c.tile_n, pe, d->wbits));
     a.stack = stack ? 1 : 0;
     a.mp = box_rows4;
+    a.res = d->residual;
+    a.ld_res = d->ld_residual;
+    a.res_scale = d->residual_scale;
     const int esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
     a.vec_y = aligned16(d->y) && ((d->ldy * esize) % 16 == 0);
     a.vec_acc = d->acc && aligned16(d->acc) && ((d->ld_acc * 4) % 16 == 0) && ((d->acc_part_stride * 4) % 16 == 0);

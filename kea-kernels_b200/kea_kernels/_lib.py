@@ -17,13 +17,15 @@ LIB_PATH = Path(os.environ.get("KEA_LOWBIT_LIB", Path(__file__).resolve().parent
 
 OK, INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES, CUDA, NO_DEVICE, DEVICE_TIMEOUT, CAPTURE = range(9)
 OUT_F32, OUT_F16 = 0, 1
-FLAG_SILU, FLAG_ORDER1, FLAG_PDL, FLAG_NO_PAIR = 1, 2, 4, 8
+FLAG_SILU, FLAG_ORDER1, FLAG_PDL, FLAG_NO_PAIR, FLAG_FORCE_PAIR = 1, 2, 4, 8, 16
 QUANT_INPUT_SILU, QUANT_PDL = 1, 2
 DEVERR_TIMEOUT, DEVERR_TAIL_BITS, DEVERR_TERNARY_11 = 1, 2, 4
 
 # Every symbol include/kea_lowbit.h declares.
 EXPORTS = ("kea_lowbit_gemm", "kea_lowbit_choose_config", "kea_lowbit_panel_bytes", "kea_lowbit_prepare",
-           "kea_lowbit_quantize", "kea_lowbit_read_error", "kea_lowbit_status_string", "kea_lowbit_version")
+           "kea_lowbit_quantize", "kea_lowbit_glu_depthwise", "kea_lowbit_read_error", "kea_lowbit_status_string",
+           "kea_lowbit_version")
+CONV_PDL = 1
 
 
 class GemmDesc(ctypes.Structure):
@@ -37,6 +39,7 @@ class GemmDesc(ctypes.Structure):
         ("m", ctypes.c_int32), ("flags", ctypes.c_int32),
         ("tile_m", ctypes.c_int32), ("tile_n", ctypes.c_int32), ("splits", ctypes.c_int32),
         ("stages", ctypes.c_int32), ("error_word", ctypes.c_void_p),
+        ("residual", ctypes.c_void_p), ("ld_residual", ctypes.c_int64), ("residual_scale", ctypes.c_float),
     ]
 
 
@@ -54,6 +57,12 @@ class QuantizeDesc(ctypes.Structure):
         ("norm_weight", ctypes.c_void_p), ("norm_bias", ctypes.c_void_p), ("eps", ctypes.c_float),
         ("flags", ctypes.c_int32),
     ]
+
+
+class ConvDesc(ctypes.Structure):
+    _fields_ = [("h", ctypes.c_void_p), ("y", ctypes.c_void_p), ("weight", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+                ("lengths", ctypes.c_void_p), ("b", ctypes.c_int32), ("t", ctypes.c_int32), ("c", ctypes.c_int32),
+                ("kw", ctypes.c_int32), ("flags", ctypes.c_int32)]
 
 
 _lib = None
@@ -78,6 +87,8 @@ def lib() -> ctypes.CDLL:
         handle.kea_lowbit_prepare.restype = ctypes.c_int
         handle.kea_lowbit_quantize.argtypes = [ctypes.POINTER(QuantizeDesc), ctypes.c_void_p]
         handle.kea_lowbit_quantize.restype = ctypes.c_int
+        handle.kea_lowbit_glu_depthwise.argtypes = [ctypes.POINTER(ConvDesc), ctypes.c_void_p]
+        handle.kea_lowbit_glu_depthwise.restype = ctypes.c_int
         handle.kea_lowbit_read_error.argtypes = [ctypes.POINTER(ctypes.c_uint32)]
         handle.kea_lowbit_read_error.restype = ctypes.c_int
         handle.kea_lowbit_status_string.argtypes = [ctypes.c_int]

@@ -52,8 +52,9 @@ class LowBitLinear(nn.Module):
         self.bias = None if bias is None else bias.to(device=device, dtype=torch.float32).contiguous()
 
     def forward(self, x: Tensor, *, norm: nn.LayerNorm | None = None, input_silu: bool = False,
-                silu: bool = False) -> Tensor:
-        """x [B, T, K] (any strides) -> [B, T, N]."""
+                silu: bool = False, residual: Tensor | None = None, residual_scale: float = 1.0) -> Tensor:
+        """x [B, T, K] (any strides) -> [B, T, N]; with `residual` ([B, T, N] contiguous FP32) the GEMM's epilogue
+        returns residual + residual_scale * projection (the layer's skip connection, same roundings as unfused)."""
         b, t, k = x.shape
         m = b * t
         y = torch.empty(b, t, self.out_features, device=x.device, dtype=torch.float32)
@@ -63,8 +64,10 @@ class LowBitLinear(nn.Module):
         # previous GEMM drains (measured slower on the clip); the GEMM after it does use it
         q, qs, ldq = lowbit.quantize(x, (x.stride(0), x.stride(1), x.stride(2), t), m, k, self.parts, norm=norm,
                                      input_silu=input_silu)
+        res = None if residual is None else residual.reshape(m, self.out_features)
         lowbit.gemm(q, qs, ldq, m, self.panels, self.wbits, self.out_features, k, self.scale, self.bias,
-                    y.view(m, self.out_features), parts=self.parts, silu=silu, pdl=self.pdl)
+                    y.view(m, self.out_features), parts=self.parts, silu=silu, pdl=self.pdl, residual=res,
+                    residual_scale=residual_scale)
         return y
 
 
@@ -169,23 +172,24 @@ class ConformerLayer(nn.Module):
             scores = scores.masked_fill(~keys, float("-inf"))
         attn = torch.softmax(scores, dim=-1)
         ctx = torch.matmul(attn, v.transpose(1, 2)).transpose(1, 2).reshape(b, t, self.d)
-        return self.lin["out"](ctx)
+        return self.lin["out"](ctx, residual=x)                          # x + out(ctx)
 
-    def conv(self, x: Tensor, frames: Tensor | None = None) -> Tensor:
-        """frames: optional [b, t, 1] of 1 at real frames, 0 at padding (zeroed before the depthwise conv)."""
+    def conv(self, x: Tensor, lengths: Tensor | None = None) -> Tensor:
+        """lengths: optional int32 [b] frames per clip (later frames are padding, zeroed before the depthwise conv).
+        GLU, padding mask and the depthwise conv (BatchNorm folded in) are one kernel between the two GEMMs, reading
+        and writing token-major rows, so pw2's quantizer (with the conv module's SiLU fused) reads unit-stride rows."""
         h = self.lin["pw1"](x, norm=self.norms["conv"])                 # [b, t, 2d]
-        h = F.glu(h, dim=-1)
-        if frames is not None:
-            h = h * frames
-        h = h.transpose(1, 2)                                           # [b, d, t]
-        h = F.conv1d(h, self.dw_weight, self.dw_bias, padding=self.kernel // 2, groups=self.d)
-        return self.lin["pw2"](h.transpose(1, 2), input_silu=True)      # SiLU fused into the quantizer
+        h = lowbit.glu_depthwise(h, self.dw_weight, self.dw_bias, lengths)   # [b, t, d]
+        return self.lin["pw2"](h, input_silu=True, residual=x)          # SiLU in the quantizer; x + pw2(...)
 
-    def forward(self, x: Tensor, keys: Tensor | None = None, frames: Tensor | None = None) -> Tensor:
-        x = x + 0.5 * self.lin["ff1_down"](self.lin["ff1_up"](x, norm=self.norms["ff1"], silu=True))
-        x = x + self.attention(x, keys)
-        x = x + self.conv(x, frames)
-        x = x + 0.5 * self.lin["ff2_down"](self.lin["ff2_up"](x, norm=self.norms["ff2"], silu=True))
+    def forward(self, x: Tensor, keys: Tensor | None = None, lengths: Tensor | None = None) -> Tensor:
+        # every skip connection is added in the epilogue of the GEMM that ends its branch (x + 0.5 ff, x + att, ...)
+        x = self.lin["ff1_down"](self.lin["ff1_up"](x, norm=self.norms["ff1"], silu=True), residual=x,
+                                 residual_scale=0.5)
+        x = self.attention(x, keys)
+        x = self.conv(x, lengths)
+        x = self.lin["ff2_down"](self.lin["ff2_up"](x, norm=self.norms["ff2"], silu=True), residual=x,
+                                 residual_scale=0.5)
         return self.norms["out"](x)
 
 
@@ -252,13 +256,13 @@ class FastConformerEncoder(nn.Module):
         zeroed before the depthwise convolution, so a clip's real frames do not depend on the padding (the
         length-bucketed batches of mixed-length clips)."""
         x = self.pre(mel)
-        keys = frames = None
+        keys = lens = None
         if lengths is not None:
             t = x.shape[1]
-            live = torch.arange(t, device=x.device)[None, :] < lengths.to(x.device)[:, None]   # [b, t]
-            keys, frames = live[:, None, None, :], live[:, :, None].to(x.dtype)
+            lens = lengths.to(device=x.device, dtype=torch.int32)
+            keys = (torch.arange(t, device=x.device)[None, :] < lens[:, None])[:, None, None, :]   # [b, 1, 1, t]
         for layer in self.layers:
-            x = layer(x, keys, frames)
+            x = layer(x, keys, lens)
         return x
 
     def gemm_shapes(self, batch: int, t: int) -> list[tuple[str, int, int, int]]:

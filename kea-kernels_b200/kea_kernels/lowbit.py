@@ -78,12 +78,15 @@ def quantize(x: Tensor, rows: tuple[int, int, int, int], m: int, k: int, parts: 
 
 def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n: int, k: int, alpha: Tensor,
          bias: Tensor | None, y: Tensor, *, parts: int, silu: bool = False, order: int = 0, acc: Tensor | None = None,
-         config=None, pdl: bool = False, error_word: Tensor | None = None, pair: bool = True) -> None:
+         config=None, pdl: bool = False, error_word: Tensor | None = None, pair: bool = True,
+         force_pair: bool = False, residual: Tensor | None = None, residual_scale: float = 1.0) -> None:
     """y[:m] (row stride y.stride(0); FP32 or FP16) from q int8 [parts, m, ldq] and qs FP32 [parts, m].
     acc, when given, receives the exact INT32 accumulators as int32 [parts, m, n] (any row / part strides).
     `config` forces the per-tile kernel's tiles, or (tile_m <= 16, m <= 16) the CUDA-core kernel's channels per CTA;
     a pair config from the table forces nothing. pair=False keeps the dispatch table away from the persistent
-    CTA-pair kernel."""
+    CTA-pair kernel; force_pair=True takes it wherever its shape allows (also below the table's tile threshold).
+    residual (FP32 [m, n], unit column stride; may be y itself) makes the epilogue write residual + residual_scale *
+    value, rounded as the unfused `residual + residual_scale * y` (FP32 y only)."""
     if m == 0:
         return
     if parts not in (1, 2, 3):
@@ -108,8 +111,15 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
     if acc is not None and (acc.dtype != torch.int32 or acc.dim() != 3 or acc.shape[0] < parts
                             or acc.shape[1] < m or acc.shape[2] < n or acc.stride(2) != 1 or acc.device != y.device):
         raise ValueError(f"acc must be int32 [{parts}, {m}, {n}] with unit column stride")
+    if residual is not None:
+        _require_cuda(residual, "residual")
+        if residual.dtype != torch.float32 or residual.dim() != 2 or residual.shape[0] < m or residual.shape[1] < n \
+                or residual.stride(1) != 1 or residual.device != y.device or y.dtype != torch.float32:
+            raise ValueError(f"residual must be FP32 [{m}, {n}] with unit column stride, with an FP32 y")
     d = _lib.GemmDesc()
     d.q, d.q_part_stride, d.ldq, d.parts = q.data_ptr(), q.stride(0), ldq, parts
+    if residual is not None:
+        d.residual, d.ld_residual, d.residual_scale = residual.data_ptr(), residual.stride(0), float(residual_scale)
     d.qs, d.qs_part_stride = qs.data_ptr(), qs.stride(0)
     d.panels, d.wbits, d.n, d.k = panels.data_ptr(), wbits, n, k
     d.alpha, d.bias = alpha.data_ptr(), (None if bias is None else bias.data_ptr())
@@ -119,10 +129,39 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
         d.acc, d.ld_acc, d.acc_part_stride = acc.data_ptr(), acc.stride(1), acc.stride(0)
     d.m = m
     d.flags = (_lib.FLAG_SILU if silu else 0) | (_lib.FLAG_ORDER1 if order else 0) | (_lib.FLAG_PDL if pdl else 0) \
-        | (0 if pair else _lib.FLAG_NO_PAIR)
+        | (0 if pair else _lib.FLAG_NO_PAIR) | (_lib.FLAG_FORCE_PAIR if force_pair else 0)
     if config is not None and getattr(config, "kernel", 0) != 1:   # a pair config from the table forces nothing
         d.tile_m, d.tile_n, d.splits, d.stages = config.tile_m, config.tile_n, config.splits, config.stages
     if error_word is not None:
         d.error_word = error_word.data_ptr()
     with torch.cuda.device(y.device):
         _lib.check(_lib.lib().kea_lowbit_gemm(ctypes.byref(d), _lib.stream_handle(y.device)), "gemm")
+
+
+def glu_depthwise(h: Tensor, weight: Tensor, bias: Tensor | None = None, lengths: Tensor | None = None, *,
+                  pdl: bool = False) -> Tensor:
+    """The convolution module's middle in one kernel: h FP32 [B, T, 2C] (pw1's output) -> GLU (first half times
+    sigmoid of the second), zero at frames t >= lengths[b], depthwise conv along time with weight FP32 [C, kw]
+    (BatchNorm folded in) and bias [C], zero padding -> FP32 [B, T, C]."""
+    _require_cuda(h, "h")
+    if h.dtype != torch.float32 or h.dim() != 3 or h.shape[2] % 2 or not h.is_contiguous():
+        raise ValueError("h must be contiguous FP32 [B, T, 2C]")
+    b, t, c2 = h.shape
+    c = c2 // 2
+    if weight.dim() == 3:
+        weight = weight.reshape(weight.shape[0], weight.shape[-1])
+    if weight.dtype != torch.float32 or weight.shape[0] != c or weight.device != h.device:
+        raise ValueError(f"weight must be FP32 [{c}, kw] on {h.device}")
+    weight = weight.contiguous()
+    if bias is not None and (bias.dtype != torch.float32 or tuple(bias.shape) != (c,) or bias.device != h.device):
+        raise ValueError(f"bias must be FP32 [{c}] on {h.device}")
+    if lengths is not None:
+        if tuple(lengths.shape) != (b,) or lengths.device != h.device:
+            raise ValueError(f"lengths must be [{b}] on {h.device}")
+        lengths = lengths.to(torch.int32).contiguous()
+    y = torch.empty(b, t, c, device=h.device, dtype=torch.float32)
+    d = _lib.ConvDesc(h=h.data_ptr(), y=y.data_ptr(), weight=weight.data_ptr(), bias=_lib.ptr(bias),
+                      lengths=_lib.ptr(lengths), b=b, t=t, c=c, kw=weight.shape[1], flags=_lib.CONV_PDL if pdl else 0)
+    with torch.cuda.device(h.device):
+        _lib.check(_lib.lib().kea_lowbit_glu_depthwise(ctypes.byref(d), _lib.stream_handle(h.device)), "glu_depthwise")
+    return y

@@ -119,3 +119,35 @@ def test_padded_bucket_matches_clip_alone():
     for got, want in ((y[1, :n], alone_short), (y[0], alone_long)):
         rel = ((got - want).norm() / want.norm()).item()
         assert rel < 2e-4, rel
+
+
+@pytest.mark.parametrize("b,t,c", [(3, 125, 1024), (1, 7, 40), (2, 1, 300), (4, 200, 1024)])
+@pytest.mark.parametrize("kw", [9, 3, 31])
+@pytest.mark.parametrize("masked", [False, True])
+@torch.inference_mode()
+def test_glu_depthwise_matches_torch(b, t, c, kw, masked):
+    """GLU + padding mask + depthwise conv in one kernel against F.glu -> mask -> F.conv1d (FP32; the kernel sums
+    the taps in its own order with FMAs, so within FP32 rounding of the conv)."""
+    from kea_kernels import lowbit
+    g = torch.Generator().manual_seed(b * 1000 + t + c + kw)
+    h = torch.randn(b, t, 2 * c, generator=g).to(DEV)
+    w = (torch.randn(c, 1, kw, generator=g) / math.sqrt(kw)).to(DEV)
+    bias = (0.1 * torch.randn(c, generator=g)).to(DEV) if kw != 3 else None
+    lengths = torch.randint(1, t + 1, (b,), generator=g).to(DEV) if masked else None
+    y = lowbit.glu_depthwise(h, w, bias, lengths)
+    gl = F.glu(h, dim=-1)
+    if masked:
+        gl = gl * (torch.arange(t, device=DEV)[None, :] < lengths[:, None])[:, :, None]
+    want = F.conv1d(gl.transpose(1, 2), w, bias, padding=kw // 2, groups=c).transpose(1, 2)
+    torch.testing.assert_close(y, want, rtol=2e-5, atol=2e-5)
+
+
+def test_glu_depthwise_rejects_bad_arguments():
+    from kea_kernels import lowbit
+    h = torch.randn(1, 4, 8, device=DEV)
+    with pytest.raises(ValueError):
+        lowbit.glu_depthwise(h, torch.randn(4, 1, 4, device=DEV))     # even width
+    with pytest.raises(ValueError):
+        lowbit.glu_depthwise(h, torch.randn(3, 1, 9, device=DEV))     # channel count
+    with pytest.raises(ValueError):
+        lowbit.glu_depthwise(h.transpose(1, 2), torch.randn(4, 1, 9, device=DEV))

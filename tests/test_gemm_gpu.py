@@ -51,7 +51,8 @@ def _channel(n: int, seed: int, bias: bool):
     return alpha, b
 
 
-def _run(codes, wbits, n, k, q, qs, alpha, bias, *, flags=0, out=torch.float32, config=None, pdl=False, pair=True):
+def _run(codes, wbits, n, k, q, qs, alpha, bias, *, flags=0, out=torch.float32, config=None, pdl=False, pair=True,
+         pair_only=False):
     parts, m, ldq = q.shape
     panels = lowbit.prepare_panels(torch.from_numpy(codes).to(DEV), wbits, n, k)
     qd, qsd = torch.from_numpy(q).to(DEV), torch.from_numpy(qs).to(DEV)
@@ -60,7 +61,7 @@ def _run(codes, wbits, n, k, q, qs, alpha, bias, *, flags=0, out=torch.float32, 
     y = torch.full((m, n), float("nan"), device=DEV, dtype=out)
     acc = torch.full((parts, m, n), -7, device=DEV, dtype=torch.int32)
     lowbit.gemm(qd, qsd, ldq, m, panels, wbits, n, k, ad, bd, y, parts=parts, silu=bool(flags & 1),
-                order=(flags >> 1) & 1, acc=acc, config=config, pdl=pdl, pair=pair)
+                order=(flags >> 1) & 1, acc=acc, config=config, pdl=pdl, pair=pair, force_pair=pair_only)
     torch.cuda.synchronize()
     assert _lib.read_device_error() == 0
     return y.cpu(), acc.cpu().numpy()
@@ -403,18 +404,20 @@ def test_pair_kernel_equals_per_tile_kernel_bitwise(wbits, n, k, m):
 
 @pytest.mark.parametrize("wbits", [1, 2])
 @pytest.mark.parametrize("n,k,m", [(256, 128, 257), (512, 2048, 300), (768, 136, 513), (1024, 4096, 1000),
-                                   (2048, 1024, 611)])
+                                   (2048, 1024, 611), (4096, 1024, 2000)])
 @pytest.mark.parametrize("flags,out", [(0, torch.float32), (2, torch.float32), (0, torch.float16),
                                        (2, torch.float16), (1, torch.float32)])
 def test_pair_kernel_two_parts_equals_oracle(wbits, n, k, m, flags, out):
     """Two residual parts on the pair kernel (both parts' boxes per load slot, one accumulator per part): both
-    combination orders, SiLU, bias, both output types, the accumulators of both parts, ragged K and M."""
-    assert configs.choose(m, n, k, wbits, 2).kernel == configs.PAIR
+    combination orders, SiLU, bias, both output types, the accumulators of both parts, ragged K and M. The table
+    takes the pair kernel for two parts from 32 pair tiles on; smaller shapes run it through pair_only."""
+    tiles = -(-m // 256) * (n // 256)
+    assert (configs.choose(m, n, k, wbits, 2).kernel == configs.PAIR) == (tiles >= 32)
     seed = wbits * 433 + n + k + m + flags
     codes, w = _codes(wbits, n, k, seed)
     q, qs = _activations(2, m, k, seed)
     alpha, bias = _channel(n, seed, m % 2 == 1)
-    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags, out=out)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags, out=out, pair_only=True)
     want, want_acc = oracle.reference(q, qs, w, alpha, bias, flags)
     _check(y, acc, want, want_acc, flags)
 
@@ -610,3 +613,37 @@ def test_graph_capture_replays_bitwise():
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(y, first)
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("n,k,m,parts,kernel", [(1024, 1024, 2, 1, configs.GEMV), (4096, 1024, 125, 1, configs.PER_TILE),
+                                                (1024, 4096, 38, 1, configs.PER_TILE),
+                                                (1024, 1024, 40, 3, configs.PER_TILE),
+                                                (300, 200, 77, 2, configs.PER_TILE), (4096, 1024, 2048, 1, configs.PAIR),
+                                                (4096, 1024, 8192, 2, configs.PAIR)])
+@pytest.mark.parametrize("scale", [1.0, 0.5])
+def test_residual_epilogue_equals_unfused(wbits, n, k, m, parts, kernel, scale):
+    """The skip connection in the epilogue (CUDA-core, per-tile with and without split-K and stacked parts, pair
+    with one and two parts): bit for bit PyTorch's `residual + scale * y`, also written in place over the residual."""
+    assert configs.choose(m, n, k, wbits, parts).kernel == kernel
+    seed = wbits * 7 + n + k + m + parts
+    codes, _ = _codes(wbits, n, k, seed)
+    q, qs = _activations(parts, m, k, seed)
+    alpha, bias = _channel(n, seed, True)
+    panels = lowbit.prepare_panels(torch.from_numpy(codes).to(DEV), wbits, n, k)
+    qd, qsd = torch.from_numpy(q).to(DEV), torch.from_numpy(qs).to(DEV)
+    ad, bd = torch.from_numpy(alpha).to(DEV), torch.from_numpy(bias).to(DEV)
+    res = torch.randn(m, n, generator=torch.Generator().manual_seed(seed)).to(DEV)
+    y = torch.empty(m, n, device=DEV)
+    lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, y, parts=parts)
+    want = res + scale * y
+    fused = torch.empty(m, n, device=DEV)
+    lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, fused, parts=parts, residual=res,
+                residual_scale=scale)
+    inplace = res.clone()
+    lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, inplace, parts=parts, residual=inplace,
+                residual_scale=scale)
+    torch.cuda.synchronize()
+    assert _lib.read_device_error() == 0
+    assert torch.equal(fused.view(torch.int32), want.view(torch.int32))
+    assert torch.equal(inplace.view(torch.int32), want.view(torch.int32))

@@ -81,7 +81,11 @@ def test_small_m_splits_k_and_large_m_does_not():
 
 def _desc(**kw):
     d = _lib.GemmDesc()
-    assert [f[0] for f in d._fields_][-5:] == ["tile_m", "tile_n", "splits", "stages", "error_word"]
+    header = (ROOT / "include" / "kea_lowbit.h").read_text()
+    body = header[header.index("typedef struct KeaGemmDesc"):header.index("} KeaGemmDesc;")]
+    declared = re.findall(r"^\s+[\w ]+?\**\s*\**(\w+)(?:,\s*(\w+))?;", body, re.M)
+    names = [n for pair in declared for n in pair if n]
+    assert [f[0] for f in d._fields_] == names   # the ctypes mirror is the header's struct, field for field
     d.q, d.ldq, d.parts, d.qs, d.panels, d.wbits, d.n, d.k = 16, 1024, 1, 16, 16, 1, 4096, 1024
     d.alpha, d.y, d.ldy, d.y_dtype, d.m = 16, 16, 4096, 0, 125
     for key, value in kw.items():
@@ -100,6 +104,11 @@ def test_c_abi_argument_errors_are_reported_before_any_device_work():
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(ldq=1000)), None) == _lib.INVALID_VALUE   # ldq < k
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(ldq=1032, k=1030)), None) == _lib.ALIGNMENT  # ldq % 16
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=64)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(residual=16, ld_residual=4095)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(residual=16, ld_residual=4096, y_dtype=1)), None) == \
+        _lib.INVALID_VALUE                                # a residual needs FP32 output
+    both = _lib.FLAG_NO_PAIR | _lib.FLAG_FORCE_PAIR   # contradictory pair flags
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=both)), None) == _lib.INVALID_VALUE
     assert lib.kea_lowbit_prepare(None, 1, 4, 8, None, None, None) == _lib.INVALID_VALUE
     with pytest.raises(ValueError):
         _lib.check(_lib.ALIGNMENT, "gemm")
