@@ -193,6 +193,26 @@ enum { KEA_CONV_PDL = 1 };
 
 int kea_lowbit_glu_depthwise(const KeaConvDesc *desc, void *stream);
 
+/* Relative-position self-attention of the FastConformer, FP32, one kernel (online softmax, no T x T buffer):
+ *   score[i, j] = ((q_i + bias_u) . k_j + (q_i + bias_v) . pos[j + t - 1 - i]) * scale, keys j >= lengths[b] masked,
+ *   ctx_i = softmax_j(score[i, :]) . v_j,
+ * qkv FP32 [b][t][3][h][dk] (q, k, v of one token row), pos FP32 [2t - 1][h][dk] (the position projection of the
+ * relative positions t - 1 .. -(t - 1)), bias_u / bias_v FP32 [h][dk], ctx FP32 [b][t][h][dk]; dk 32, 64 or 128;
+ * 16-byte aligned buffers. No reference C counterpart: replaces the reference's fused relative attention
+ * (src/kea_kernels/ternary/fused_kernels.py, relative_attention) and NeMo's RelPositionMultiHeadAttention math. */
+typedef struct KeaAttentionDesc {
+    const float *qkv;
+    const float *pos;
+    const float *bias_u, *bias_v;
+    const int32_t *lengths;   /* [b] key frames per clip, or NULL */
+    float *ctx;
+    int32_t b, t, h, dk;
+    float scale;
+    int32_t flags;            /* KEA_CONV_PDL */
+} KeaAttentionDesc;
+
+int kea_lowbit_rel_attention(const KeaAttentionDesc *desc, void *stream);
+
 /* Reads and clears the library's own device error word on the current device. Synchronizes the device. */
 int kea_lowbit_read_error(uint32_t *out);
 

@@ -13,6 +13,7 @@
 #include "gemm_pair_kernel.cuh"
 #include "gemv_kernel.cuh"
 #include "conv_kernels.cuh"
+#include "attention_kernels.cuh"
 #include "aux_kernels.cuh"
 
 namespace {
@@ -89,6 +90,15 @@ int device_setup(int *device_out) {
         if (cudaFuncSetAttribute((const void *)kea::quantize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  64 * 1024) != cudaSuccess)
             status = KEA_ERR_CUDA;
+        const void *attn_kernels[3] = {(const void *)kea::rel_attention_kernel<32>,
+                                       (const void *)kea::rel_attention_kernel<64>,
+                                       (const void *)kea::rel_attention_kernel<128>};
+        const int attn_smem[3] = {kea::attn_smem_floats<32>() * 4, kea::attn_smem_floats<64>() * 4,
+                                  kea::attn_smem_floats<128>() * 4};
+        for (int i = 0; i < 3; ++i)
+            if (cudaFuncSetAttribute(attn_kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem[i]) !=
+                cudaSuccess)
+                status = KEA_ERR_CUDA;
         const void *gemv_kernels[18] = {
 #define KEA_GEMV_MT(W, P) (const void *)kea::lowbit_gemv_kernel<W, P, 1>, (const void *)kea::lowbit_gemv_kernel<W, P, 4>, \
                           (const void *)kea::lowbit_gemv_kernel<W, P, 16>
@@ -491,6 +501,12 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
 
 }  // namespace
 
+template <int DK>
+cudaError_t launch_rel_attention(cudaLaunchConfig_t *cfg, const kea::RelAttnArgs &a) {
+    cfg->dynamicSmemBytes = (size_t)kea::attn_smem_floats<DK>() * sizeof(float);
+    return cudaLaunchKernelEx(cfg, kea::rel_attention_kernel<DK>, a);
+}
+
 template <int KW>
 cudaError_t launch_glu_dw(cudaLaunchConfig_t *cfg, const kea::ConvArgs &a) {
     return cudaLaunchKernelEx(cfg, kea::glu_depthwise_kernel<KW>, a);
@@ -546,6 +562,50 @@ int kea_lowbit_prepare(const uint8_t *codes, int32_t wbits, int32_t n, int32_t k
     kea::prepare_panels_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(codes, row_bytes, wbits, n, k, kb, rows,
                                                                           panels, error_word);
     return cudaGetLastError() == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
+}
+
+int kea_lowbit_rel_attention(const KeaAttentionDesc *d, void *stream) {
+    if (!d || !d->qkv || !d->pos || !d->bias_u || !d->bias_v || !d->ctx || d->b < 0 || d->t < 0 || d->h < 1 ||
+        (d->flags & ~KEA_CONV_PDL))
+        return KEA_ERR_INVALID_VALUE;
+    if (d->dk != 32 && d->dk != 64 && d->dk != 128) return KEA_ERR_UNSUPPORTED;
+    if (!aligned16(d->qkv) || !aligned16(d->pos) || !aligned16(d->bias_u) || !aligned16(d->bias_v) ||
+        !aligned16(d->ctx))
+        return KEA_ERR_ALIGNMENT;
+    if (d->b == 0 || d->t == 0) return KEA_OK;
+    if (d->b > 65535 || d->h > 65535) return KEA_ERR_UNSUPPORTED;
+    int dev = 0;
+    const int st = device_setup(&dev);
+    if (st != KEA_OK) return st;
+    kea::RelAttnArgs a{};
+    a.qkv = d->qkv;
+    a.pos = d->pos;
+    a.bias_u = d->bias_u;
+    a.bias_v = d->bias_v;
+    a.lengths = d->lengths;
+    a.ctx = d->ctx;
+    a.B = d->b;
+    a.T = d->t;
+    a.H = d->h;
+    a.scale = d->scale;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ceil_div(d->t, kea::kAttnQ), (unsigned)d->h, (unsigned)d->b);
+    cfg.blockDim = dim3(kea::kAttnThreads, 1, 1);
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    if (d->flags & KEA_CONV_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 1;
+    }
+    const cudaError_t e = d->dk == 128 ? launch_rel_attention<128>(&cfg, a)
+                          : d->dk == 64 ? launch_rel_attention<64>(&cfg, a) : launch_rel_attention<32>(&cfg, a);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return KEA_ERR_CUDA;
+    }
+    return KEA_OK;
 }
 
 int kea_lowbit_glu_depthwise(const KeaConvDesc *d, void *stream) {

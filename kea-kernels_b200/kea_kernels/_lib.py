@@ -23,8 +23,8 @@ DEVERR_TIMEOUT, DEVERR_TAIL_BITS, DEVERR_TERNARY_11 = 1, 2, 4
 
 # Every symbol include/kea_lowbit.h declares.
 EXPORTS = ("kea_lowbit_gemm", "kea_lowbit_choose_config", "kea_lowbit_panel_bytes", "kea_lowbit_prepare",
-           "kea_lowbit_quantize", "kea_lowbit_glu_depthwise", "kea_lowbit_read_error", "kea_lowbit_status_string",
-           "kea_lowbit_version")
+           "kea_lowbit_quantize", "kea_lowbit_glu_depthwise", "kea_lowbit_rel_attention", "kea_lowbit_read_error",
+           "kea_lowbit_status_string", "kea_lowbit_version")
 CONV_PDL = 1
 
 
@@ -65,6 +65,13 @@ class ConvDesc(ctypes.Structure):
                 ("kw", ctypes.c_int32), ("flags", ctypes.c_int32)]
 
 
+class AttentionDesc(ctypes.Structure):
+    _fields_ = [("qkv", ctypes.c_void_p), ("pos", ctypes.c_void_p), ("bias_u", ctypes.c_void_p),
+                ("bias_v", ctypes.c_void_p), ("lengths", ctypes.c_void_p), ("ctx", ctypes.c_void_p),
+                ("b", ctypes.c_int32), ("t", ctypes.c_int32), ("h", ctypes.c_int32), ("dk", ctypes.c_int32),
+                ("scale", ctypes.c_float), ("flags", ctypes.c_int32)]
+
+
 _lib = None
 
 
@@ -89,6 +96,8 @@ def lib() -> ctypes.CDLL:
         handle.kea_lowbit_quantize.restype = ctypes.c_int
         handle.kea_lowbit_glu_depthwise.argtypes = [ctypes.POINTER(ConvDesc), ctypes.c_void_p]
         handle.kea_lowbit_glu_depthwise.restype = ctypes.c_int
+        handle.kea_lowbit_rel_attention.argtypes = [ctypes.POINTER(AttentionDesc), ctypes.c_void_p]
+        handle.kea_lowbit_rel_attention.restype = ctypes.c_int
         handle.kea_lowbit_read_error.argtypes = [ctypes.POINTER(ctypes.c_uint32)]
         handle.kea_lowbit_read_error.restype = ctypes.c_int
         handle.kea_lowbit_status_string.argtypes = [ctypes.c_int]

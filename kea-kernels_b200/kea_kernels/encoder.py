@@ -157,21 +157,14 @@ class ConformerLayer(nn.Module):
             self._pos_cache[t] = p
         return p
 
-    def attention(self, x: Tensor, keys: Tensor | None = None) -> Tensor:
-        """keys: optional bool [b, 1, 1, t], False at padded frames (masked out as keys)."""
+    def attention(self, x: Tensor, lengths: Tensor | None = None) -> Tensor:
+        """Relative-position MHSA: LayerNorm fused into the QKV quantizer, the attention itself one FP32 kernel
+        (both position biases, the shifted position scores, key masking past `lengths`, online softmax) reading the
+        QKV GEMM's rows and writing the out projection's, whose epilogue adds the skip connection."""
         b, t, _ = x.shape
-        qkv = self.lin["qkv"](x, norm=self.norms["att"]).view(b, t, 3, self.heads, self.dk)
-        q, k, v = qkv.unbind(2)                                         # [b, t, h, dk]
-        p = self.positions(t, x.device).view(2 * t - 1, self.heads, self.dk)
-        q_u = (q + self.pos_bias_u).transpose(1, 2)                     # [b, h, t, dk]
-        q_v = (q + self.pos_bias_v).transpose(1, 2)
-        ac = torch.matmul(q_u, k.permute(0, 2, 3, 1))                   # [b, h, t, t]
-        bd = rel_shift(torch.matmul(q_v, p.permute(1, 2, 0)))           # [b, h, t, t]
-        scores = (ac + bd) * (1.0 / math.sqrt(self.dk))
-        if keys is not None:
-            scores = scores.masked_fill(~keys, float("-inf"))
-        attn = torch.softmax(scores, dim=-1)
-        ctx = torch.matmul(attn, v.transpose(1, 2)).transpose(1, 2).reshape(b, t, self.d)
+        qkv = self.lin["qkv"](x, norm=self.norms["att"])                # [b, t, 3 d]: q, k, v by heads
+        ctx = lowbit.rel_attention(qkv, self.positions(t, x.device), self.pos_bias_u, self.pos_bias_v, self.heads,
+                                   lengths)
         return self.lin["out"](ctx, residual=x)                          # x + out(ctx)
 
     def conv(self, x: Tensor, lengths: Tensor | None = None) -> Tensor:
@@ -182,11 +175,11 @@ class ConformerLayer(nn.Module):
         h = lowbit.glu_depthwise(h, self.dw_weight, self.dw_bias, lengths)   # [b, t, d]
         return self.lin["pw2"](h, input_silu=True, residual=x)          # SiLU in the quantizer; x + pw2(...)
 
-    def forward(self, x: Tensor, keys: Tensor | None = None, lengths: Tensor | None = None) -> Tensor:
+    def forward(self, x: Tensor, lengths: Tensor | None = None) -> Tensor:
         # every skip connection is added in the epilogue of the GEMM that ends its branch (x + 0.5 ff, x + att, ...)
         x = self.lin["ff1_down"](self.lin["ff1_up"](x, norm=self.norms["ff1"], silu=True), residual=x,
                                  residual_scale=0.5)
-        x = self.attention(x, keys)
+        x = self.attention(x, lengths)
         x = self.conv(x, lengths)
         x = self.lin["ff2_down"](self.lin["ff2_up"](x, norm=self.norms["ff2"], silu=True), residual=x,
                                  residual_scale=0.5)
@@ -256,13 +249,9 @@ class FastConformerEncoder(nn.Module):
         zeroed before the depthwise convolution, so a clip's real frames do not depend on the padding (the
         length-bucketed batches of mixed-length clips)."""
         x = self.pre(mel)
-        keys = lens = None
-        if lengths is not None:
-            t = x.shape[1]
-            lens = lengths.to(device=x.device, dtype=torch.int32)
-            keys = (torch.arange(t, device=x.device)[None, :] < lens[:, None])[:, None, None, :]   # [b, 1, 1, t]
+        lens = None if lengths is None else lengths.to(device=x.device, dtype=torch.int32)
         for layer in self.layers:
-            x = layer(x, keys, lens)
+            x = layer(x, lens)
         return x
 
     def gemm_shapes(self, batch: int, t: int) -> list[tuple[str, int, int, int]]:

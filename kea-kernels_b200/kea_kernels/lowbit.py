@@ -12,6 +12,7 @@ writes caller-owned outputs, so it can be captured in a CUDA graph.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 from torch import Tensor
@@ -165,3 +166,36 @@ def glu_depthwise(h: Tensor, weight: Tensor, bias: Tensor | None = None, lengths
     with torch.cuda.device(h.device):
         _lib.check(_lib.lib().kea_lowbit_glu_depthwise(ctypes.byref(d), _lib.stream_handle(h.device)), "glu_depthwise")
     return y
+
+
+def rel_attention(qkv: Tensor, pos: Tensor, bias_u: Tensor, bias_v: Tensor, heads: int,
+                  lengths: Tensor | None = None, *, pdl: bool = False) -> Tensor:
+    """Relative-position self-attention in one kernel: qkv FP32 [B, T, 3 * H * DK] (q, k, v of each token, heads
+    inside), pos FP32 [2T - 1, H * DK] (the position projection of relative positions T - 1 .. -(T - 1)),
+    bias_u / bias_v [H, DK] -> ctx FP32 [B, T, H * DK]; keys at frames >= lengths[b] are masked."""
+    _require_cuda(qkv, "qkv")
+    if qkv.dtype != torch.float32 or qkv.dim() != 3 or not qkv.is_contiguous() or qkv.shape[2] % (3 * heads):
+        raise ValueError("qkv must be contiguous FP32 [B, T, 3 * H * DK]")
+    b, t, w3 = qkv.shape
+    d = w3 // 3
+    dk = d // heads
+    pos = pos.reshape(-1, d)
+    if pos.dtype != torch.float32 or pos.shape[0] != max(0, 2 * t - 1) or pos.device != qkv.device:
+        raise ValueError(f"pos must be FP32 [{2 * t - 1}, {d}] on {qkv.device}")
+    pos = pos.contiguous()
+    bu, bv = bias_u.contiguous(), bias_v.contiguous()
+    for name, x in (("bias_u", bu), ("bias_v", bv)):
+        if x.dtype != torch.float32 or x.numel() != d or x.device != qkv.device:
+            raise ValueError(f"{name} must be FP32 [{heads}, {dk}] on {qkv.device}")
+    if lengths is not None:
+        if tuple(lengths.shape) != (b,) or lengths.device != qkv.device:
+            raise ValueError(f"lengths must be [{b}] on {qkv.device}")
+        lengths = lengths.to(torch.int32).contiguous()
+    ctx = torch.empty(b, t, d, device=qkv.device, dtype=torch.float32)
+    desc = _lib.AttentionDesc(qkv=qkv.data_ptr(), pos=pos.data_ptr(), bias_u=bu.data_ptr(), bias_v=bv.data_ptr(),
+                              lengths=_lib.ptr(lengths), ctx=ctx.data_ptr(), b=b, t=t, h=heads, dk=dk,
+                              scale=1.0 / math.sqrt(dk), flags=_lib.CONV_PDL if pdl else 0)
+    with torch.cuda.device(qkv.device):
+        _lib.check(_lib.lib().kea_lowbit_rel_attention(ctypes.byref(desc), _lib.stream_handle(qkv.device)),
+                   "rel_attention")
+    return ctx

@@ -151,3 +151,37 @@ def test_glu_depthwise_rejects_bad_arguments():
         lowbit.glu_depthwise(h, torch.randn(3, 1, 9, device=DEV))     # channel count
     with pytest.raises(ValueError):
         lowbit.glu_depthwise(h.transpose(1, 2), torch.randn(4, 1, 9, device=DEV))
+
+
+def _torch_rel_attention(qkv, pos, u, v, heads, lengths=None):
+    b, t, w3 = qkv.shape
+    d = w3 // 3
+    dk = d // heads
+    q, k, vv = qkv.view(b, t, 3, heads, dk).unbind(2)
+    p = pos.view(2 * t - 1, heads, dk)
+    ac = torch.matmul((q + u).transpose(1, 2), k.permute(0, 2, 3, 1))
+    bd = E.rel_shift(torch.matmul((q + v).transpose(1, 2), p.permute(1, 2, 0)))
+    s = (ac + bd) * (1.0 / math.sqrt(dk))
+    if lengths is not None:
+        s = s.masked_fill(~(torch.arange(t, device=qkv.device)[None, :] < lengths[:, None])[:, None, None, :],
+                          float("-inf"))
+    return torch.matmul(torch.softmax(s, dim=-1), vv.transpose(1, 2)).transpose(1, 2).reshape(b, t, d)
+
+
+@pytest.mark.parametrize("b,t,heads,dk", [(2, 125, 8, 128), (1, 7, 2, 32), (3, 33, 4, 64), (1, 375, 8, 128),
+                                          (2, 64, 1, 32)])
+@pytest.mark.parametrize("masked", [False, True])
+@torch.inference_mode()
+def test_rel_attention_matches_torch(b, t, heads, dk, masked):
+    """The fused relative-position attention against the torch sequence it replaces (bias adds, two score matmuls,
+    Transformer-XL shift, scale, key mask, softmax, context matmul), FP32 within summation-order rounding."""
+    from kea_kernels import lowbit
+    g = torch.Generator().manual_seed(b * 100 + t + heads + dk)
+    d = heads * dk
+    qkv = torch.randn(b, t, 3 * d, generator=g).to(DEV)
+    pos = torch.randn(2 * t - 1, d, generator=g).to(DEV)
+    u, v = (0.1 * torch.randn(heads, dk, generator=g)).to(DEV), (0.1 * torch.randn(heads, dk, generator=g)).to(DEV)
+    lengths = torch.randint(1, t + 1, (b,), generator=g).to(DEV) if masked else None
+    got = lowbit.rel_attention(qkv, pos, u, v, heads, lengths)
+    want = _torch_rel_attention(qkv, pos, u, v, heads, lengths)
+    torch.testing.assert_close(got, want, rtol=1e-4, atol=2e-5)
