@@ -104,6 +104,31 @@ def rel_shift(x: Tensor) -> Tensor:
     return x[:, :, :, : t]
 
 
+def torch_rel_attention(qkv: Tensor, pos: Tensor, bias_u: Tensor, bias_v: Tensor, heads: int,
+                        lengths: Tensor | None = None) -> Tensor:
+    """The relative-position attention as PyTorch FP32 ops (NeMo's RelPositionMultiHeadAttention math): the same
+    function as lowbit.rel_attention, used where that kernel measured slower (one clip: too few CTAs; long clips)."""
+    b, t, w3 = qkv.shape
+    d = w3 // 3
+    dk = d // heads
+    q, k, v = qkv.view(b, t, 3, heads, dk).unbind(2)                   # [b, t, h, dk]
+    p = pos.view(2 * t - 1, heads, dk)
+    ac = torch.matmul((q + bias_u).transpose(1, 2), k.permute(0, 2, 3, 1))            # [b, h, t, t]
+    bd = rel_shift(torch.matmul((q + bias_v).transpose(1, 2), p.permute(1, 2, 0)))   # [b, h, t, t]
+    scores = (ac + bd) * (1.0 / math.sqrt(dk))
+    if lengths is not None:
+        keys = torch.arange(t, device=qkv.device)[None, :] < lengths.to(qkv.device)[:, None]
+        scores = scores.masked_fill(~keys[:, None, None, :], float("-inf"))
+    attn = torch.softmax(scores, dim=-1)
+    return torch.matmul(attn, v.transpose(1, 2)).transpose(1, 2).reshape(b, t, d)
+
+
+# The fused FP32 attention kernel measured faster than the PyTorch sequence from 16 (clip, head) pairs up to clips of
+# ~200 frames (B200: 1.5x at 4 clips of 125 frames, 1.2x at 256); one clip gives it too few CTAs and 375-frame clips
+# favour the library matmuls.
+FUSED_ATTENTION_MIN_ROWS, FUSED_ATTENTION_MAX_T = 16, 192
+
+
 def rel_positions(t: int, d: int, device) -> Tensor:
     """Sinusoidal table for relative positions t - 1 ... -(t - 1): [2 t - 1, d]."""
     pos = torch.arange(t - 1, -t, -1, device=device, dtype=torch.float32)[:, None]
@@ -163,8 +188,9 @@ class ConformerLayer(nn.Module):
         QKV GEMM's rows and writing the out projection's, whose epilogue adds the skip connection."""
         b, t, _ = x.shape
         qkv = self.lin["qkv"](x, norm=self.norms["att"])                # [b, t, 3 d]: q, k, v by heads
-        ctx = lowbit.rel_attention(qkv, self.positions(t, x.device), self.pos_bias_u, self.pos_bias_v, self.heads,
-                                   lengths)
+        attend = lowbit.rel_attention if (b * self.heads >= FUSED_ATTENTION_MIN_ROWS and
+                                          t <= FUSED_ATTENTION_MAX_T) else torch_rel_attention
+        ctx = attend(qkv, self.positions(t, x.device), self.pos_bias_u, self.pos_bias_v, self.heads, lengths)
         return self.lin["out"](ctx, residual=x)                          # x + out(ctx)
 
     def conv(self, x: Tensor, lengths: Tensor | None = None) -> Tensor:

@@ -185,3 +185,5 @@ def test_rel_attention_matches_torch(b, t, heads, dk, masked):
     got = lowbit.rel_attention(qkv, pos, u, v, heads, lengths)
     want = _torch_rel_attention(qkv, pos, u, v, heads, lengths)
     torch.testing.assert_close(got, want, rtol=1e-4, atol=2e-5)
+    # the encoder's own PyTorch route (small batches, long clips) is the same function
+    torch.testing.assert_close(E.torch_rel_attention(qkv, pos, u, v, heads, lengths), want, rtol=1e-5, atol=1e-6)
