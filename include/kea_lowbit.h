@@ -109,6 +109,12 @@ typedef struct KeaGemmDesc {
                                  y itself: every element is read before it is written, by the same thread */
     int64_t ld_residual;
     float residual_scale;
+    void *workspace;          /* NULL, or device scratch of workspace_bytes (16-byte aligned) for split-K of the pair
+                                 kernel: where a shape has too few 256 x 256 tiles to occupy the GPU, its K range is
+                                 cut into slices whose INT32 partial sums go here and are finished by a second kernel
+                                 (same bits). kea_lowbit_workspace_bytes says how much a shape uses; with less (or
+                                 NULL) the GEMM runs unsplit. Calls sharing a workspace must not overlap on the GPU. */
+    int64_t workspace_bytes;
 } KeaGemmDesc;
 
 /* Tile configuration picked for a shape (the M-bucketed split-K dispatch table). */
@@ -132,6 +138,11 @@ int kea_lowbit_choose_config(int32_t m, int32_t n, int32_t k, int32_t wbits, int
 /* Bytes of the prepared panel layout: ceil(n/128) * ceil(k/128) * wbits * 2048.
  * Replaces kernels.fragment_bytes (src/kea_kernels/binary/kernels.py:726-727). */
 size_t kea_lowbit_panel_bytes(int32_t wbits, int32_t n, int32_t k);
+
+/* Scratch bytes kea_lowbit_gemm uses for split-K at this shape under the dispatch table (0: none):
+ * slices x parts x m x n x 4. Replaces the reference's per-call workspace sizing
+ * (src/kea_kernels/binary/kernels.py:640-700, DotConfig workspace; allocated per call at layer.py:194-195). */
+size_t kea_lowbit_workspace_bytes(int32_t m, int32_t n, int32_t k, int32_t wbits, int32_t parts);
 
 /* Re-lays export codes (uint8 [n][ceil(k*wbits/8)] on the device; parakeet-binary-v1 LSB-first signs or
  * parakeet-ternary-v1 2-bit fields) into panels of kea_lowbit_panel_bytes bytes, and checks the codes:

@@ -61,6 +61,9 @@ struct PairArgs {
     long long ld_acc, acc_stride;
     int M, N, K, kb_total;
     int n_tiles, tiles;          // 256-channel tiles, pair tiles in all
+    int splits, kbs, items;      // K slices per tile, k-blocks per slice, work items = tiles x splits
+    int *ws;                     // splits > 1: INT32 partial sums [splits][P][M][N] (scratch), finished by
+                                 // splitk_finish_kernel; null otherwise
     int flags;                   // KEA_FLAG_SILU, KEA_FLAG_ORDER1
     const float *res;            // residual FP32 [M][ld_res] (16-byte rows) or null: y = res + res_scale * value
     long long ld_res;
@@ -107,6 +110,14 @@ KEA_DEVI float finish2(int lo, int hi, float s_lo, float s_hi, float alpha, floa
     float y = BIAS ? __fmaf_rn(r, alpha, bias) : __fmul_rn(r, alpha);
     if constexpr (SILU) y = silu_approx(y);
     return y;
+}
+
+// Work item w: pair tile w % tiles over k-blocks [kb0, kb1) of slice w / tiles (one slice when not split).
+KEA_DEVI void pair_item(const PairArgs &a, int w, int &tile, int &slice, int &kb0, int &kb1) {
+    tile = w % a.tiles;
+    slice = w / a.tiles;
+    kb0 = slice * a.kbs;
+    kb1 = min(a.kb_total, kb0 + a.kbs);
 }
 
 // One epilogue warp's share of a finished tile: its 32 token rows x 128 channels of tensor memory in four chunks of
@@ -301,6 +312,36 @@ KEA_DEVI void pair_epilogue_tile2(const PairArgs &a, const CUtensorMap *ymap, ui
     }
 }
 
+// A K slice's raw INT32 sums of one warp's 32 token rows x 128 channels (every part) into the scratch partials.
+template <int P>
+KEA_DEVI void pair_partial_tile(const PairArgs &a, uint32_t cbase, uint32_t acc_empty, int nbase, int t, int slice) {
+    const int lane = threadIdx.x & 31;
+    uint32_t v[P][32];
+#pragma unroll 1
+    for (int ci = 0; ci < 4; ++ci) {
+#pragma unroll
+        for (int p = 0; p < P; ++p) pair_load32(cbase + (uint32_t)p * kPairAccCols + (uint32_t)(32 * ci), v[p]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int p = 0; p < P; ++p) tmem_regs_ready(v[p]);
+        if (ci == 3) {   // every TMEM read of the buffer is done: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc_empty);
+        }
+        if (t < a.M) {
+#pragma unroll
+            for (int p = 0; p < P; ++p) {
+                int4 *dst = reinterpret_cast<int4 *>(a.ws + (((long long)slice * P + p) * a.M + t) * a.N + nbase +
+                                                     32 * ci);
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    dst[q] = make_int4((int)v[p][4 * q], (int)v[p][4 * q + 1], (int)v[p][4 * q + 2], (int)v[p][4 * q + 3]);
+            }
+        }
+    }
+}
+
 template <int WBITS, int P>
 __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                           const __grid_constant__ CUtensorMap ymap,
@@ -379,11 +420,13 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
             uint32_t ph = 0;
             long long issued = 0;
             const uint32_t tx = ASLOT + PKB;
-            for (int tile = pair; tile < a.tiles && ok; tile += npairs) {
+            for (int w = pair; w < a.items && ok; w += npairs) {
+                int tile, slice, kb0, kb1;
+                pair_item(a, w, tile, slice, kb0, kb1);
                 const int mt = tile / a.n_tiles, nt = tile - mt * a.n_tiles;
                 const int t0 = mt * kPairTileM + (int)rank * kBM;
                 const uint8_t *wsrc = a.panels + (size_t)(nt * 2 + (int)rank) * (size_t)kbt * PKB;
-                for (int kb = 0; kb < kbt; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (issued >= S && !mbar_wait(smem_u32(&bar_empty[s]), ph ^ 1u, kWaitBudget)) {
                         ok = false;
                         break;
@@ -415,7 +458,9 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
             const uint32_t idesc = idesc_i8(2 * kBM, (uint32_t)kPairTileN);
             const uint64_t ad0 = sw128_kmajor_desc(A0), bd0 = sw128_kmajor_desc(B0);
             int j = 0, step = 0;
-            for (int tile = pair; tile < a.tiles; tile += npairs, ++j) {
+            for (int w = pair; w < a.items; w += npairs, ++j) {
+                int tile, slice, kb0, kb1;
+                pair_item(a, w, tile, slice, kb0, kb1);
                 const int buf = j % NBUF;
                 const uint32_t use = (uint32_t)(j / NBUF);
                 if (j >= NBUF) {
@@ -427,7 +472,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                 }
                 tc_fence_after();
                 const uint32_t dcol = tmem + (uint32_t)buf * kPairAccCols;
-                for (int kb = 0; kb < kbt; ++kb, ++step) {
+                for (int kb = kb0; kb < kb1; ++kb, ++step) {
                     const int sa = step % S, sb = step % kPairBStages;
                     const bool ready = mbar_wait_cluster(smem_u32(&bar_ready[sb]), (uint32_t)((step / kPairBStages) & 1),
                                                          kWaitBudget);
@@ -445,7 +490,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                             for (int kk = 0; kk < 4; ++kk)   // K = 32 per MMA: + 32 bytes = 2 descriptor units
                                 mma_i8_pair(dcol + (uint32_t)p * kPairAccCols,
                                             ad + (uint64_t)((p * kPairHalfTile) >> 4) + (uint64_t)(kk * 2),
-                                            bd + (uint64_t)(kk * 2), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                                            bd + (uint64_t)(kk * 2), idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
                         mma_commit_pair(smem_u32(&bar_empty[sa]), (uint16_t)3);
                         mma_commit_pair(smem_u32(&bar_bempty[sb]), (uint16_t)3);
                     }
@@ -471,9 +516,12 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
         const int e = threadIdx.x - (kPairExpWarp0 + eg * kPairExpGroupWarps) * 32;   // thread within the group
         const uint32_t ready0 = map_to_rank(smem_u32(&bar_ready[0]), 0u);
         constexpr int units = kPanelN * (WBITS == 1 ? 4 : 8);
-        int my_tiles = 0;
-        for (int tile = pair; tile < a.tiles; tile += npairs) ++my_tiles;
-        const int steps = my_tiles * kbt;
+        int steps = 0;   // k-blocks of this pair's work items, in order
+        for (int w = pair; w < a.items; w += npairs) {
+            int tile, slice, kb0, kb1;
+            pair_item(a, w, tile, slice, kb0, kb1);
+            steps += kb1 - kb0;
+        }
         for (int step = eg; step < steps; step += kPairExpGroups) {
             const int sa = step % S, sb = step % kPairBStages;
             // The MMAs that last read B slot sb (step - kPairBStages) are done, then the codes have landed. The order
@@ -511,7 +559,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
         const uint32_t acc_empty0 = map_to_rank(smem_u32(&bar_acc_empty[0]), 0u);
         const bool has_bias = a.bias != nullptr;
         int j = 0;
-        for (int tile = pair; tile < a.tiles; tile += npairs, ++j) {
+        for (int w = pair; w < a.items; w += npairs, ++j) {
+            const int tile = w % a.tiles;
             const int buf = j % NBUF;
             const uint32_t use = (uint32_t)(j / NBUF);
             const int mt = tile / a.n_tiles, nt = tile - mt * a.n_tiles;
@@ -542,6 +591,10 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
             const float sq1 = (P > 1 && t < a.M) ? __ldg(a.qs + a.qs_stride + t) : 0.f;
             const uint32_t cbase = lane_base + (uint32_t)buf * kPairAccCols + (uint32_t)(half * 128);
             const uint32_t acc_empty = acc_empty0 + (uint32_t)buf * 8u;
+            if (a.splits > 1) {   // a K slice: raw sums to the scratch partials, finished by splitk_finish_kernel
+                pair_partial_tile<P>(a, cbase, acc_empty, nbase, t, w / a.tiles);
+                continue;
+            }
             // one instantiation per (output type, bias, SiLU): no run-time branch inside the finishing loop
             const int variant = (a.y_f16 ? 4 : 0) | (has_bias ? 2 : 0) | (a.flags & 1);
 #define KEA_PAIR_EPI(F16, BIAS, SILU)                                                                             \
@@ -578,6 +631,70 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
         tmem_dealloc_pair(tmem, kPairTmemCols);
     }
     KEA_PTRACE(threadIdx.x == 0, 7, 2);
+}
+
+// Split-K finish: y[t, n .. n + 3] from the sum over K slices of the pair kernel's INT32 partials
+// ws[slice][part][M][N], with the tensor-core kernels' FP32 epilogue (finish_value: comb_P in the order flag's
+// order, alpha, bias, SiLU) and optional accumulator / residual outputs, so the result is bit-identical to the
+// unsplit pair kernel. One thread per 4 channels of a token; N is a multiple of 256 here.
+struct SplitFinishArgs {
+    const int *ws;
+    int splits, parts, M, N;
+    const float *qs;
+    long long qs_stride;
+    const float *alpha, *bias;
+    void *y;
+    long long ldy;
+    int y_f16;
+    int *acc;
+    long long ld_acc, acc_stride;
+    const float *res;
+    long long ld_res;
+    float res_scale;
+    int flags;
+};
+
+__global__ void __launch_bounds__(256) splitk_finish_kernel(const SplitFinishArgs a) {
+    grid_dependency_wait();
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;   // (token, 4-channel group)
+    const int groups = a.N / 4;
+    if (idx >= (long long)a.M * groups) return;
+    const int t = (int)(idx / groups), n = (int)(idx - (long long)t * groups) * 4;
+    int tot[3][4] = {};
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+        if (p >= a.parts) break;
+        for (int s = 0; s < a.splits; ++s) {
+            const int4 v = __ldg(reinterpret_cast<const int4 *>(a.ws + (((long long)s * a.parts + p) * a.M + t) * a.N + n));
+            tot[p][0] += v.x;
+            tot[p][1] += v.y;
+            tot[p][2] += v.z;
+            tot[p][3] += v.w;
+        }
+    }
+    float sq[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+        if (p < a.parts) sq[p] = __ldg(a.qs + p * a.qs_stride + t);
+    const bool has_bias = a.bias != nullptr;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float v = finish_value(tot[0][j], tot[1][j], tot[2][j], sq[0], sq[1], sq[2], a.parts, a.flags,
+                               __ldg(a.alpha + n + j), has_bias, has_bias ? __ldg(a.bias + n + j) : 0.f);
+        if (a.res) v = __fadd_rn(__ldg(a.res + (long long)t * a.ld_res + n + j), __fmul_rn(a.res_scale, v));
+        if (a.y_f16)
+            reinterpret_cast<__half *>(a.y)[(long long)t * a.ldy + n + j] = __float2half_rn(v);
+        else
+            reinterpret_cast<float *>(a.y)[(long long)t * a.ldy + n + j] = v;
+    }
+    if (a.acc) {
+#pragma unroll
+        for (int p = 0; p < 3; ++p)
+            if (p < a.parts)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) a.acc[p * a.acc_stride + (long long)t * a.ld_acc + n + j] = tot[p][j];
+    }
+    grid_launch_dependents();
 }
 
 }  // namespace kea

@@ -195,6 +195,26 @@ bool pair_shape(int m, int n, int k, int parts) {
     return pair_fits(m, n, k, parts) &&
            (parts == 1 || ceil_div(m, kea::kPairTileM) * (n / kea::kPairTileN) >= kPairMinTiles2);
 }
+// Split-K of the pair kernel: when the tiles occupy at most a quarter of the SM pairs and K is long (>= 16
+// k-blocks), each tile's K range is cut into slices (>= 4 k-blocks each, at most 8) so that tiles x slices approaches
+// the pair count; the slices' INT32 partial sums go through scratch memory and splitk_finish_kernel. Measured
+// (B200): N 1024, K 4096, M 512 (8 tiles, 8 slices) 16.5 us against 18.3 unsplit; with 32 tiles or K = 1024 the
+// pair kernel's fixed latency (~8 us a launch) dominates and the extra pass made it slower, hence the bounds.
+// Returns the slice count (1: unsplit).
+int pair_splits(int m, int n, int k, int sms) {
+    const int tiles = ceil_div(m, kea::kPairTileM) * (n / kea::kPairTileN), pairs = std::max(1, sms / 2);
+    const int kbt = ceil_div(k, kea::kBK);
+    if (4 * tiles > pairs || kbt < 16) return 1;
+    int s = std::min(std::min(pairs / tiles, kbt / 4), 8);
+    if (s < 2) return 1;
+    const int kbs = ceil_div(kbt, s);
+    return ceil_div(kbt, kbs);   // every slice non-empty
+}
+size_t pair_workspace_bytes(int m, int n, int k, int parts, int sms) {
+    const int s = pair_splits(m, n, k, sms);
+    return s > 1 ? (size_t)s * (size_t)parts * (size_t)m * (size_t)n * 4u : 0u;
+}
+
 KeaGemmConfig pair_config(int wbits, int parts) {
     KeaGemmConfig c{};
     c.tile_m = kea::kPairTileM;
@@ -464,7 +484,20 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
     a.y_f16 = esize == 2;
     a.stages = c.stages;
     a.err = d->error_word;
-    const int pairs = std::min(a.tiles, std::max(1, sms / 2));
+    // split-K through the caller's scratch, when the shape wants it and the workspace holds it
+    const int splits = pair_splits(d->m, d->n, d->k, sms);
+    const size_t ws_need = pair_workspace_bytes(d->m, d->n, d->k, d->parts, sms);
+    const bool split = splits > 1 && d->workspace && aligned16(d->workspace) &&
+                       (size_t)std::max<int64_t>(d->workspace_bytes, 0) >= ws_need;
+    a.splits = split ? splits : 1;
+    a.kbs = split ? ceil_div(a.kb_total, splits) : a.kb_total;
+    a.items = a.tiles * a.splits;
+    a.ws = split ? static_cast<int *>(d->workspace) : nullptr;
+    if (split) {   // the finish kernel writes y, acc and the residual sum
+        a.acc = nullptr;
+        a.res = nullptr;
+    }
+    const int pairs = std::min(a.items, std::max(1, sms / 2));
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
@@ -491,6 +524,41 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
         case 6: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<1, 2>, qmap, ymap, a); break;
         case 9: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<2, 1>, qmap, ymap, a); break;
         default: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<2, 2>, qmap, ymap, a); break;
+    }
+    if (e == cudaSuccess && split) {
+        kea::SplitFinishArgs f{};
+        f.ws = a.ws;
+        f.splits = splits;
+        f.parts = d->parts;
+        f.M = d->m;
+        f.N = d->n;
+        f.qs = d->qs;
+        f.qs_stride = d->qs_part_stride;
+        f.alpha = d->alpha;
+        f.bias = d->bias;
+        f.y = d->y;
+        f.ldy = d->ldy;
+        f.y_f16 = esize == 2;
+        f.acc = d->acc;
+        f.ld_acc = d->ld_acc;
+        f.acc_stride = d->acc_part_stride;
+        f.res = d->residual;
+        f.ld_res = d->ld_residual;
+        f.res_scale = d->residual_scale;
+        f.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
+        cudaLaunchConfig_t fc = {};
+        const long long threads = (long long)d->m * (d->n / 4);
+        fc.gridDim = dim3((unsigned)((threads + 255) / 256), 1, 1);
+        fc.blockDim = dim3(256, 1, 1);
+        fc.stream = (cudaStream_t)stream;
+        cudaLaunchAttribute fattr[1];
+        fc.attrs = fattr;
+        if (d->flags & KEA_FLAG_PDL) {   // its CTAs wait (griddepcontrol.wait) for the partial sums
+            fattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            fattr[0].val.programmaticStreamSerializationAllowed = 1;
+            fc.numAttrs = 1;
+        }
+        e = cudaLaunchKernelEx(&fc, kea::splitk_finish_kernel, f);
     }
     if (e != cudaSuccess) {
         cudaGetLastError();
@@ -534,6 +602,19 @@ const char *kea_lowbit_status_string(int status) {
 size_t kea_lowbit_panel_bytes(int32_t wbits, int32_t n, int32_t k) {
     if ((wbits != 1 && wbits != 2) || n < 1 || k < 1) return 0;
     return (size_t)ceil_div(n, kea::kPanelN) * (size_t)ceil_div(k, kea::kBK) * (size_t)wbits * kea::kPanelSubBytes;
+}
+
+size_t kea_lowbit_workspace_bytes(int32_t m, int32_t n, int32_t k, int32_t wbits, int32_t parts) {
+    if (m < 1 || n < 1 || k < 1 || (wbits != 1 && wbits != 2) || parts < 1 || parts > 3) return 0;
+    int sms = kSmsB200;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+    }
+    cudaGetLastError();   // no device here (a CPU host): size for a B200
+    const KeaGemmConfig c = choose(m, n, k, wbits, parts, sms);
+    return c.kernel == 1 ? pair_workspace_bytes(m, n, k, parts, sms) : 0u;
 }
 
 int kea_lowbit_choose_config(int32_t m, int32_t n, int32_t k, int32_t wbits, int32_t parts, KeaGemmConfig *out) {

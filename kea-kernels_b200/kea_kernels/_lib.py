@@ -22,7 +22,8 @@ QUANT_INPUT_SILU, QUANT_PDL = 1, 2
 DEVERR_TIMEOUT, DEVERR_TAIL_BITS, DEVERR_TERNARY_11 = 1, 2, 4
 
 # Every symbol include/kea_lowbit.h declares.
-EXPORTS = ("kea_lowbit_gemm", "kea_lowbit_choose_config", "kea_lowbit_panel_bytes", "kea_lowbit_prepare",
+EXPORTS = ("kea_lowbit_gemm", "kea_lowbit_choose_config", "kea_lowbit_panel_bytes", "kea_lowbit_workspace_bytes",
+           "kea_lowbit_prepare",
            "kea_lowbit_quantize", "kea_lowbit_glu_depthwise", "kea_lowbit_rel_attention", "kea_lowbit_read_error",
            "kea_lowbit_status_string", "kea_lowbit_version")
 CONV_PDL = 1
@@ -40,6 +41,7 @@ class GemmDesc(ctypes.Structure):
         ("tile_m", ctypes.c_int32), ("tile_n", ctypes.c_int32), ("splits", ctypes.c_int32),
         ("stages", ctypes.c_int32), ("error_word", ctypes.c_void_p),
         ("residual", ctypes.c_void_p), ("ld_residual", ctypes.c_int64), ("residual_scale", ctypes.c_float),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64),
     ]
 
 
@@ -89,6 +91,8 @@ def lib() -> ctypes.CDLL:
         handle.kea_lowbit_choose_config.restype = ctypes.c_int
         handle.kea_lowbit_panel_bytes.argtypes = [ctypes.c_int32] * 3
         handle.kea_lowbit_panel_bytes.restype = ctypes.c_size_t
+        handle.kea_lowbit_workspace_bytes.argtypes = [ctypes.c_int32] * 5
+        handle.kea_lowbit_workspace_bytes.restype = ctypes.c_size_t
         handle.kea_lowbit_prepare.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         handle.kea_lowbit_prepare.restype = ctypes.c_int
@@ -127,6 +131,11 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 def panel_bytes(wbits: int, n: int, k: int) -> int:
     return int(lib().kea_lowbit_panel_bytes(wbits, n, k))
+
+
+def workspace_bytes(m: int, n: int, k: int, wbits: int, parts: int) -> int:
+    """Scratch bytes the dispatch table's split-K uses at this shape (0: none)."""
+    return int(lib().kea_lowbit_workspace_bytes(m, n, k, wbits, parts))
 
 
 def choose_config(m: int, n: int, k: int, wbits: int, parts: int) -> GemmConfig:

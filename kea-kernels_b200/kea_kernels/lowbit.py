@@ -80,14 +80,17 @@ def quantize(x: Tensor, rows: tuple[int, int, int, int], m: int, k: int, parts: 
 def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n: int, k: int, alpha: Tensor,
          bias: Tensor | None, y: Tensor, *, parts: int, silu: bool = False, order: int = 0, acc: Tensor | None = None,
          config=None, pdl: bool = False, error_word: Tensor | None = None, pair: bool = True,
-         force_pair: bool = False, residual: Tensor | None = None, residual_scale: float = 1.0) -> None:
+         force_pair: bool = False, residual: Tensor | None = None, residual_scale: float = 1.0,
+         workspace: Tensor | None = None) -> None:
     """y[:m] (row stride y.stride(0); FP32 or FP16) from q int8 [parts, m, ldq] and qs FP32 [parts, m].
     acc, when given, receives the exact INT32 accumulators as int32 [parts, m, n] (any row / part strides).
     `config` forces the per-tile kernel's tiles, or (tile_m <= 16, m <= 16) the CUDA-core kernel's channels per CTA;
     a pair config from the table forces nothing. pair=False keeps the dispatch table away from the persistent
     CTA-pair kernel; force_pair=True takes it wherever its shape allows (also below the table's tile threshold).
     residual (FP32 [m, n], unit column stride; may be y itself) makes the epilogue write residual + residual_scale *
-    value, rounded as the unfused `residual + residual_scale * y` (FP32 y only)."""
+    value, rounded as the unfused `residual + residual_scale * y` (FP32 y only). workspace: scratch for the pair
+    kernel's split-K (few tiles, long K): None takes _lib.workspace_bytes of it from PyTorch's allocator when the
+    shape splits; a caller's uint8 CUDA tensor is used as given (an empty one runs the GEMM unsplit)."""
     if m == 0:
         return
     if parts not in (1, 2, 3):
@@ -135,6 +138,14 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
         d.tile_m, d.tile_n, d.splits, d.stages = config.tile_m, config.tile_n, config.splits, config.stages
     if error_word is not None:
         d.error_word = error_word.data_ptr()
+    if workspace is None and pair and d.tile_m == 0:
+        need = _lib.workspace_bytes(m, n, k, wbits, parts)
+        if need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=y.device)
+    if workspace is not None and workspace.numel():
+        if workspace.device != y.device or not workspace.is_contiguous():
+            raise ValueError("workspace must be a contiguous tensor on y's device")
+        d.workspace, d.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     with torch.cuda.device(y.device):
         _lib.check(_lib.lib().kea_lowbit_gemm(ctypes.byref(d), _lib.stream_handle(y.device)), "gemm")
 

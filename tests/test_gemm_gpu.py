@@ -647,3 +647,54 @@ def test_residual_epilogue_equals_unfused(wbits, n, k, m, parts, kernel, scale):
     assert _lib.read_device_error() == 0
     assert torch.equal(fused.view(torch.int32), want.view(torch.int32))
     assert torch.equal(inplace.view(torch.int32), want.view(torch.int32))
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("n,k,m,parts", [(1024, 4096, 512, 1), (1024, 8192, 1000, 1), (512, 4096, 700, 1),
+                                         (1024, 4096, 300, 2), (256, 2100, 600, 1)])
+@pytest.mark.parametrize("flags,out,extras", [(0, torch.float16, False), (2, torch.float32, True),
+                                              (1, torch.float32, True), (0, torch.float32, False)])
+def test_pair_split_k_equals_unsplit(wbits, n, k, m, parts, flags, out, extras):
+    """Few pair tiles, long K: the K range is cut into slices whose INT32 partial sums go through the scratch
+    workspace and a finishing kernel - bit for bit the unsplit pair kernel, accumulators and residual included."""
+    need = _lib.workspace_bytes(m, n, k, wbits, 1) * parts
+    assert need > 0
+    seed = wbits * 5 + n + k + m + parts + flags
+    codes, _ = _codes(wbits, n, k, seed)
+    q, qs = _activations(parts, m, k, seed)
+    alpha, bias = _channel(n, seed, extras)
+    panels = lowbit.prepare_panels(torch.from_numpy(codes).to(DEV), wbits, n, k)
+    qd, qsd = torch.from_numpy(q).to(DEV), torch.from_numpy(qs).to(DEV)
+    ad = torch.from_numpy(alpha).to(DEV)
+    bd = None if bias is None else torch.from_numpy(bias).to(DEV)
+    res = torch.randn(m, n, generator=torch.Generator().manual_seed(seed)).to(DEV) if out == torch.float32 and extras \
+        else None
+
+    def run(ws):
+        y = torch.full((m, n), float("nan"), device=DEV, dtype=out)
+        acc = torch.full((parts, m, n), -7, device=DEV, dtype=torch.int32) if extras else None
+        lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, y, parts=parts, silu=bool(flags & 1),
+                    order=(flags >> 1) & 1, acc=acc, force_pair=True, residual=res, workspace=ws)
+        return y, acc
+
+    ws = torch.full((need,), 0x5A, dtype=torch.uint8, device=DEV)   # stale contents must not matter
+    y_split, acc_split = run(ws)
+    y_one, acc_one = run(torch.empty(0, dtype=torch.uint8, device=DEV))
+    torch.cuda.synchronize()
+    assert _lib.read_device_error() == 0
+    bits_of = (lambda t: t.view(torch.int16)) if out == torch.float16 else (lambda t: t.view(torch.int32))
+    assert torch.equal(bits_of(y_split), bits_of(y_one))
+    if extras:
+        assert torch.equal(acc_split, acc_one)
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
+def test_pair_split_k_equals_oracle(wbits):
+    n, k, m = 1024, 4096, 512
+    assert _lib.workspace_bytes(m, n, k, wbits, 1) > 0       # the table's own split, workspace from gemm
+    codes, w = _codes(wbits, n, k, 404)
+    q, qs = _activations(1, m, k, 405)
+    alpha, bias = _channel(n, 406, True)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias)
+    want, want_acc = oracle.reference(q, qs, w, alpha, bias)
+    _check(y, acc, want, want_acc, 0)

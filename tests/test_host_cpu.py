@@ -228,3 +228,14 @@ def test_encoder_layer_shapes_are_the_parakeet_linears():
                                                     (2048, 1024), (1024, 1024), (4096, 1024), (1024, 4096)]
     assert shapes["linear_pos"] == (1024, 1024)
     assert sum(n * k for n, k in (shapes[x] for x in E.LAYER_LINEARS)) == 24_117_248   # 2.875 MiB of signs per layer
+
+
+def test_split_k_workspace_only_where_pair_tiles_are_few():
+    """Pair tiles filling at most a quarter of the SM pairs, with >= 16 k-blocks, split K through scratch: slices x
+    parts x M x N INT32; every other shape needs none."""
+    assert _lib.workspace_bytes(512, 1024, 4096, 1, 1) == 8 * 512 * 1024 * 4       # 8 tiles, 32 k-blocks: 8 slices
+    assert _lib.workspace_bytes(1000, 1024, 8192, 2, 1) == 4 * 1000 * 1024 * 4     # 16 tiles: 4 slices
+    assert _lib.workspace_bytes(600, 256, 2100, 1, 1) == 4 * 600 * 256 * 4         # 3 tiles, 17 k-blocks: 4 slices
+    for shape in ((8192, 4096, 1024), (2048, 1024, 4096), (512, 4096, 1024), (125, 4096, 1024), (1, 1024, 4096),
+                  (512, 1024, 1024)):
+        assert _lib.workspace_bytes(*shape, 1, 1) == 0, shape
