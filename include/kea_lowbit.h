@@ -38,7 +38,8 @@ enum {
     KEA_ERR_CUDA = 5,            /* a CUDA runtime / driver call failed (launch, attribute, tensor map) */
     KEA_ERR_NO_DEVICE = 6,       /* the current device is not an sm_100 (B200-class) GPU */
     KEA_ERR_DEVICE_TIMEOUT = 7,  /* a kernel's bounded wait expired and the kernel returned early */
-    KEA_ERR_CAPTURE = 8          /* first use of a device inside a CUDA-graph capture (one-time set-up needed) */
+    KEA_ERR_CAPTURE = 8,         /* first use of a device inside a CUDA-graph capture (one-time set-up needed) */
+    KEA_ERR_SCRATCH_LIMIT = 9    /* kea_lowbit_gemm_noalloc: the shape's split-K scratch exceeds its static buffer */
 };
 
 /* Output element type of y. FP32 is the reference's output (src/kea_kernels/binary/kernels.py:315-325);
@@ -130,6 +131,22 @@ typedef struct KeaGemmConfig {
 } KeaGemmConfig;
 
 int kea_lowbit_gemm(const KeaGemmDesc *desc, void *stream);
+
+/* kea_lowbit_gemm for callers that cannot allocate device memory. No counterpart in the reference (whose launcher
+ * allocates a workspace with every call). A speech service answering requests in real time may not call cudaMalloc
+ * on its request path: cudaMalloc can wait for the whole device and its latency has no bound; and a host that runs
+ * this library inside its own memory budget must not have device memory grow behind its back. This entry point
+ * allocates nothing: where the dispatch table splits K (few pair tiles, long K), the INT32 partial sums go to a
+ * scratch buffer of KEA_NOALLOC_SCRATCH_BYTES (16 MiB) that the library holds in a static device array, present on
+ * every GPU that loads the library until the process exits; desc->workspace / workspace_bytes are ignored.
+ * The caller still passes every input and output. A shape whose split would need more scratch is refused with
+ * KEA_ERR_SCRATCH_LIMIT (kea_lowbit_workspace_bytes says how much a shape needs); shapes that do not split need none.
+ * The first call on a device looks up the buffer's device address (once per device): make that call before any
+ * stream capture. All calls on a device share its one buffer, which keeps the last call's contents (nothing in it needs
+ * to start at zero: each call writes every partial sum it later reads), so calls on that device that overlap on the
+ * GPU (for example on two streams) race: keep them on one stream or order them with events. */
+#define KEA_NOALLOC_SCRATCH_BYTES (16u << 20)
+int kea_lowbit_gemm_noalloc(const KeaGemmDesc *desc, void *stream);
 
 /* The configuration kea_lowbit_gemm uses when tile_m / tile_n / splits / stages are 0.
  * Replaces configs.choose (src/kea_kernels/binary/configs.py:53-58). */

@@ -580,6 +580,25 @@ cudaError_t launch_glu_dw(cudaLaunchConfig_t *cfg, const kea::ConvArgs &a) {
     return cudaLaunchKernelEx(cfg, kea::glu_depthwise_kernel<KW>, a);
 }
 
+// ---- scratch of the no-allocation entry point ----------------------------------------------------------------
+// Split-K partial sums for kea_lowbit_gemm_noalloc, in a static device array so that its callers allocate nothing.
+// Host code must not use the array's name as a device address (on the host it names a stand-in); the address comes
+// from cudaGetSymbolAddress, looked up once per device with that device current.
+static __device__ __align__(256) int g_noalloc_scratch[KEA_NOALLOC_SCRATCH_BYTES / sizeof(int)];
+void *g_noalloc_addr[kMaxDevices] = {};
+
+// The split-K scratch kea_lowbit_gemm would use for this descriptor (the dispatch decisions it makes), 0 for none.
+size_t noalloc_scratch_need(const KeaGemmDesc *d, int sms) {
+    if (d->m < 1 || d->n < 1 || d->k < 1 || d->parts < 1 || d->parts > 3 || (d->wbits != 1 && d->wbits != 2))
+        return 0;   // kea_lowbit_gemm rejects or skips it
+    const bool forced = d->tile_m || d->tile_n || d->splits || d->stages;
+    if (forced || (d->flags & KEA_FLAG_NO_PAIR)) return 0;
+    const KeaGemmConfig c = choose(d->m, d->n, d->k, d->wbits, d->parts, sms);
+    if (c.kernel == 2) return 0;
+    const bool pair = c.kernel == 1 || ((d->flags & KEA_FLAG_FORCE_PAIR) && pair_fits(d->m, d->n, d->k, d->parts));
+    return pair ? pair_workspace_bytes(d->m, d->n, d->k, d->parts, sms) : 0;
+}
+
 extern "C" {
 
 int kea_lowbit_version(void) { return KEA_LOWBIT_VERSION; }
@@ -595,6 +614,8 @@ const char *kea_lowbit_status_string(int status) {
         case KEA_ERR_NO_DEVICE: return "current device is not an sm_100 GPU";
         case KEA_ERR_DEVICE_TIMEOUT: return "a kernel wait timed out";
         case KEA_ERR_CAPTURE: return "first use of a device during stream capture";
+        case KEA_ERR_SCRATCH_LIMIT:
+            return "the shape's split-K partial sums need more scratch than the no-allocation entry point's 16 MiB";
         default: return "unknown status";
     }
 }
@@ -615,6 +636,29 @@ size_t kea_lowbit_workspace_bytes(int32_t m, int32_t n, int32_t k, int32_t wbits
     cudaGetLastError();   // no device here (a CPU host): size for a B200
     const KeaGemmConfig c = choose(m, n, k, wbits, parts, sms);
     return c.kernel == 1 ? pair_workspace_bytes(m, n, k, parts, sms) : 0u;
+}
+
+int kea_lowbit_gemm_noalloc(const KeaGemmDesc *d, void *stream) {
+    if (!d) return KEA_ERR_INVALID_VALUE;
+    int dev = 0;
+    const int st = device_setup(&dev);
+    if (st != KEA_OK) return st;
+    {   // once per device, with it current: the scratch array's device address
+        std::lock_guard<std::mutex> lock(g_mutex);
+        if (!g_noalloc_addr[dev]) {
+            void *addr = nullptr;
+            if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess || !addr) {
+                cudaGetLastError();
+                return KEA_ERR_CUDA;
+            }
+            g_noalloc_addr[dev] = addr;
+        }
+    }
+    if (noalloc_scratch_need(d, g_devices[dev].sms) > (size_t)KEA_NOALLOC_SCRATCH_BYTES) return KEA_ERR_SCRATCH_LIMIT;
+    KeaGemmDesc g = *d;
+    g.workspace = g_noalloc_addr[dev];
+    g.workspace_bytes = (int64_t)KEA_NOALLOC_SCRATCH_BYTES;
+    return kea_lowbit_gemm(&g, stream);
 }
 
 int kea_lowbit_choose_config(int32_t m, int32_t n, int32_t k, int32_t wbits, int32_t parts, KeaGemmConfig *out) {

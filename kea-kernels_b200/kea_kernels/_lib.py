@@ -15,14 +15,14 @@ import torch
 
 LIB_PATH = Path(os.environ.get("KEA_LOWBIT_LIB", Path(__file__).resolve().parent / "libkea_lowbit.so"))
 
-OK, INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES, CUDA, NO_DEVICE, DEVICE_TIMEOUT, CAPTURE = range(9)
+OK, INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES, CUDA, NO_DEVICE, DEVICE_TIMEOUT, CAPTURE, SCRATCH_LIMIT = range(10)
 OUT_F32, OUT_F16 = 0, 1
 FLAG_SILU, FLAG_ORDER1, FLAG_PDL, FLAG_NO_PAIR, FLAG_FORCE_PAIR = 1, 2, 4, 8, 16
 QUANT_INPUT_SILU, QUANT_PDL = 1, 2
 DEVERR_TIMEOUT, DEVERR_TAIL_BITS, DEVERR_TERNARY_11 = 1, 2, 4
 
 # Every symbol include/kea_lowbit.h declares.
-EXPORTS = ("kea_lowbit_gemm", "kea_lowbit_choose_config", "kea_lowbit_panel_bytes", "kea_lowbit_workspace_bytes",
+EXPORTS = ("kea_lowbit_gemm", "kea_lowbit_gemm_noalloc", "kea_lowbit_choose_config", "kea_lowbit_panel_bytes", "kea_lowbit_workspace_bytes",
            "kea_lowbit_prepare",
            "kea_lowbit_quantize", "kea_lowbit_glu_depthwise", "kea_lowbit_rel_attention", "kea_lowbit_read_error",
            "kea_lowbit_status_string", "kea_lowbit_version")
@@ -87,6 +87,8 @@ def lib() -> ctypes.CDLL:
         handle = ctypes.CDLL(str(LIB_PATH))
         handle.kea_lowbit_gemm.argtypes = [ctypes.POINTER(GemmDesc), ctypes.c_void_p]
         handle.kea_lowbit_gemm.restype = ctypes.c_int
+        handle.kea_lowbit_gemm_noalloc.argtypes = [ctypes.POINTER(GemmDesc), ctypes.c_void_p]
+        handle.kea_lowbit_gemm_noalloc.restype = ctypes.c_int
         handle.kea_lowbit_choose_config.argtypes = [ctypes.c_int32] * 5 + [ctypes.POINTER(GemmConfig)]
         handle.kea_lowbit_choose_config.restype = ctypes.c_int
         handle.kea_lowbit_panel_bytes.argtypes = [ctypes.c_int32] * 3
@@ -116,7 +118,7 @@ def check(status: int, what: str) -> None:
     if status == OK:
         return
     text = lib().kea_lowbit_status_string(status).decode()
-    if status in (INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES):
+    if status in (INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES, SCRATCH_LIMIT):
         raise ValueError(f"{what}: {text}")
     raise RuntimeError(f"{what}: {text} (status {status})")
 
