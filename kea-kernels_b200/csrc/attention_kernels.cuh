@@ -18,6 +18,10 @@
 // DK / 8 output columns (16-byte chunks c, c + 8, ...). The 8 lanes of a shared-memory phase read K and band rows
 // four apart, so those tiles store 16-byte chunk c of row r at c ^ ((r / 4) % 8): conflict-free. FP32 FMAs
 // throughout; the softmax uses expf and the final division is IEEE.
+//
+// KG = 2 (small grids: one clip gives only 32 CTAs) doubles the CTA to two 128-thread groups that take alternate key
+// blocks, each with its own K / V / band / probability tiles and online-softmax state; the two states are merged at
+// the end (max, rescaled sums), halving the chain of key blocks each CTA walks.
 #pragma once
 
 #include "ptx.cuh"
@@ -38,24 +42,29 @@ struct RelAttnArgs {
     float scale;
 };
 
-// Shared memory floats for head width DK: Qu, Qv, V tiles (rows padded by 4), K and the position band (swizzled),
-// the probability tile.
+// Shared memory floats for head width DK: Qu, Qv (rows padded by 4), then per key group a V tile (padded), K and the
+// position band (swizzled) and the probability tile.
 template <int DK>
-constexpr int attn_smem_floats() {
-    return (2 * kAttnQ + kAttnK) * (DK + 4) + (kAttnK + kAttnBand) * DK + kAttnQ * (kAttnK + 1);
+__host__ __device__ constexpr int attn_group_floats() {
+    return kAttnK * (DK + 4) + (kAttnK + kAttnBand) * DK + kAttnQ * (kAttnK + 1);
+}
+template <int DK, int KG>
+__host__ __device__ constexpr int attn_smem_floats() {
+    return 2 * kAttnQ * (DK + 4) + KG * attn_group_floats<DK>();
 }
 // float offset of 16-byte chunk c4 of row r in a swizzled tile of DK-float rows
 template <int DK>
 KEA_DEVI int swz(int r, int c4) { return r * DK + 4 * (c4 ^ ((r >> 2) & 7)); }
 
-template <int DK>
-__global__ void __launch_bounds__(kAttnThreads) rel_attention_kernel(const RelAttnArgs a) {
+template <int DK, int KG>
+__global__ void __launch_bounds__(kAttnThreads * KG) rel_attention_kernel(const RelAttnArgs a) {
     extern __shared__ __align__(16) float asmem[];
     static_assert(DK % 32 == 0, "head width: a multiple of 32 (eight 16-byte chunks for the swizzle)");
     constexpr int LD = DK + 4;   // padded row: 16-byte aligned, rows start on different banks
-    float *Qu = asmem, *Qv = Qu + kAttnQ * LD, *Vs = Qv + kAttnQ * LD;
+    const int g = threadIdx.x / kAttnThreads, tid = threadIdx.x % kAttnThreads;   // key group, thread within it
+    float *Qu = asmem, *Qv = Qu + kAttnQ * LD;
+    float *Vs = Qv + kAttnQ * LD + g * attn_group_floats<DK>();
     float *Ks = Vs + kAttnK * LD, *Ps = Ks + kAttnK * DK, *Pr = Ps + kAttnBand * DK;   // Pr: [kAttnQ][kAttnK + 1]
-    const int tid = threadIdx.x;
     const int i0 = blockIdx.x * kAttnQ, h = blockIdx.y, b = blockIdx.z;
     const int T = a.T, H = a.H;
     const long long row3 = 3LL * H * DK;   // floats per token row of qkv
@@ -65,7 +74,7 @@ __global__ void __launch_bounds__(kAttnThreads) rel_attention_kernel(const RelAt
 
     constexpr int V4 = DK / 4;   // float4 per head row
     // queries (+ both position biases)
-    for (int e = tid; e < kAttnQ * V4; e += kAttnThreads) {
+    for (int e = threadIdx.x; e < kAttnQ * V4; e += kAttnThreads * KG) {
         const int r = e / V4, c4 = e - r * V4, i = i0 + r;
         float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
         if (i < T) q = __ldg(reinterpret_cast<const float4 *>(qkv_b + (long long)i * row3 + (long long)h * DK) + c4);
@@ -89,8 +98,13 @@ __global__ void __launch_bounds__(kAttnThreads) rel_attention_kernel(const RelAt
 #pragma unroll
         for (int c = 0; c < OC; ++c) o[r][c] = 0.f;
 
-    for (int j0 = 0; j0 < live; j0 += kAttnK) {
+    // group g takes key blocks g, g + KG, ...; every thread passes every barrier (a group without a block idles)
+    const int trips = ((live + kAttnK - 1) / kAttnK + KG - 1) / KG;
+    for (int trip = 0; trip < trips; ++trip) {
+        const int j0 = (trip * KG + g) * kAttnK;
+        const bool act = j0 < live;
         __syncthreads();   // the previous block's K / V / band / probabilities are consumed
+        if (act)
         for (int e = tid; e < kAttnK * V4; e += kAttnThreads) {
             const int r = e / V4, c4 = e - r * V4, j = j0 + r;
             float4 kk = make_float4(0.f, 0.f, 0.f, 0.f), vv = kk;
@@ -104,6 +118,7 @@ __global__ void __launch_bounds__(kAttnThreads) rel_attention_kernel(const RelAt
         }
         // band row s <-> relative offset (j - i) = j0 - i0 - (kAttnQ - 1) + s <-> pos row offset + T - 1
         const int rel0 = j0 - i0 - (kAttnQ - 1);
+        if (act)
         for (int e = tid; e < kAttnBand * V4; e += kAttnThreads) {
             const int s = e / V4, c4 = e - s * V4, pr = rel0 + s + T - 1;
             float4 pp = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -112,6 +127,10 @@ __global__ void __launch_bounds__(kAttnThreads) rel_attention_kernel(const RelAt
             *reinterpret_cast<float4 *>(Ps + swz<DK>(s, c4)) = pp;
         }
         __syncthreads();
+        if (!act) {   // this group has no block in this trip: only the barriers
+            __syncthreads();
+            continue;
+        }
 
         // scores: ac = Qu_i . K_j, bd = Qv_i . P_(j - i), for 2 x 4 (i, j)
         float ac[2][4], bd[2][4];
@@ -193,6 +212,42 @@ __global__ void __launch_bounds__(kAttnThreads) rel_attention_kernel(const RelAt
                 o[1][4 * c4 + 1] = __fmaf_rn(p1, vv.y, o[1][4 * c4 + 1]);
                 o[1][4 * c4 + 2] = __fmaf_rn(p1, vv.z, o[1][4 * c4 + 2]);
                 o[1][4 * c4 + 3] = __fmaf_rn(p1, vv.w, o[1][4 * c4 + 3]);
+            }
+        }
+    }
+    if constexpr (KG > 1) {   // merge group 1's state into group 0's (group 1's tiles hold it: [kAttnQ][DK + 4])
+        __syncthreads();
+        float *cm = asmem + 2 * kAttnQ * LD + attn_group_floats<DK>();
+        if (g == 1) {
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                float *row = cm + (qi0 + r) * LD;
+#pragma unroll
+                for (int c4 = 0; c4 < OC / 4; ++c4)
+                    *reinterpret_cast<float4 *>(row + 4 * (oc4 + 8 * c4)) =
+                        make_float4(o[r][4 * c4], o[r][4 * c4 + 1], o[r][4 * c4 + 2], o[r][4 * c4 + 3]);
+                if (oc4 == 0) {
+                    row[DK] = m_run[r];
+                    row[DK + 1] = l_run[r];
+                }
+            }
+        }
+        __syncthreads();
+        if (g != 0) return;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const float *row = cm + (qi0 + r) * LD;
+            const float m1 = row[DK], l1 = row[DK + 1], m = fmaxf(m_run[r], m1);
+            const float c0 = m_run[r] == -INFINITY ? 0.f : expf(m_run[r] - m);
+            const float c1 = m1 == -INFINITY ? 0.f : expf(m1 - m);
+            l_run[r] = __fmaf_rn(l_run[r], c0, __fmul_rn(l1, c1));
+#pragma unroll
+            for (int c4 = 0; c4 < OC / 4; ++c4) {
+                const float4 p = *reinterpret_cast<const float4 *>(row + 4 * (oc4 + 8 * c4));
+                o[r][4 * c4] = __fmaf_rn(o[r][4 * c4], c0, __fmul_rn(p.x, c1));
+                o[r][4 * c4 + 1] = __fmaf_rn(o[r][4 * c4 + 1], c0, __fmul_rn(p.y, c1));
+                o[r][4 * c4 + 2] = __fmaf_rn(o[r][4 * c4 + 2], c0, __fmul_rn(p.z, c1));
+                o[r][4 * c4 + 3] = __fmaf_rn(o[r][4 * c4 + 3], c0, __fmul_rn(p.w, c1));
             }
         }
     }

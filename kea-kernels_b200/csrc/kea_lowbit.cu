@@ -90,12 +90,14 @@ int device_setup(int *device_out) {
         if (cudaFuncSetAttribute((const void *)kea::quantize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  64 * 1024) != cudaSuccess)
             status = KEA_ERR_CUDA;
-        const void *attn_kernels[3] = {(const void *)kea::rel_attention_kernel<32>,
-                                       (const void *)kea::rel_attention_kernel<64>,
-                                       (const void *)kea::rel_attention_kernel<128>};
-        const int attn_smem[3] = {kea::attn_smem_floats<32>() * 4, kea::attn_smem_floats<64>() * 4,
-                                  kea::attn_smem_floats<128>() * 4};
-        for (int i = 0; i < 3; ++i)
+        const void *attn_kernels[6] = {
+            (const void *)kea::rel_attention_kernel<32, 1>, (const void *)kea::rel_attention_kernel<64, 1>,
+            (const void *)kea::rel_attention_kernel<128, 1>, (const void *)kea::rel_attention_kernel<32, 2>,
+            (const void *)kea::rel_attention_kernel<64, 2>, (const void *)kea::rel_attention_kernel<128, 2>};
+        const int attn_smem[6] = {kea::attn_smem_floats<32, 1>() * 4, kea::attn_smem_floats<64, 1>() * 4,
+                                  kea::attn_smem_floats<128, 1>() * 4, kea::attn_smem_floats<32, 2>() * 4,
+                                  kea::attn_smem_floats<64, 2>() * 4, kea::attn_smem_floats<128, 2>() * 4};
+        for (int i = 0; i < 6; ++i)
             if (cudaFuncSetAttribute(attn_kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem[i]) !=
                 cudaSuccess)
                 status = KEA_ERR_CUDA;
@@ -569,10 +571,17 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
 
 }  // namespace
 
+// Two key groups per CTA when the grid is small (under two CTAs per SM): each CTA's chain of key blocks halves.
 template <int DK>
-cudaError_t launch_rel_attention(cudaLaunchConfig_t *cfg, const kea::RelAttnArgs &a) {
-    cfg->dynamicSmemBytes = (size_t)kea::attn_smem_floats<DK>() * sizeof(float);
-    return cudaLaunchKernelEx(cfg, kea::rel_attention_kernel<DK>, a);
+cudaError_t launch_rel_attention(cudaLaunchConfig_t *cfg, const kea::RelAttnArgs &a, int sms) {
+    const long long ctas = (long long)cfg->gridDim.x * cfg->gridDim.y * cfg->gridDim.z;
+    if (ctas < 2LL * sms) {
+        cfg->blockDim = dim3(2 * kea::kAttnThreads, 1, 1);
+        cfg->dynamicSmemBytes = (size_t)kea::attn_smem_floats<DK, 2>() * sizeof(float);
+        return cudaLaunchKernelEx(cfg, kea::rel_attention_kernel<DK, 2>, a);
+    }
+    cfg->dynamicSmemBytes = (size_t)kea::attn_smem_floats<DK, 1>() * sizeof(float);
+    return cudaLaunchKernelEx(cfg, kea::rel_attention_kernel<DK, 1>, a);
 }
 
 template <int KW>
@@ -724,8 +733,9 @@ int kea_lowbit_rel_attention(const KeaAttentionDesc *d, void *stream) {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.numAttrs = 1;
     }
-    const cudaError_t e = d->dk == 128 ? launch_rel_attention<128>(&cfg, a)
-                          : d->dk == 64 ? launch_rel_attention<64>(&cfg, a) : launch_rel_attention<32>(&cfg, a);
+    const int sms = g_devices[dev].sms;
+    const cudaError_t e = d->dk == 128 ? launch_rel_attention<128>(&cfg, a, sms)
+                          : d->dk == 64 ? launch_rel_attention<64>(&cfg, a, sms) : launch_rel_attention<32>(&cfg, a, sms);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return KEA_ERR_CUDA;

@@ -123,10 +123,10 @@ def torch_rel_attention(qkv: Tensor, pos: Tensor, bias_u: Tensor, bias_v: Tensor
     return torch.matmul(attn, v.transpose(1, 2)).transpose(1, 2).reshape(b, t, d)
 
 
-# The fused FP32 attention kernel measured faster than the PyTorch sequence from 16 (clip, head) pairs up to clips of
-# ~200 frames (B200: 1.5x at 4 clips of 125 frames, 1.2x at 256); one clip gives it too few CTAs and 375-frame clips
-# favour the library matmuls.
-FUSED_ATTENTION_MIN_ROWS, FUSED_ATTENTION_MAX_T = 16, 192
+# The fused FP32 attention kernel measured faster than the PyTorch sequence from 16 (clip, head) pairs on (B200, 125
+# frames: 1.6-2.1x at 2-4 clips, 1.4x at 256; 85 clips of 375 frames: 1.03x); one clip ties at 125 frames and loses
+# at 375 (too few CTAs), so a single clip takes the PyTorch sequence.
+FUSED_ATTENTION_MIN_ROWS, FUSED_ATTENTION_MAX_T = 16, 1 << 30
 
 
 def rel_positions(t: int, d: int, device) -> Tensor:

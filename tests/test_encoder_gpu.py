@@ -169,7 +169,7 @@ def _torch_rel_attention(qkv, pos, u, v, heads, lengths=None):
 
 
 @pytest.mark.parametrize("b,t,heads,dk", [(2, 125, 8, 128), (1, 7, 2, 32), (3, 33, 4, 64), (1, 375, 8, 128),
-                                          (2, 64, 1, 32)])
+                                          (2, 64, 1, 32), (16, 125, 8, 128), (40, 70, 4, 64)])
 @pytest.mark.parametrize("masked", [False, True])
 @torch.inference_mode()
 def test_rel_attention_matches_torch(b, t, heads, dk, masked):
