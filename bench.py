@@ -519,16 +519,19 @@ def clip_workloads(torch, dev, stream, rank, world, dist, local, pdl, hbm_peak, 
 
 
 KEA_T_FRAMES_CAP = 32000   # padded encoder frames per forward (bounds the subsampling activations to ~10 GB)
-KEA_T_BUCKET = 32          # length-bucket width in encoder frames
+# Forward planning (kea_kernels.batch.plan): a forward's cost modelled as a fixed floor plus a cost per padded encoder
+# frame, both fitted on B200 to this workload's length-bucket runs (13 forwards / 218k padded frames in 1156 ms on one
+# GPU, 12 / 27k in 205 ms per rank on eight); a rank's clips are grouped into padded forwards at the least modelled cost.
+KEA_T_FORWARD_US = 6000.0
+KEA_T_FRAME_US = 5.0
 
 
 def kea_t_batch(torch, dev, stream, world, dist, local, pdl, n_clips):
     """a Kea-T-shaped encoder (the same 24-layer FastConformer, 2-bit ternary weights, two
     residual INT8 parts: Kea-T's default x2 mode) over `n_clips` synthetic clips whose lengths are uniform in
-    2-30 s (log-mel at 100 frames/s, N(0, 1)). Whole clips are sharded over the ranks by frame count; each rank sorts
-    its clips into length buckets KEA_T_BUCKET encoder frames wide, pads each bucket to its longest clip (masked as
-    attention keys and before the depthwise convolution) and runs it in forwards of at most KEA_T_FRAMES_CAP padded
-    frames. One untimed pass fills the per-length position-projection cache; the timed pass is bracketed by CUDA
+    2-30 s (log-mel at 100 frames/s, N(0, 1)). Whole clips are sharded over the ranks by frame count; each rank groups
+    its clips into forwards by `batch.plan` (least modelled cost, at most KEA_T_FRAMES_CAP padded frames each) and
+    pads each forward to its longest clip (masked as attention keys and before the depthwise convolution). One untimed pass fills the per-length position-projection cache; the timed pass is bracketed by CUDA
     events on the rank's stream, labels and timings gathered with NCCL, max over ranks."""
     from kea_kernels import batch as B
     from kea_kernels import encoder as E
@@ -540,24 +543,22 @@ def kea_t_batch(torch, dev, stream, world, dist, local, pdl, n_clips):
     enc_frames = [enc.frames(t) for t in mel_frames]
     dgen = torch.Generator(device=dev).manual_seed(4242)
 
+    n_forwards = [0]
+
     def process(indices):
         if not indices:
             return [], 0.0
         fr = [enc_frames[i] for i in indices]
         work = []
-        for bucket in B.buckets(fr, range(KEA_T_BUCKET, max(fr) + KEA_T_BUCKET, KEA_T_BUCKET)):
-            if not bucket:
-                continue
-            ids = [indices[j] for j in bucket]                      # longest first
-            t_mel = mel_frames[ids[0]]
-            per = max(1, KEA_T_FRAMES_CAP // enc.frames(t_mel))
-            for s0 in range(0, len(ids), per):
-                sub = ids[s0:s0 + per]
-                mel = torch.zeros(len(sub), 128, t_mel, device=dev)
-                for j, i in enumerate(sub):
-                    mel[j, :, :mel_frames[i]].normal_(generator=dgen)
-                lengths = torch.tensor([enc_frames[i] for i in sub], device=dev)
-                work.append((sub, mel, lengths))
+        for group in B.plan(fr, KEA_T_FRAMES_CAP, KEA_T_FORWARD_US, KEA_T_FRAME_US):
+            sub = [indices[j] for j in group]                       # longest first
+            t_mel = max(mel_frames[i] for i in sub)
+            mel = torch.zeros(len(sub), 128, t_mel, device=dev)
+            for j, i in enumerate(sub):
+                mel[j, :, :mel_frames[i]].normal_(generator=dgen)
+            lengths = torch.tensor([enc_frames[i] for i in sub], device=dev)
+            work.append((sub, mel, lengths))
+        n_forwards[0] = len(work)
         labels = {}
         with torch.cuda.stream(stream):
             for sub, mel, lengths in work:                          # untimed: position cache, allocator
@@ -582,9 +583,10 @@ def kea_t_batch(torch, dev, stream, world, dist, local, pdl, n_clips):
               for layer in enc.layers for n in E.LAYER_LINEARS) * total / 1e9
     return {"workload": f"BASELINE config 4: {n_clips} synthetic clips, lengths U[2, 30] s ({total} encoder frames, "
                         f"{min(enc_frames)}-{max(enc_frames)} per clip), Kea-T-shaped random-init encoder (2-bit "
-                        f"ternary, x2 residual parts), sharded over {world} GPU(s) by frames, length buckets "
-                        f"{KEA_T_BUCKET} frames wide padded per bucket, <= {KEA_T_FRAMES_CAP} padded frames per "
-                        "forward; labels and timings gathered with NCCL",
+                        f"ternary, x2 residual parts), sharded over {world} GPU(s) by frames, grouped into padded "
+                        f"forwards of <= {KEA_T_FRAMES_CAP} frames at least modelled cost ({KEA_T_FORWARD_US:.0f} us "
+                        f"per forward + {KEA_T_FRAME_US} us per padded frame); labels and timings gathered with NCCL",
+            "forwards_rank0": n_forwards[0],
             "clips_per_s": n_clips / t, "frames_per_s": total / t, "ms_per_batch": t * 1e3,
             "per_rank_ms": [v * 1e3 for v in res.seconds], "per_rank_frames": res.frames,
             "lowbit_gop_unpadded": ops, "encoder_lowbit_tops_unpadded": ops / t / 1e3,

@@ -5,6 +5,8 @@ process per GPU): every rank runs the whole encoder on its clips, and the only c
 after the batch (NCCL on GPUs, gloo in the CPU tests). Nothing here touches the GEMM.
 
   * `buckets(frames, edges)`   - clip indices grouped by length bucket, longest first inside a bucket;
+  * `plan(frames, cap, ...)`   - clips grouped into padded forwards at the least modelled cost (a fixed cost per
+                                 forward + a cost per padded frame), at most `cap` padded frames per forward;
   * `shard(frames, world)`     - whole clips dealt to ranks, balanced by frame count (longest-processing-time
                                  greedy; deterministic);
   * `pack(rows)`               - varlen packing: per-clip [T_i, D] feature rows -> one [sum T_i, D] matrix + offsets,
@@ -41,6 +43,41 @@ def buckets(frames: Sequence[int], edges: Sequence[int]) -> list[list[int]]:
     for lst in out:
         lst.sort(key=lambda i: (-frames[i], i))
     return out
+
+
+def plan(frames: Sequence[int], cap: int, forward_cost: float, frame_cost: float) -> list[list[int]]:
+    """Groups clips into padded forwards: each group is padded to its longest clip, so it costs
+    `forward_cost + frame_cost * len(group) * longest` and holds at most `cap` padded frames (a single clip longer
+    than `cap` goes alone). Exact minimum of the summed cost over all groupings: an optimal grouping takes clips
+    contiguous in length order, so a dynamic programme over the clips sorted longest first (ties by index) finds it.
+    A large `forward_cost` against `frame_cost` merges few-clip length ranges into one forward; a small one keeps
+    lengths apart. Returns the groups longest first, each longest first."""
+    if cap < 1:
+        raise ValueError("cap must be >= 1")
+    if forward_cost < 0 or frame_cost < 0:
+        raise ValueError("costs must be >= 0")
+    for i, f in enumerate(frames):
+        if f < 0:
+            raise ValueError(f"clip {i}: negative frame count {f}")
+    order = sorted(range(len(frames)), key=lambda i: (-frames[i], i))
+    lens = [int(frames[i]) for i in order]
+    n = len(order)
+    best = [0.0] + [float("inf")] * n       # best[j]: least cost of the first j clips in `order`
+    start = [0] * (n + 1)
+    for j in range(1, n + 1):
+        for i in range(j - 1, -1, -1):      # group order[i:j], padded to lens[i]; grows as i falls
+            padded = (j - i) * lens[i]
+            if padded > cap and i < j - 1:
+                break
+            c = best[i] + forward_cost + frame_cost * padded
+            if c < best[j]:
+                best[j], start[j] = c, i
+    groups = []
+    j = n
+    while j > 0:
+        groups.append(order[start[j]:j])
+        j = start[j]
+    return groups[::-1]
 
 
 def shard(frames: Sequence[int], world: int) -> list[list[int]]:

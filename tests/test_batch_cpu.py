@@ -41,6 +41,53 @@ def test_buckets_group_by_length():
         batch.buckets([-1], [10])
 
 
+def _set_partitions(items):
+    if not items:
+        yield []
+        return
+    for p in _set_partitions(items[1:]):
+        for k in range(len(p)):
+            yield p[:k] + [[items[0]] + p[k]] + p[k + 1:]
+        yield [[items[0]]] + p
+
+
+def _plan_cost(groups, frames, cap, forward_cost, frame_cost):
+    total = 0.0
+    for g in groups:
+        padded = len(g) * max(frames[i] for i in g)
+        if padded > cap and len(g) > 1:
+            return float("inf")
+        total += forward_cost + frame_cost * padded
+    return total
+
+
+def test_plan_is_the_least_cost_grouping():
+    """The planner's grouping costs no more than the best of all set partitions (brute force, up to 6 clips)."""
+    rng = random.Random(7)
+    for _ in range(150):
+        frames = [rng.randint(0, 60) for _ in range(rng.randint(0, 6))]
+        cap, fc, pc = rng.randint(1, 200), rng.choice([0, 1, 5, 30, 100]), rng.choice([0, 0.1, 1, 3])
+        groups = batch.plan(frames, cap, fc, pc)
+        assert sorted(i for g in groups for i in g) == list(range(len(frames)))
+        for g in groups:
+            assert [frames[i] for i in g] == sorted((frames[i] for i in g), reverse=True)
+        best = min(_plan_cost(p, frames, cap, fc, pc) for p in _set_partitions(list(range(len(frames)))))
+        assert _plan_cost(groups, frames, cap, fc, pc) == pytest.approx(best)
+
+
+def test_plan_merges_or_splits_by_cost():
+    frames = [100] * 4 + [60] * 4
+    assert batch.plan(frames, 10_000, 1.0, 1.0) == [[0, 1, 2, 3], [4, 5, 6, 7]]      # no padding when forwards are cheap
+    assert batch.plan(frames, 10_000, 1e6, 1.0) == [list(range(8))]                   # one forward when they are dear
+    assert batch.plan(frames, 250, 1e6, 1.0) == [[0, 1], [2, 3], [4, 5, 6, 7]]        # at most 250 padded frames
+    assert batch.plan([500, 10], 100, 1.0, 1.0) == [[0], [1]]                         # a clip over the cap goes alone
+    assert batch.plan([], 100, 1.0, 1.0) == []
+    for bad in ((lambda: batch.plan([1], 0, 1, 1)), (lambda: batch.plan([-1], 9, 1, 1)),
+                (lambda: batch.plan([1], 9, -1, 1))):
+        with pytest.raises(ValueError):
+            bad()
+
+
 def test_pack_round_trip():
     rows = [torch.randn(t, 8) for t in (3, 0, 5, 1)]
     packed, off = batch.pack(rows)
