@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define KEA_LOWBIT_VERSION 1
+#define KEA_LOWBIT_VERSION 2
 
 /* Status codes. The Python layer maps 1-4 to ValueError and 5-8 to RuntimeError, as the reference raises
  * ValueError for argument errors (src/kea_kernels/binary/layer.py:66-78,188-189) and RuntimeError for a failed
@@ -53,8 +53,14 @@ enum {
     KEA_FLAG_ORDER1 = 2,
     KEA_FLAG_PDL = 4,           /* launch with programmatic dependent launch (overlap with the previous kernel) */
     KEA_FLAG_NO_PAIR = 8,       /* never use the persistent CTA-pair kernel (the per-tile kernel runs instead) */
-    KEA_FLAG_FORCE_PAIR = 16    /* the pair kernel wherever its shape allows (1-2 parts, N % 256 == 0, m > 256,
+    KEA_FLAG_FORCE_PAIR = 16,   /* the pair kernel wherever its shape allows (1-2 parts, N % 256 == 0, m > 256,
                                    k <= 32768), also where the table would take the per-tile kernel */
+    KEA_FLAG_FORCE_SWAP = 32,   /* the small-M swapped-operand kernel (weights on the MMA's M axis, tokens on N) at any
+                                   shape; `splits` / `stages` (0: the table's) then apply to it, tile_m / tile_n must be 0 */
+    KEA_FLAG_NO_SWAP = 64,      /* keep the table off the swapped-operand kernel (128-token tiles run instead) */
+    KEA_FLAG_TEST_STALL = 128   /* tests only, with KEA_FLAG_FORCE_SWAP: the kernel's producer issues no activation
+                                   copy, so its MMA warp's bounded wait runs out (see wait_clocks), the kernel reports
+                                   KEA_DEVERR_TIMEOUT and returns; the output is left undefined */
 };
 
 /* Device error word bits (written by kernels into `error_word`, or into the library's own device word). */
@@ -116,6 +122,9 @@ typedef struct KeaGemmDesc {
                                  (same bits). kea_lowbit_workspace_bytes says how much a shape uses; with less (or
                                  NULL) the GEMM runs unsplit. Calls sharing a workspace must not overlap on the GPU. */
     int64_t workspace_bytes;
+    int64_t wait_clocks;      /* 0: the library's bound on a kernel's wait (4e9 SM clocks, about 2 s); else the SM clocks
+                                 one wait of the small-M kernel may last before it gives up, reports KEA_DEVERR_TIMEOUT
+                                 in the error word and returns (the context stays usable) */
 } KeaGemmDesc;
 
 /* Tile configuration picked for a shape (the M-bucketed split-K dispatch table). */
@@ -127,7 +136,8 @@ typedef struct KeaGemmConfig {
     int32_t smem_bytes;       /* dynamic shared memory per CTA */
     int32_t kernel;           /* 0: the per-tile tcgen05 kernel; 1: the persistent CTA-pair kernel (tcgen05
                                  cta_group::2, 256 x 256 tiles per pair of SMs, double-buffered accumulators); 2: the
-                                 CUDA-core kernel for M <= 16 (tile_n = channels per CTA) */
+                                 CUDA-core kernel for M <= 16 (tile_n = channels per CTA); 3: the small-M swapped-operand
+                                 kernel (tile_m = tokens per token tile, tile_n = 128 channels, splits = cluster along K) */
 } KeaGemmConfig;
 
 int kea_lowbit_gemm(const KeaGemmDesc *desc, void *stream);

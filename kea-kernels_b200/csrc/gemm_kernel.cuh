@@ -174,16 +174,23 @@ KEA_DEVI void expand_unit(uint32_t pk, uint32_t dst, int tn_log2, int u) {
 // ex2 / divide sequences that issue for every output even when the flag is off.
 __device__ __noinline__ float silu_call(float y) { return silu_approx(y); }
 
-// comb_P then alpha / bias then optional SiLU, one IEEE FP32 rounding per operation.
+// INT32 -> FP32 without the conversion unit (which is not full-rate on sm_100): exact for |a| < 2^22, where
+// 1.5 * 2^23 + a is a float whose bit pattern is the integer sum, and subtracting 1.5 * 2^23 is exact; so it equals
+// cvt.rn.f32.s32. Accumulators stay below 2^22 whenever K <= 32768 (|acc| <= 128 K).
+KEA_DEVI float i2f_exact(int a) { return __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f); }
+KEA_DEVI float acc_to_float(int a, bool small) { return small ? i2f_exact(a) : __int2float_rn(a); }
+
+// comb_P then alpha / bias then optional SiLU, one IEEE FP32 rounding per operation. `small`: every accumulator is
+// below 2^22 in magnitude (K <= 32768), so the exact fast conversion applies.
 KEA_DEVI float finish_value(int a0, int a1, int a2, float s0, float s1, float s2, int parts, int flags,
-                            float alpha, bool has_bias, float bias) {
+                            float alpha, bool has_bias, float bias, bool small) {
     float r;
     if (parts == 1) {
-        r = __fmul_rn(__int2float_rn(a0), s0);
+        r = __fmul_rn(acc_to_float(a0, small), s0);
     } else {
-        r = (flags & 2) ? __fmaf_rn(__int2float_rn(a1), s1, __fmul_rn(__int2float_rn(a0), s0))
-                        : __fmaf_rn(__int2float_rn(a0), s0, __fmul_rn(__int2float_rn(a1), s1));
-        if (parts == 3) r = __fmaf_rn(__int2float_rn(a2), s2, r);
+        r = (flags & 2) ? __fmaf_rn(acc_to_float(a1, small), s1, __fmul_rn(acc_to_float(a0, small), s0))
+                        : __fmaf_rn(acc_to_float(a0, small), s0, __fmul_rn(acc_to_float(a1, small), s1));
+        if (parts == 3) r = __fmaf_rn(acc_to_float(a2, small), s2, r);
     }
     r = has_bias ? __fmaf_rn(r, alpha, bias) : __fmul_rn(r, alpha);
     if (flags & 1) r = silu_call(r);
@@ -206,7 +213,7 @@ KEA_DEVI void finish_store(const GemmArgs &a, int t, int n, int c, const int (&a
     for (int j = 0; j < CNT; ++j)
         v[j] = finish_value(acc[0][j], P > 1 ? acc[P > 1 ? 1 : 0][j] : 0, P > 2 ? acc[P > 2 ? 2 : 0][j] : 0, s[0],
                             P > 1 ? s[P > 1 ? 1 : 0] : 0.f, P > 2 ? s[P > 2 ? 2 : 0] : 0.f, P, a.flags,
-                            s_alpha[c + j], has_bias, has_bias ? s_bias[c + j] : 0.f);
+                            s_alpha[c + j], has_bias, has_bias ? s_bias[c + j] : 0.f, a.K <= 32768);
     const bool full = n + CNT <= a.N;
     if (a.res) {   // residual + scale * value: the two roundings of the unfused `x + s * y`
         const float *r = a.res + (long long)t * a.ld_res + n;
@@ -720,7 +727,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                             f[j] = finish_value((int)v[0][j], P > 1 ? (int)v[P > 1 ? 1 : 0][j] : 0,
                                                 P > 2 ? (int)v[P > 2 ? 2 : 0][j] : 0, s[0], P > 1 ? s[P > 1 ? 1 : 0] : 0.f,
                                                 P > 2 ? s[P > 2 ? 2 : 0] : 0.f, P, a.flags, s_alpha[c + j], has_bias,
-                                                has_bias ? s_bias[c + j] : 0.f);
+                                                has_bias ? s_bias[c + j] : 0.f, a.K <= 32768);
                         // 16 values = 32 bytes (fp16) or 64 bytes (fp32) of this thread's staged row
                         if (a.y_f16) {
 #pragma unroll

@@ -680,7 +680,7 @@ __global__ void __launch_bounds__(256) splitk_finish_kernel(const SplitFinishArg
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         float v = finish_value(tot[0][j], tot[1][j], tot[2][j], sq[0], sq[1], sq[2], a.parts, a.flags,
-                               __ldg(a.alpha + n + j), has_bias, has_bias ? __ldg(a.bias + n + j) : 0.f);
+                               __ldg(a.alpha + n + j), has_bias, has_bias ? __ldg(a.bias + n + j) : 0.f, true);
         if (a.res) v = __fadd_rn(__ldg(a.res + (long long)t * a.ld_res + n + j), __fmul_rn(a.res_scale, v));
         if (a.y_f16)
             reinterpret_cast<__half *>(a.y)[(long long)t * a.ldy + n + j] = __float2half_rn(v);

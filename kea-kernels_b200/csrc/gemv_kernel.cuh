@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) lowbit_gemv_kern
         }
         const bool has_bias = a.bias != nullptr;
         float v = finish_value(tot[0], tot[1], tot[2], s[0], s[1], s[2], P, a.flags, __ldg(a.alpha + nn), has_bias,
-                               has_bias ? __ldg(a.bias + nn) : 0.f);
+                               has_bias ? __ldg(a.bias + nn) : 0.f, a.K <= 32768);
         if (a.res) v = __fadd_rn(__ldg(a.res + (long long)m * a.ld_res + nn), __fmul_rn(a.res_scale, v));
         if (a.y_f16)
             reinterpret_cast<__half *>(a.y)[(long long)m * a.ldy + nn] = __float2half_rn(v);

@@ -11,6 +11,7 @@
 #include "kea_lowbit.h"
 #include "gemm_kernel.cuh"
 #include "gemm_pair_kernel.cuh"
+#include "gemm_swap_kernel.cuh"
 #include "gemv_kernel.cuh"
 #include "conv_kernels.cuh"
 #include "attention_kernels.cuh"
@@ -36,18 +37,25 @@ struct DeviceState {
     bool ready = false;
     int status = KEA_OK;
     int sms = kSmsB200;
+    void *noalloc_scratch = nullptr;   // device address of g_noalloc_scratch on this device
 };
 DeviceState g_devices[kMaxDevices];
 std::mutex g_mutex;
+
+// Split-K partial sums for kea_lowbit_gemm_noalloc, in a static device array so that its callers allocate nothing.
+// Host code must not use the array's name as a device address (on the host it names a stand-in); the address comes
+// from cudaGetSymbolAddress, looked up in the one-time set-up of each device with that device current.
+static __device__ __align__(256) int g_noalloc_scratch[KEA_NOALLOC_SCRATCH_BYTES / sizeof(int)];
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
 
-// One-time per-device set-up: capability check and kernel attributes (not stream work, so it is legal
-// inside a CUDA-graph capture; nothing here allocates).
-int device_setup(int *device_out) {
+// One-time per-device set-up: capability check, kernel attributes and the no-allocation scratch address. Nothing here
+// allocates, but it loads the library's kernels onto the device, which a stream capture may not see happen: an entry
+// point called for the first time on a device while `stream` is capturing returns KEA_ERR_CAPTURE instead.
+int device_setup(int *device_out, void *stream, bool check_capture = true) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return KEA_ERR_CUDA;
     if (dev < 0 || dev >= kMaxDevices) return KEA_ERR_UNSUPPORTED;
@@ -55,6 +63,14 @@ int device_setup(int *device_out) {
     std::lock_guard<std::mutex> lock(g_mutex);
     DeviceState &st = g_devices[dev];
     if (st.ready) return st.status;
+    if (check_capture) {
+        cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing((cudaStream_t)stream, &capturing) != cudaSuccess) {
+            cudaGetLastError();
+            return KEA_ERR_CUDA;
+        }
+        if (capturing != cudaStreamCaptureStatusNone) return KEA_ERR_CAPTURE;
+    }
     int major = 0, minor = 0, sms = 0;
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
@@ -87,6 +103,15 @@ int device_setup(int *device_out) {
         for (const void *k : pair_kernels)
             if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairMaxDynSmem) != cudaSuccess)
                 status = KEA_ERR_CUDA;
+        const void *swap_kernels[6] = {
+            (const void *)kea::lowbit_gemm_swap_kernel<1, 1>, (const void *)kea::lowbit_gemm_swap_kernel<1, 2>,
+            (const void *)kea::lowbit_gemm_swap_kernel<1, 3>, (const void *)kea::lowbit_gemm_swap_kernel<2, 1>,
+            (const void *)kea::lowbit_gemm_swap_kernel<2, 2>, (const void *)kea::lowbit_gemm_swap_kernel<2, 3>};
+        for (const void *k : swap_kernels) {
+            if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem) != cudaSuccess ||
+                cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+                status = KEA_ERR_CUDA;
+        }
         if (cudaFuncSetAttribute((const void *)kea::quantize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  64 * 1024) != cudaSuccess)
             status = KEA_ERR_CUDA;
@@ -111,6 +136,12 @@ int device_setup(int *device_out) {
             if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kea::kGemvMaxSmem) != cudaSuccess)
                 status = KEA_ERR_CUDA;
     }
+    if (status == KEA_OK) {
+        void *addr = nullptr;
+        if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess || !addr) status = KEA_ERR_CUDA;
+        st.noalloc_scratch = addr;
+    }
+    if (status != KEA_OK) cudaGetLastError();
     st.status = status;
     st.sms = sms > 0 ? sms : kSmsB200;
     st.ready = true;
@@ -302,6 +333,109 @@ KeaGemmConfig choose_tile(int m, int n, int k, int wbits, int parts_in, int sms,
     return c;
 }
 
+// ---- the swapped-operand kernel for small M (gemm_swap_kernel.cuh) --------------------------------------------------
+// Tokens per token tile: at most 256 (the TMA box's rows) and P x tokens <= 512 (tensor-memory columns), in multiples
+// of 16 (the MMA's N step); a shape with more tokens is cut into equal tiles.
+int swap_max_tokens(int parts) { return std::min(kea::kSwapMaxTokens, (kea::kSwapMaxRows / parts) / 16 * 16); }
+void swap_tokens(int m, int parts, int *mt, int *tiles) {
+    *tiles = ceil_div(std::max(m, 1), swap_max_tokens(parts));
+    *mt = round_up(ceil_div(std::max(m, 1), *tiles), 16);
+}
+// Per stage: the activation box (every part's tokens x 128 k), the expanded weights (128 rows x 128 k), the codes.
+int swap_stage_bytes(int rows, int wbits) { return rows * kea::kBK + (int)kea::kSwapWTile + wbits * kea::kPanelSubBytes; }
+// Split-K receive buffer: [peer slot (splits - 1)][owned unit][part][4 token quarters][32 channels] x 16 bytes.
+int swap_units_per_owner(int mt, int splits) { return ceil_div(4 * (mt / 16), splits); }
+int swap_recv_bytes(int mt, int parts, int splits) {
+    return splits > 1 ? (splits - 1) * swap_units_per_owner(mt, splits) * parts * kea::kSwapUnitBytes : 0;
+}
+
+struct SwapPlan {
+    int mt = 0, token_tiles = 0, rows = 0, splits = 1, stages = 1, nacc = 1, smem = 0;
+    int recv = 0;                // split-K receive buffer bytes (0 unsplit)
+    uint32_t tmem_cols = 32;
+};
+// The epilogue area (receive buffer, then the epilogue warps' output tiles) starts at the stage area's offset 0: it
+// is used only once every MMA of the cluster is done.
+constexpr int kSwapStaging = kea::kSwapEpiWarps * kea::kSwapStagingBytes;
+int swap_epilogue_bytes(int recv) { return round_up(recv, 1024) + kSwapStaging; }
+
+// The swap kernel's plan for a shape. forced_splits / forced_stages 0 take the table's choice: K split over a cluster
+// (<= 8 CTAs) until the channel tiles x token tiles x splits approach the SM count; as many stages as the CTA's
+// k-blocks, while two CTAs still fit on an SM. False when a forced plan does not fit.
+bool swap_plan(int m, int n, int k, int wbits, int parts, int sms, int forced_splits, int forced_stages, SwapPlan *out) {
+    if (k > 32768) return false;   // |acc| <= 127 K < 2^22: the epilogue's exact two-operation INT32 -> FP32 conversion
+    SwapPlan p;
+    swap_tokens(m, parts, &p.mt, &p.token_tiles);
+    p.rows = parts * p.mt;
+    const int kb = ceil_div(k, kea::kBK);
+    const int tiles = ceil_div(n, kea::kPanelN) * p.token_tiles;
+    const int stage = swap_stage_bytes(p.rows, wbits);
+    int splits = forced_splits ? forced_splits : std::min({kb, kMaxPortableCluster, std::max(1, sms / tiles)});
+    // two MMAs per K step (more than 256 stacked rows): the exchange grows with the rows, so split only long K (<= 4)
+    if (!forced_splits && p.rows > 256) splits = kb <= 8 ? 1 : std::min(splits, 4);
+    if (splits < 1 || splits > kMaxCluster || splits > kb) return false;
+    for (;; --splits) {
+        if (splits < 1) return false;
+        const int recv = swap_recv_bytes(p.mt, parts, splits);
+        const int epi = swap_epilogue_bytes(recv);
+        if (1024 + epi > kMaxDynSmem) {
+            if (forced_splits) return false;
+            continue;
+        }
+        const int nkb = ceil_div(kb, splits);
+        int stages = forced_stages;
+        if (!stages) {
+            stages = std::min(nkb, kea::kSwapStagesMax);
+            // two CTAs per SM (programmatic dependent launch overlaps consecutive launches) when that keeps >= 2
+            // stages; otherwise as many as fit
+            const int two_per_sm = (kSmemPerSm / 2 - 2048 - 1024) / stage;
+            if (stages > two_per_sm && two_per_sm >= 2 && std::max(two_per_sm * stage, epi) <= kSmemPerSm / 2 - 3072)
+                stages = two_per_sm;
+            while (stages > 1 && 1024 + stages * stage > kMaxDynSmem) --stages;
+        }
+        if (stages < 1 || stages > kea::kSwapStagesMax || 1024 + stages * stage > kMaxDynSmem) return false;
+        p.splits = splits;
+        p.stages = stages;
+        p.recv = recv;
+        p.smem = 1024 + std::max(stages * stage, epi);
+        break;
+    }
+    // narrow N (<= 32 stacked rows) is issue-bound: one accumulator per K = 32 step keeps consecutive MMAs independent
+    p.nacc = p.rows <= 32 ? 4 : 1;
+    const uint32_t need = (uint32_t)(p.nacc * p.rows);
+    while (p.tmem_cols < need) p.tmem_cols <<= 1;
+    // never more CTAs on an SM than its 512 tensor-memory columns serve (a cluster peer waiting in tcgen05.alloc)
+    const int max_ctas = std::max(1, (int)(512 / p.tmem_cols));
+    p.smem = std::max(p.smem, kSmemPerSm / (max_ctas + 1) + 1);
+    *out = p;
+    return true;
+}
+
+// Where the table takes the swap kernel (B200, graph-timed cold over the Parakeet shapes against the 128-token-tile
+// kernel): one part at M <= 32 (4.7 vs 5.4 us at N 4096, K 1024) and 128 < M <= 256 (its 128-channel tiles serve
+// every token at once; 11.4 vs 11.8 us at M 256); several parts once their stacked tokens fill two MMAs (P x M >= 512:
+// 10.7 vs 16.6 us at 3 x 256 tokens, N 4096) on wide or deep layers. In between, the tile kernel's 32-channel tiles
+// without a partial exchange are faster: at this M the swap kernel's split-K exchange through distributed shared
+// memory (~16 B per clock per SM) costs more than the tcgen05 issue slots it saves.
+bool swap_shape(int m, int n, int k, int parts) {
+    if (m < 1 || k > 32768) return false;
+    if (parts == 1) return m <= 32 || (m > 128 && m <= 256);
+    return parts * round_up(m, 16) >= 512 && m <= 512 && (n >= 2048 || k >= 4096);
+}
+
+KeaGemmConfig swap_config(int m, int n, int k, int wbits, int parts, int sms) {
+    SwapPlan p;
+    KeaGemmConfig c{};
+    if (!swap_plan(m, n, k, wbits, parts, sms, 0, 0, &p)) return c;
+    c.tile_m = p.mt;
+    c.tile_n = kea::kPanelN;
+    c.splits = p.splits;
+    c.stages = p.stages;
+    c.smem_bytes = p.smem;
+    c.kernel = 3;
+    return c;
+}
+
 // The CUDA-core kernel: 8 channels per CTA (32 K slices per channel) spreads even 1024-channel layers over the SMs.
 // 16 (fewer, longer slices) measured faster for small weights (N x K <= 1M: the whole job is a few CTAs per SM) and
 // for wide layers (N > 3072) with several activation rows, unless the rows are the tokens of one 2-bit part (its
@@ -318,10 +452,14 @@ bool gemv_fits(int m, int parts, int ch) {
     return m >= 1 && m <= kea::kGemvMaxM && kea::gemv_smem_bytes(m * parts, ch) <= kea::kGemvMaxSmem;
 }
 
-// The full table: the CUDA-core kernel for M <= 16, the pair kernel where its shape rule holds, else the per-tile
-// kernel's entry.
+// The full table: the CUDA-core kernel for M x parts <= 4, the swap kernel up to 256 tokens, the pair kernel where its
+// shape rule holds, else the per-tile kernel's entry.
 KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
     KeaGemmConfig c = choose_tile(m, n, k, wbits, parts, sms);
+    if (swap_shape(m, n, k, parts)) {
+        const KeaGemmConfig s = swap_config(m, n, k, wbits, parts, sms);
+        if (s.kernel == 3) c = s;
+    }
     if (pair_shape(m, n, k, parts)) c = pair_config(wbits, parts);
     if (m * parts <= kGemvTableRows && gemv_fits(m, parts, gemv_channels(n, k, wbits, m, parts))) {
         c.kernel = 2;
@@ -432,12 +570,17 @@ int launch_gemv(const KeaGemmDesc *d, const KeaGemmConfig &c, void *stream) {
 
 // Launches the persistent CTA-pair kernel. KEA_ERR_UNSUPPORTED when an operand's alignment or stride rules it out
 // (the caller then runs the per-tile kernel); other codes are final.
+// The pair kernel's epilogue stores 16-byte vectors and TMA boxes: its outputs and channel constants must be aligned.
+bool pair_operands_ok(const KeaGemmDesc *d) {
+    const int esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
+    return aligned16(d->y) && (d->ldy * esize) % 16 == 0 && aligned16(d->alpha) && (!d->bias || aligned16(d->bias)) &&
+           (!d->acc || (aligned16(d->acc) && d->ld_acc % 4 == 0 && (d->parts == 1 || d->acc_part_stride % 4 == 0))) &&
+           (!d->residual || (aligned16(d->residual) && d->ld_residual % 4 == 0));
+}
+
 int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *stream) {
     const int esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
-    if (!aligned16(d->y) || (d->ldy * esize) % 16 || !aligned16(d->alpha) || (d->bias && !aligned16(d->bias)) ||
-        (d->acc && (!aligned16(d->acc) || d->ld_acc % 4 || (d->parts > 1 && d->acc_part_stride % 4))) ||
-        (d->residual && (!aligned16(d->residual) || d->ld_residual % 4)))
-        return KEA_ERR_UNSUPPORTED;
+    if (!pair_operands_ok(d)) return KEA_ERR_UNSUPPORTED;
     // Activations: 3-D (k, row, part) with 128 x 128 x 1 boxes in the 128-byte swizzle; columns >= k and rows >= m
     // read as 0.
     CUtensorMap qmap, ymap;
@@ -569,6 +712,199 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
     return KEA_OK;
 }
 
+// Argument checks of kea_lowbit_gemm (and its no-allocation variant): KEA_OK for a valid descriptor (m == 0 included).
+int validate_gemm(const KeaGemmDesc *d) {
+    if (!d) return KEA_ERR_INVALID_VALUE;
+    if (d->m < 0 || d->n < 1 || d->k < 1 || d->parts < 1 || d->parts > 3 || (d->wbits != 1 && d->wbits != 2) ||
+        (d->y_dtype != KEA_OUT_F32 && d->y_dtype != KEA_OUT_F16))
+        return KEA_ERR_INVALID_VALUE;
+    if (d->m == 0) return KEA_OK;
+    if (!d->q || !d->qs || !d->panels || !d->alpha || !d->y || d->ldy < d->n || d->ldq < d->k) return KEA_ERR_INVALID_VALUE;
+    if (d->acc && (d->ld_acc < d->n || (d->parts > 1 && d->acc_part_stride < (int64_t)d->m * d->ld_acc)))
+        return KEA_ERR_INVALID_VALUE;
+    if (d->residual && (d->y_dtype != KEA_OUT_F32 || d->ld_residual < d->n)) return KEA_ERR_INVALID_VALUE;
+    if (!aligned16(d->q) || d->ldq % 16 || !aligned16(d->panels)) return KEA_ERR_ALIGNMENT;
+    if (d->parts > 1 && (d->q_part_stride % 16 || d->q_part_stride < (int64_t)d->m * d->ldq)) return KEA_ERR_ALIGNMENT;
+    if (d->flags & ~(KEA_FLAG_SILU | KEA_FLAG_ORDER1 | KEA_FLAG_PDL | KEA_FLAG_NO_PAIR | KEA_FLAG_FORCE_PAIR |
+                     KEA_FLAG_FORCE_SWAP | KEA_FLAG_NO_SWAP | KEA_FLAG_TEST_STALL))
+        return KEA_ERR_INVALID_VALUE;
+    if ((d->flags & KEA_FLAG_NO_PAIR) && (d->flags & KEA_FLAG_FORCE_PAIR)) return KEA_ERR_INVALID_VALUE;
+    if ((d->flags & KEA_FLAG_FORCE_SWAP) &&
+        (d->tile_m || d->tile_n || (d->flags & (KEA_FLAG_NO_SWAP | KEA_FLAG_FORCE_PAIR))))
+        return KEA_ERR_INVALID_VALUE;
+    if ((d->flags & KEA_FLAG_TEST_STALL) && !(d->flags & KEA_FLAG_FORCE_SWAP)) return KEA_ERR_INVALID_VALUE;
+    if (d->wait_clocks < 0) return KEA_ERR_INVALID_VALUE;
+    return KEA_OK;
+}
+
+// ---- routing: the one decision of which kernel runs a descriptor (the launch, the no-allocation scratch check) ----
+enum Route { kRouteGemv, kRoutePair, kRouteSwap, kRouteTile };
+
+int route_gemm(const KeaGemmDesc *d, int sms, Route *route, KeaGemmConfig *c, SwapPlan *sp) {
+    const bool forced = d->tile_m || d->tile_n || d->splits || d->stages;
+    if (d->flags & KEA_FLAG_FORCE_SWAP) {   // splits / stages (0: the table's) apply to the swap kernel
+        if (!swap_plan(d->m, d->n, d->k, d->wbits, d->parts, sms, d->splits, d->stages, sp)) return KEA_ERR_UNSUPPORTED;
+        *route = kRouteSwap;
+        return KEA_OK;
+    }
+    *c = choose(d->m, d->n, d->k, d->wbits, d->parts, sms);
+    if (c->kernel == 2 && !forced) {
+        *route = kRouteGemv;
+        return KEA_OK;
+    }
+    if (forced && d->tile_m >= 1 && d->tile_m <= kea::kGemvMaxM) {   // the CUDA-core kernel, forced
+        if ((d->tile_n != 8 && d->tile_n != 16 && d->tile_n != 32) || !gemv_fits(d->m, d->parts, d->tile_n) ||
+            d->splits > 1 || d->stages > 1)
+            return KEA_ERR_UNSUPPORTED;
+        c->kernel = 2;
+        c->tile_m = d->m;
+        c->tile_n = d->tile_n;
+        *route = kRouteGemv;
+        return KEA_OK;
+    }
+    if (!forced && (d->flags & KEA_FLAG_FORCE_PAIR) && pair_fits(d->m, d->n, d->k, d->parts))
+        *c = pair_config(d->wbits, d->parts);
+    if (!forced && c->kernel == 1 && !(d->flags & KEA_FLAG_NO_PAIR) && pair_operands_ok(d)) {
+        *route = kRoutePair;
+        return KEA_OK;
+    }
+    if (!forced && c->kernel == 3 && !(d->flags & KEA_FLAG_NO_SWAP) &&
+        swap_plan(d->m, d->n, d->k, d->wbits, d->parts, sms, 0, 0, sp)) {
+        *route = kRouteSwap;
+        return KEA_OK;
+    }
+    *route = kRouteTile;
+    return KEA_OK;
+}
+
+// The split-K scratch the routed launch of this descriptor writes (the pair kernel's slices), 0 for none.
+size_t routed_scratch_bytes(const KeaGemmDesc *d, int sms) {
+    Route r;
+    KeaGemmConfig c{};
+    SwapPlan sp;
+    if (route_gemm(d, sms, &r, &c, &sp) != KEA_OK || r != kRoutePair) return 0;
+    return pair_workspace_bytes(d->m, d->n, d->k, d->parts, sms);
+}
+
+int launch_swap(const KeaGemmDesc *d, const SwapPlan &p, void *stream) {
+    const int kb_total = ceil_div(d->k, kea::kBK);
+    const bool q4d = d->k % kea::kBK == 0;
+    const long long pstride = d->parts > 1 ? d->q_part_stride : (long long)d->m * d->ldq;
+    // Activations: (k in block, row, part, k-block) with one box per stage of 128 k x mt rows x every part, landing
+    // as [part][row][128 bytes] (part p's tokens at rows p * mt); or, when K is not a multiple of 128, (k, row, part)
+    // with one 128 x mt box per part whose columns >= k read as zero. 128-byte swizzle; rows >= m read as zero.
+    CUtensorMap qmap;
+    CUresult r;
+    if (q4d) {
+        const cuuint64_t dims[4] = {(cuuint64_t)kea::kBK, (cuuint64_t)d->m, (cuuint64_t)d->parts, (cuuint64_t)kb_total};
+        const cuuint64_t strides[3] = {(cuuint64_t)d->ldq, (cuuint64_t)std::max<long long>(pstride, 16), (cuuint64_t)kea::kBK};
+        const cuuint32_t box[4] = {(cuuint32_t)kea::kBK, (cuuint32_t)p.mt, (cuuint32_t)d->parts, 1};
+        const cuuint32_t estr[4] = {1, 1, 1, 1};
+        r = g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t *>(d->q), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        const cuuint64_t dims[3] = {(cuuint64_t)d->k, (cuuint64_t)d->m, (cuuint64_t)d->parts};
+        const cuuint64_t strides[2] = {(cuuint64_t)d->ldq, (cuuint64_t)std::max<long long>(pstride, 16)};
+        const cuuint32_t box[3] = {(cuuint32_t)kea::kBK, (cuuint32_t)p.mt, 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        r = g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t *>(d->q), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS) return KEA_ERR_CUDA;
+    // Output: TMA box stores of 32 channels x 16 tokens (no swizzle) when y's base and row stride allow them.
+    const int esize = d->y_dtype == KEA_OUT_F16 ? 2 : 4;
+    CUtensorMap ymap;
+    std::memset(&ymap, 0, sizeof(ymap));
+    bool tma_store = aligned16(d->y) && (d->ldy * esize) % 16 == 0;
+    if (tma_store) {
+        const cuuint64_t ydims[2] = {(cuuint64_t)d->n, (cuuint64_t)d->m};
+        const cuuint64_t ystrides[1] = {(cuuint64_t)(d->ldy * esize)};
+        const cuuint32_t ybox[2] = {32, 16};
+        const cuuint32_t yestr[2] = {1, 1};
+        if (g_encode(&ymap, esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, d->y, ydims,
+                     ystrides, ybox, yestr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            tma_store = false;
+    }
+    kea::SwapArgs a{};
+    a.panels = d->panels;
+    a.qs = d->qs;
+    a.qs_stride = d->qs_part_stride;
+    a.alpha = d->alpha;
+    a.bias = d->bias;
+    a.y = d->y;
+    a.ldy = d->ldy;
+    a.y_f16 = d->y_dtype == KEA_OUT_F16;
+    a.acc = d->acc;
+    a.ld_acc = d->ld_acc;
+    a.acc_stride = d->acc_part_stride;
+    a.res = d->residual;
+    a.ld_res = d->ld_residual;
+    a.res_scale = d->residual_scale;
+    a.M = d->m;
+    a.N = d->n;
+    a.K = d->k;
+    a.kb_total = kb_total;
+    a.splits = p.splits;
+    a.stages = p.stages;
+    a.mt = p.mt;
+    a.rows = p.rows;
+    a.nacc = p.nacc;
+    a.tmem_cols = p.tmem_cols;
+    a.a_stage = (uint32_t)(p.rows * kea::kBK);
+    a.w_region = (uint32_t)p.stages * a.a_stage;
+    a.pk_region = a.w_region + (uint32_t)p.stages * kea::kSwapWTile;
+    a.epi_off = 0;
+    a.stg_off = (uint32_t)round_up(p.recv, 1024);
+    a.epi_alias = p.splits > 1 ? 1 : 0;
+    a.tma_store = tma_store ? 1 : 0;
+    a.units_per_owner = swap_units_per_owner(p.mt, p.splits);
+    a.q4d = q4d ? 1 : 0;
+    a.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
+    a.pdl = (d->flags & KEA_FLAG_PDL) ? 1 : 0;
+    a.stall = (d->flags & KEA_FLAG_TEST_STALL) ? 1 : 0;
+    a.wait_clocks = d->wait_clocks > 0 ? d->wait_clocks : kea::kWaitBudget;
+    a.err = d->error_word;
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ceil_div(d->n, kea::kPanelN), (unsigned)p.token_tiles, (unsigned)p.splits);
+    cfg.blockDim = dim3(kea::kSwapThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)p.smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attrs[2];
+    unsigned na = 0;
+    if (p.splits > 1) {
+        attrs[na].id = cudaLaunchAttributeClusterDimension;
+        attrs[na].val.clusterDim.x = 1;
+        attrs[na].val.clusterDim.y = 1;
+        attrs[na].val.clusterDim.z = (unsigned)p.splits;
+        ++na;
+    }
+    if (d->flags & KEA_FLAG_PDL) {
+        attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attrs[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = na;
+    cudaError_t e;
+    switch (d->wbits * 4 + d->parts) {
+        case 5: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_swap_kernel<1, 1>, qmap, ymap, a); break;
+        case 6: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_swap_kernel<1, 2>, qmap, ymap, a); break;
+        case 7: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_swap_kernel<1, 3>, qmap, ymap, a); break;
+        case 9: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_swap_kernel<2, 1>, qmap, ymap, a); break;
+        case 10: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_swap_kernel<2, 2>, qmap, ymap, a); break;
+        default: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_swap_kernel<2, 3>, qmap, ymap, a); break;
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return KEA_ERR_CUDA;
+    }
+    return KEA_OK;
+}
+
 }  // namespace
 
 // Two key groups per CTA when the grid is small (under two CTAs per SM): each CTA's chain of key blocks halves.
@@ -587,25 +923,6 @@ cudaError_t launch_rel_attention(cudaLaunchConfig_t *cfg, const kea::RelAttnArgs
 template <int KW>
 cudaError_t launch_glu_dw(cudaLaunchConfig_t *cfg, const kea::ConvArgs &a) {
     return cudaLaunchKernelEx(cfg, kea::glu_depthwise_kernel<KW>, a);
-}
-
-// ---- scratch of the no-allocation entry point ----------------------------------------------------------------
-// Split-K partial sums for kea_lowbit_gemm_noalloc, in a static device array so that its callers allocate nothing.
-// Host code must not use the array's name as a device address (on the host it names a stand-in); the address comes
-// from cudaGetSymbolAddress, looked up once per device with that device current.
-static __device__ __align__(256) int g_noalloc_scratch[KEA_NOALLOC_SCRATCH_BYTES / sizeof(int)];
-void *g_noalloc_addr[kMaxDevices] = {};
-
-// The split-K scratch kea_lowbit_gemm would use for this descriptor (the dispatch decisions it makes), 0 for none.
-size_t noalloc_scratch_need(const KeaGemmDesc *d, int sms) {
-    if (d->m < 1 || d->n < 1 || d->k < 1 || d->parts < 1 || d->parts > 3 || (d->wbits != 1 && d->wbits != 2))
-        return 0;   // kea_lowbit_gemm rejects or skips it
-    const bool forced = d->tile_m || d->tile_n || d->splits || d->stages;
-    if (forced || (d->flags & KEA_FLAG_NO_PAIR)) return 0;
-    const KeaGemmConfig c = choose(d->m, d->n, d->k, d->wbits, d->parts, sms);
-    if (c.kernel == 2) return 0;
-    const bool pair = c.kernel == 1 || ((d->flags & KEA_FLAG_FORCE_PAIR) && pair_fits(d->m, d->n, d->k, d->parts));
-    return pair ? pair_workspace_bytes(d->m, d->n, d->k, d->parts, sms) : 0;
 }
 
 extern "C" {
@@ -648,24 +965,14 @@ size_t kea_lowbit_workspace_bytes(int32_t m, int32_t n, int32_t k, int32_t wbits
 }
 
 int kea_lowbit_gemm_noalloc(const KeaGemmDesc *d, void *stream) {
-    if (!d) return KEA_ERR_INVALID_VALUE;
+    const int v = validate_gemm(d);
+    if (v != KEA_OK || d->m == 0) return v;
     int dev = 0;
-    const int st = device_setup(&dev);
+    const int st = device_setup(&dev, stream);
     if (st != KEA_OK) return st;
-    {   // once per device, with it current: the scratch array's device address
-        std::lock_guard<std::mutex> lock(g_mutex);
-        if (!g_noalloc_addr[dev]) {
-            void *addr = nullptr;
-            if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess || !addr) {
-                cudaGetLastError();
-                return KEA_ERR_CUDA;
-            }
-            g_noalloc_addr[dev] = addr;
-        }
-    }
-    if (noalloc_scratch_need(d, g_devices[dev].sms) > (size_t)KEA_NOALLOC_SCRATCH_BYTES) return KEA_ERR_SCRATCH_LIMIT;
+    if (routed_scratch_bytes(d, g_devices[dev].sms) > (size_t)KEA_NOALLOC_SCRATCH_BYTES) return KEA_ERR_SCRATCH_LIMIT;
     KeaGemmDesc g = *d;
-    g.workspace = g_noalloc_addr[dev];
+    g.workspace = g_devices[dev].noalloc_scratch;
     g.workspace_bytes = (int64_t)KEA_NOALLOC_SCRATCH_BYTES;
     return kea_lowbit_gemm(&g, stream);
 }
@@ -687,7 +994,7 @@ int kea_lowbit_prepare(const uint8_t *codes, int32_t wbits, int32_t n, int32_t k
     if (!codes || !panels || (wbits != 1 && wbits != 2) || n < 1 || k < 1) return KEA_ERR_INVALID_VALUE;
     if (!aligned16(panels)) return KEA_ERR_ALIGNMENT;
     int dev = 0;
-    const int st = device_setup(&dev);
+    const int st = device_setup(&dev, stream);
     if (st != KEA_OK) return st;
     const int row_bytes = ceil_div((long long)k * wbits, 8);
     const int kb = ceil_div(k, kea::kBK);
@@ -709,7 +1016,7 @@ int kea_lowbit_rel_attention(const KeaAttentionDesc *d, void *stream) {
     if (d->b == 0 || d->t == 0) return KEA_OK;
     if (d->b > 65535 || d->h > 65535) return KEA_ERR_UNSUPPORTED;
     int dev = 0;
-    const int st = device_setup(&dev);
+    const int st = device_setup(&dev, stream);
     if (st != KEA_OK) return st;
     kea::RelAttnArgs a{};
     a.qkv = d->qkv;
@@ -751,7 +1058,7 @@ int kea_lowbit_glu_depthwise(const KeaConvDesc *d, void *stream) {
     if (d->b == 0 || d->t == 0) return KEA_OK;
     if (d->b > 65535) return KEA_ERR_UNSUPPORTED;
     int dev = 0;
-    const int st = device_setup(&dev);
+    const int st = device_setup(&dev, stream);
     if (st != KEA_OK) return st;
     kea::ConvArgs a{};
     a.h = d->h;
@@ -794,7 +1101,7 @@ int kea_lowbit_quantize(const KeaQuantizeDesc *d, void *stream) {
         return KEA_ERR_ALIGNMENT;
     if (d->m == 0) return KEA_OK;
     int dev = 0;
-    const int st = device_setup(&dev);
+    const int st = device_setup(&dev, stream);
     if (st != KEA_OK) return st;
     kea::QuantArgs a{};
     a.x = d->x;
@@ -848,44 +1155,21 @@ int kea_lowbit_quantize(const KeaQuantizeDesc *d, void *stream) {
 }
 
 int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
-    if (!d) return KEA_ERR_INVALID_VALUE;
-    if (d->m < 0 || d->n < 1 || d->k < 1 || d->parts < 1 || d->parts > 3 || (d->wbits != 1 && d->wbits != 2) ||
-        (d->y_dtype != KEA_OUT_F32 && d->y_dtype != KEA_OUT_F16))
-        return KEA_ERR_INVALID_VALUE;
-    if (d->m == 0) return KEA_OK;
-    if (!d->q || !d->qs || !d->panels || !d->alpha || !d->y || d->ldy < d->n || d->ldq < d->k) return KEA_ERR_INVALID_VALUE;
-    if (d->acc && (d->ld_acc < d->n || (d->parts > 1 && d->acc_part_stride < (int64_t)d->m * d->ld_acc)))
-        return KEA_ERR_INVALID_VALUE;
-    if (d->residual && (d->y_dtype != KEA_OUT_F32 || d->ld_residual < d->n)) return KEA_ERR_INVALID_VALUE;
-    if (!aligned16(d->q) || d->ldq % 16 || !aligned16(d->panels)) return KEA_ERR_ALIGNMENT;
-    if (d->parts > 1 && (d->q_part_stride % 16 || d->q_part_stride < (int64_t)d->m * d->ldq)) return KEA_ERR_ALIGNMENT;
-    if (d->flags & ~(KEA_FLAG_SILU | KEA_FLAG_ORDER1 | KEA_FLAG_PDL | KEA_FLAG_NO_PAIR | KEA_FLAG_FORCE_PAIR))
-        return KEA_ERR_INVALID_VALUE;
-    if ((d->flags & KEA_FLAG_NO_PAIR) && (d->flags & KEA_FLAG_FORCE_PAIR)) return KEA_ERR_INVALID_VALUE;
-
+    const int v = validate_gemm(d);
+    if (v != KEA_OK || d->m == 0) return v;
     int dev = 0;
-    const int st = device_setup(&dev);
+    const int st = device_setup(&dev, stream);
     if (st != KEA_OK) return st;
 
-    KeaGemmConfig c = choose(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms);
     const bool forced = d->tile_m || d->tile_n || d->splits || d->stages;
-    if (c.kernel == 2 && !forced) return launch_gemv(d, c, stream);
-    if (forced && d->tile_m >= 1 && d->tile_m <= kea::kGemvMaxM) {   // the CUDA-core kernel, forced
-        if ((d->tile_n != 8 && d->tile_n != 16 && d->tile_n != 32) || !gemv_fits(d->m, d->parts, d->tile_n) ||
-            d->splits > 1 || d->stages > 1)
-            return KEA_ERR_UNSUPPORTED;
-        KeaGemmConfig g = c;
-        g.kernel = 2;
-        g.tile_m = d->m;
-        g.tile_n = d->tile_n;
-        return launch_gemv(d, g, stream);
-    }
-    if (!forced && (d->flags & KEA_FLAG_FORCE_PAIR) && pair_fits(d->m, d->n, d->k, d->parts))
-        c = pair_config(d->wbits, d->parts);
-    if (c.kernel == 1 && !forced && !(d->flags & KEA_FLAG_NO_PAIR)) {
-        const int ps = launch_pair(d, c, g_devices[dev].sms, stream);
-        if (ps != KEA_ERR_UNSUPPORTED) return ps;
-    }
+    Route route;
+    KeaGemmConfig c{};
+    SwapPlan sp;
+    const int rs = route_gemm(d, g_devices[dev].sms, &route, &c, &sp);
+    if (rs != KEA_OK) return rs;
+    if (route == kRouteGemv) return launch_gemv(d, c, stream);
+    if (route == kRouteSwap) return launch_swap(d, sp, stream);
+    if (route == kRoutePair) return launch_pair(d, c, g_devices[dev].sms, stream);
     if (c.kernel) c = choose_tile(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms);
     // Stacked parts (one 128-row tile holds every part's tokens): pe is the parts the tile's footprint counts.
     // forced tiles may stack whenever the shape allows; the table stacks where it chose to
@@ -1117,7 +1401,7 @@ int kea_trace_clear(void) {
 int kea_lowbit_read_error(uint32_t *out) {
     if (!out) return KEA_ERR_INVALID_VALUE;
     int dev = 0;
-    const int st = device_setup(&dev);
+    const int st = device_setup(&dev, nullptr, false);
     if (st != KEA_OK) return st;
     uint32_t v = 0;
     if (cudaMemcpyFromSymbol(&v, kea::g_device_error, sizeof(v)) != cudaSuccess) return KEA_ERR_CUDA;

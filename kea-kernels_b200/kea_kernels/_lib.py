@@ -18,6 +18,7 @@ LIB_PATH = Path(os.environ.get("KEA_LOWBIT_LIB", Path(__file__).resolve().parent
 OK, INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES, CUDA, NO_DEVICE, DEVICE_TIMEOUT, CAPTURE, SCRATCH_LIMIT = range(10)
 OUT_F32, OUT_F16 = 0, 1
 FLAG_SILU, FLAG_ORDER1, FLAG_PDL, FLAG_NO_PAIR, FLAG_FORCE_PAIR = 1, 2, 4, 8, 16
+FLAG_FORCE_SWAP, FLAG_NO_SWAP, FLAG_TEST_STALL = 32, 64, 128
 QUANT_INPUT_SILU, QUANT_PDL = 1, 2
 DEVERR_TIMEOUT, DEVERR_TAIL_BITS, DEVERR_TERNARY_11 = 1, 2, 4
 
@@ -41,7 +42,7 @@ class GemmDesc(ctypes.Structure):
         ("tile_m", ctypes.c_int32), ("tile_n", ctypes.c_int32), ("splits", ctypes.c_int32),
         ("stages", ctypes.c_int32), ("error_word", ctypes.c_void_p),
         ("residual", ctypes.c_void_p), ("ld_residual", ctypes.c_int64), ("residual_scale", ctypes.c_float),
-        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64), ("wait_clocks", ctypes.c_int64),
     ]
 
 
@@ -151,3 +152,14 @@ def read_device_error() -> int:
     v = ctypes.c_uint32(0)
     check(lib().kea_lowbit_read_error(ctypes.byref(v)), "read_error")
     return int(v.value)
+
+
+def raise_device_errors(word: int | None = None) -> None:
+    """Raises RuntimeError when a kernel reported an expired wait (KEA_DEVERR_TIMEOUT) - in `word` (a caller's error
+    word, already read back) or, when None, in the library's own word (read and cleared; synchronizes). The
+    reference raised RuntimeError for a failed launch (_nvrtc.py:123-124); a wait that ran out is this library's
+    equivalent, reported after the kernel has returned."""
+    bits = read_device_error() if word is None else int(word)
+    if bits & DEVERR_TIMEOUT:
+        raise RuntimeError(f"kernel: {lib().kea_lowbit_status_string(DEVICE_TIMEOUT).decode()} "
+                           f"(device error bits {bits:#x})")

@@ -16,7 +16,7 @@ from kea_kernels import _lib
 SMS = 148
 
 
-PER_TILE, PAIR, GEMV = 0, 1, 2
+PER_TILE, PAIR, GEMV, SWAP = 0, 1, 2, 3
 
 
 @dataclasses.dataclass(frozen=True)
@@ -24,7 +24,10 @@ class DotConfig:
     """CTA = `tile_m` tokens x `tile_n` channels over 1/`splits` of K, `stages` k128 blocks in flight (the per-tile
     tcgen05 kernel). kernel == PAIR: the persistent CTA-pair kernel, 256 x 256 tiles per pair of SMs (tcgen05
     cta_group::2), walked by at most SMS / 2 pairs, two accumulator buffers in tensor memory. kernel == GEMV: the
-    CUDA-core kernel for M <= 16, `tile_n` channels per CTA. Passing a PER_TILE config forces those tiles."""
+    CUDA-core kernel for M <= 16, `tile_n` channels per CTA. kernel == SWAP: the small-M kernel with the operands
+    swapped (128 weight rows on the MMA's M axis, every part's `tile_m` tokens on its N axis, K split over a cluster
+    of `splits` CTAs). Passing a PER_TILE config forces those tiles; a SWAP config forces the swap kernel with its
+    splits and stages."""
     tile_m: int
     tile_n: int
     splits: int
@@ -40,11 +43,17 @@ class DotConfig:
             return f"pair{self.tile_m}x{self.tile_n}_s{self.stages}"
         if self.kernel == GEMV:
             return f"gemv_n{self.tile_n}"
+        if self.kernel == SWAP:
+            return f"swap_t{self.tile_m}_c{self.splits}_s{self.stages}"
         return f"m{self.tile_m}_n{self.tile_n}_c{self.splits}_s{self.stages}"
 
     def validate(self, parts: int = 1) -> None:
         if self.kernel == GEMV:
             if not (1 <= self.tile_m <= 16 and self.tile_n in (8, 16, 32)):
+                raise ValueError(f"invalid config {self}")
+            return
+        if self.kernel == SWAP:
+            if not (1 <= self.splits <= 16 and 1 <= self.stages <= 8):
                 raise ValueError(f"invalid config {self}")
             return
         if not (self.tile_m in (128, 256) and self.tile_n in (32, 64, 128, 256) and 1 <= self.splits <= 16
@@ -57,6 +66,8 @@ class DotConfig:
         if self.pair:
             tiles = -(-n // self.tile_n) * -(-m // self.tile_m)
             return (2 * min(tiles, SMS // 2), 1, 1)
+        if self.kernel == SWAP:
+            return (-(-n // 128), -(-m // self.tile_m), self.splits)
         return (-(-n // self.tile_n), -(-m // self.tile_m), self.splits)
 
 

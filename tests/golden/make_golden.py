@@ -10,18 +10,29 @@ This script imports exactly those functions, draws seeded inputs the way the ref
 scales, the reference's int64 accumulators and its FP64 outputs. The oracle (oracle/kea_oracle.py) is checked
 against these fixtures by tests/test_oracle_golden.py; the GPU tests check the CUDA library against both.
 
-Usage: python tests/golden/make_golden.py [REFERENCE_ROOT]   (default /root/reference; needs only torch + numpy)
+Two files are written: golden.npz (small cases in full) and golden_config.npz (config-size cases from
+config_cases.py: the inputs are redrawn from their seeds by the tests, so only SHA-256 digests of the reference's
+codes, INT32 accumulators and FP64 outputs, per-row accumulator sums and a few sampled rows are stored).
+
+Usage: python tests/golden/make_golden.py REFERENCE_ROOT   (or KEA_REFERENCE_ROOT in the environment; the root of a
+kea-kernels checkout; needs only torch + numpy)
 """
 from __future__ import annotations
 
+import hashlib
 import importlib.util
+import os
 import sys
 from pathlib import Path
 
 import numpy as np
 import torch
 
-OUT = Path(__file__).resolve().parent / "golden.npz"
+HERE = Path(__file__).resolve().parent
+OUT = HERE / "golden.npz"
+OUT_CONFIG = HERE / "golden_config.npz"
+sys.path.insert(0, str(HERE))
+from config_cases import CONFIG_CASES, SAMPLE_ROWS, draw  # noqa: E402
 
 # (name, wbits, n, k, m, parts, bias): config-0/1 style cases at reduced N, ragged shapes, every part count.
 CASES = [
@@ -99,7 +110,38 @@ def main(root: Path) -> None:
     out["cases"] = np.array(names)
     np.savez_compressed(OUT, **out)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(names)} GEMM cases)")
+    config_fixtures(bits, formats, exact_epilogue)
+
+
+def digest(a: np.ndarray) -> np.ndarray:
+    return np.frombuffer(hashlib.sha256(np.ascontiguousarray(a).tobytes()).digest(), dtype=np.uint8)
+
+
+def config_fixtures(bits, formats, exact_epilogue) -> None:
+    out: dict[str, np.ndarray] = {}
+    for name, wbits, n, k, m, parts in CONFIG_CASES:
+        w, q, qs, alpha = draw(wbits, n, k, m, parts)
+        codes = bits.pack_signs(w) if wbits == 1 else formats.pack_ternary(w)
+        dense = bits.unpack_signs(codes, k) if wbits == 1 else formats.unpack_ternary(codes, k)
+        assert torch.equal(dense, w)
+        acc = torch.stack([q[c].to(torch.int64) @ dense.to(torch.int64).t() for c in range(parts)])
+        y64 = exact_epilogue(q, qs, dense, alpha, parts)
+        acc32 = acc.to(torch.int32).numpy()
+        out[f"{name}/meta"] = np.array([wbits, n, k, m, parts], dtype=np.int64)
+        out[f"{name}/codes_sha256"] = digest(codes.numpy())
+        out[f"{name}/acc_sha256"] = digest(acc32)
+        out[f"{name}/y64_sha256"] = digest(y64.numpy())
+        out[f"{name}/acc_rowsum"] = acc.sum(dim=2).numpy()
+        out[f"{name}/acc_rows"] = acc32[:, list(SAMPLE_ROWS)]
+        out[f"{name}/y64_rows"] = y64.numpy()[list(SAMPLE_ROWS)]
+        print(f"{name}: reference accumulators and FP64 outputs recorded")
+    out["cases"] = np.array([c[0] for c in CONFIG_CASES])
+    np.savez_compressed(OUT_CONFIG, **out)
+    print(f"wrote {OUT_CONFIG} ({OUT_CONFIG.stat().st_size} bytes)")
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KEA_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT (or set KEA_REFERENCE_ROOT)")
+    main(Path(root))

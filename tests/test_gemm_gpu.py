@@ -52,7 +52,7 @@ def _channel(n: int, seed: int, bias: bool):
 
 
 def _run(codes, wbits, n, k, q, qs, alpha, bias, *, flags=0, out=torch.float32, config=None, pdl=False, pair=True,
-         pair_only=False):
+         pair_only=False, swap=True):
     parts, m, ldq = q.shape
     panels = lowbit.prepare_panels(torch.from_numpy(codes).to(DEV), wbits, n, k)
     qd, qsd = torch.from_numpy(q).to(DEV), torch.from_numpy(qs).to(DEV)
@@ -61,7 +61,7 @@ def _run(codes, wbits, n, k, q, qs, alpha, bias, *, flags=0, out=torch.float32, 
     y = torch.full((m, n), float("nan"), device=DEV, dtype=out)
     acc = torch.full((parts, m, n), -7, device=DEV, dtype=torch.int32)
     lowbit.gemm(qd, qsd, ldq, m, panels, wbits, n, k, ad, bd, y, parts=parts, silu=bool(flags & 1),
-                order=(flags >> 1) & 1, acc=acc, config=config, pdl=pdl, pair=pair, force_pair=pair_only)
+                order=(flags >> 1) & 1, acc=acc, config=config, pdl=pdl, pair=pair, force_pair=pair_only, swap=swap)
     torch.cuda.synchronize()
     assert _lib.read_device_error() == 0
     return y.cpu(), acc.cpu().numpy()
@@ -164,15 +164,17 @@ def test_gemm_parts_and_order(wbits, parts, n, k, m, flags):
                                    (1024, 4096, 1), (1024, 1024, 5), (512, 256, 33), (1024, 1024, 126),
                                    (4096, 1024, 368), (1024, 4096, 257), (640, 512, 511)])
 @pytest.mark.parametrize("flags", [0, 2, 1])
-def test_stacked_parts_small_m(wbits, parts, n, k, m, flags):
-    """M <= 512 with 2 or 3 parts: the tokens are cut into tiles of mp tokens whose parts are stacked along one
-    128-row tile (one MMA per K step for all parts), with and without split-K; bit for bit the oracle's results."""
+@pytest.mark.parametrize("swap", [True, False])
+def test_stacked_parts_small_m(wbits, parts, n, k, m, flags, swap):
+    """M <= 512 with 2 or 3 parts, both small-M kernels: the swap kernel stacks the parts along the MMA's N (token)
+    axis; the 128-token-tile kernel (swap=False) cuts the tokens into tiles of mp tokens whose parts are stacked along
+    one 128-row tile, with and without split-K. Bit for bit the oracle's results."""
     seed = wbits * 31 + parts * 7 + n + k + m + flags
     codes, w = _codes(wbits, n, k, seed)
     q, qs = _activations(parts, m, k, seed)
     alpha, bias = _channel(n, seed, flags != 2)
     out = torch.float16 if flags == 2 else torch.float32
-    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags, out=out)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias, flags=flags, out=out, swap=swap)
     want, want_acc = oracle.reference(q, qs, w, alpha, bias, flags)
     _check(y, acc, want, want_acc, flags)
 
@@ -619,13 +621,18 @@ def test_graph_capture_replays_bitwise():
 @pytest.mark.parametrize("n,k,m,parts,kernel", [(1024, 1024, 2, 1, configs.GEMV), (4096, 1024, 125, 1, configs.PER_TILE),
                                                 (1024, 4096, 38, 1, configs.PER_TILE),
                                                 (1024, 1024, 40, 3, configs.PER_TILE),
-                                                (300, 200, 77, 2, configs.PER_TILE), (4096, 1024, 2048, 1, configs.PAIR),
+                                                (300, 200, 77, 2, configs.PER_TILE), (4096, 1024, 16, 1, configs.SWAP),
+                                                (1024, 4096, 16, 1, configs.SWAP), (1024, 4096, 256, 3, configs.SWAP),
+                                                (2048, 1024, 256, 2, configs.SWAP), (1024, 1024, 200, 1, configs.SWAP), (4096, 1024, 2048, 1, configs.PAIR),
                                                 (4096, 1024, 8192, 2, configs.PAIR)])
 @pytest.mark.parametrize("scale", [1.0, 0.5])
 def test_residual_epilogue_equals_unfused(wbits, n, k, m, parts, kernel, scale):
-    """The skip connection in the epilogue (CUDA-core, per-tile with and without split-K and stacked parts, pair
-    with one and two parts): bit for bit PyTorch's `residual + scale * y`, also written in place over the residual."""
-    assert configs.choose(m, n, k, wbits, parts).kernel == kernel
+    """The skip connection in the epilogue (CUDA-core, swap with and without split-K, per-tile with and without
+    split-K and stacked parts, pair with one and two parts): bit for bit PyTorch's `residual + scale * y`, also
+    written in place over the residual."""
+    swap = kernel != configs.PER_TILE
+    if swap:
+        assert configs.choose(m, n, k, wbits, parts).kernel == kernel
     seed = wbits * 7 + n + k + m + parts
     codes, _ = _codes(wbits, n, k, seed)
     q, qs = _activations(parts, m, k, seed)
@@ -635,14 +642,14 @@ def test_residual_epilogue_equals_unfused(wbits, n, k, m, parts, kernel, scale):
     ad, bd = torch.from_numpy(alpha).to(DEV), torch.from_numpy(bias).to(DEV)
     res = torch.randn(m, n, generator=torch.Generator().manual_seed(seed)).to(DEV)
     y = torch.empty(m, n, device=DEV)
-    lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, y, parts=parts)
+    lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, y, parts=parts, swap=swap)
     want = res + scale * y
     fused = torch.empty(m, n, device=DEV)
     lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, fused, parts=parts, residual=res,
-                residual_scale=scale)
+                residual_scale=scale, swap=swap)
     inplace = res.clone()
     lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, inplace, parts=parts, residual=inplace,
-                residual_scale=scale)
+                residual_scale=scale, swap=swap)
     torch.cuda.synchronize()
     assert _lib.read_device_error() == 0
     assert torch.equal(fused.view(torch.int32), want.view(torch.int32))

@@ -22,7 +22,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.kea_lowbit_version() == 1
+    assert lib.kea_lowbit_version() == 2
     assert lib.kea_lowbit_status_string(0) == b"success"
     assert lib.kea_lowbit_status_string(4) == b"invalid packed codes"
 
@@ -57,6 +57,18 @@ def test_every_shape_has_a_valid_config(n, k, wbits, parts):
             assert c.tile_m == 256 and c.tile_n == 256 and parts <= 2 and c.splits == 1
             assert c.smem_bytes <= 227 * 1024
             continue
+        swap = m <= 32 or 128 < m <= 256 if parts == 1 else (parts * -(-m // 16) * 16 >= 512 and m <= 512
+                                                                and (n >= 2048 or k >= 4096))
+        assert (c.kernel == configs.SWAP) == (swap and not (c.kernel == configs.PAIR))
+        if c.kernel == configs.SWAP:   # 128 channels x tile_m tokens of every part (<= 512 TMEM columns)
+            assert c.tile_n == 128 and c.tile_m % 16 == 0 and c.tile_m <= 256 and parts * c.tile_m <= 512
+            assert c.tile_m * -(-m // c.tile_m) >= m and c.tile_m < m + 16 * -(-m // c.tile_m)
+            assert 1 <= c.splits <= min(kb, 8) and 1 <= c.stages <= 8 and c.smem_bytes <= 227 * 1024
+            cfg = configs.choose(m, n, k, wbits, parts)
+            cfg.validate(parts)
+            gx, gy, gz = cfg.grid(m, n)
+            assert gx * gy * gz <= 148 or gz == 1      # K is split only while the grid stays within one wave
+            continue
         assert c.tile_m in (128, 256) and c.tile_n in (32, 64, 128, 256)
         assert (c.tile_m // 128) * parts * c.tile_n <= 512
         assert 1 <= c.splits <= min(kb, 16) and 1 <= c.stages <= 8
@@ -72,9 +84,15 @@ def test_every_shape_has_a_valid_config(n, k, wbits, parts):
 
 def test_small_m_splits_k_and_large_m_does_not():
     c = _lib.choose_config(125, 4096, 1024, 1, 1)       # 32-channel tiles already give 128 CTAs
-    assert c.tile_m == 128 and c.tile_n == 32 and c.splits == 1
+    assert (c.kernel, c.tile_m, c.tile_n, c.splits) == (configs.PER_TILE, 128, 32, 1)
     c = _lib.choose_config(125, 1024, 4096, 1, 1)       # 32 channel tiles: K split over a cluster
-    assert c.tile_m == 128 and c.splits > 1
+    assert c.kernel == configs.PER_TILE and c.splits > 1
+    c = _lib.choose_config(16, 4096, 1024, 1, 1)        # swap: 32 channel tiles x 4 K slices = 128 CTAs
+    assert (c.kernel, c.tile_m, c.tile_n, c.splits) == (configs.SWAP, 16, 128, 4)
+    c = _lib.choose_config(16, 1024, 4096, 1, 1)        # swap: 8 channel tiles, K over a cluster of 8
+    assert (c.kernel, c.splits) == (configs.SWAP, 8)
+    c = _lib.choose_config(256, 4096, 1024, 1, 3)       # three parts stacked along the MMA's N: 3 x 128 tokens x 2
+    assert (c.kernel, c.tile_m, c.splits) == (configs.SWAP, 128, 1)
     c = _lib.choose_config(8192, 4096, 1024, 1, 1)
     assert c.splits == 1
 
@@ -103,7 +121,12 @@ def test_c_abi_argument_errors_are_reported_before_any_device_work():
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(q=24)), None) == _lib.ALIGNMENT
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(ldq=1000)), None) == _lib.INVALID_VALUE   # ldq < k
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(ldq=1032, k=1030)), None) == _lib.ALIGNMENT  # ldq % 16
-    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=64)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=256)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_TEST_STALL)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_FORCE_SWAP, tile_m=128)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_FORCE_SWAP | _lib.FLAG_NO_SWAP)), None) == \
+        _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(wait_clocks=-1)), None) == _lib.INVALID_VALUE
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(residual=16, ld_residual=4095)), None) == _lib.INVALID_VALUE
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(residual=16, ld_residual=4096, y_dtype=1)), None) == \
         _lib.INVALID_VALUE                                # a residual needs FP32 output
