@@ -9,8 +9,9 @@ with host buffers (pinned host -> device activations, device -> pinned host outp
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-`--impl reference` times the reference's CPU algorithm (unpack the packed codes, exact integer GEMM, FP32 epilogue;
-the C restatement in oracle/) on a bounded sample of the sweep, with every host core.
+`--impl reference` times the reference's CPU algorithm (unpack the packed codes, exact integer GEMM, FP32 epilogue,
+fp16 out) on the same workload - every step one pass over the whole sweep - with every host core: the strong
+restatement of that arithmetic through FP32 BLAS (exact: every partial sum is an integer below 2^24), oracle.gemm_blas.
 """
 from __future__ import annotations
 
@@ -32,7 +33,6 @@ UNIT = "TOPS"
 SHAPES = [(4096, 1024), (1024, 4096)]
 MS = [1, 16, 125, 512, 2048, 8192]
 CASES = [(wbits, n, k, m) for wbits in (1, 2) for (n, k) in SHAPES for m in MS]
-SAMPLE_MS = (1, 16, 125, 512)           # the CPU sample: every case with M <= 512
 POOL = 4                                 # distinct weight / activation sets per case in the step graphs
 COLD_BYTES = 512 << 20                   # per (wbits, N, K): distinct weights swept by the per-case cold timing
 L2_BYTES = 126 << 20
@@ -107,18 +107,18 @@ class ClockSampler:
 
 
 # ---- the CPU side (reference arm and cpu_baseline) --------------------------------------------------------------
-def cpu_sample(threads: int, min_seconds: float = 10.0, max_seconds: float = 30.0, repeats: int | None = None):
-    """Times the reference's CPU algorithm (oracle port) over the M <= 512 cases of the sweep. Returns
-    (TOPS, seconds, passes)."""
+WORKLOAD = ("BASELINE config 1: M sweep {1,16,125,512,2048,8192} x (N,K) in {(4096,1024),(1024,4096)} x "
+            "{1-bit, 2-bit} weights, 1 INT8 part, fp16 out")
+
+
+def _cpu_work(cases, seed=0):
     sys.path.insert(0, str(ROOT / "oracle"))
     import numpy as np
     import kea_oracle as oracle
 
-    rng = np.random.default_rng(0)
+    rng = np.random.default_rng(seed)
     work = []
-    for wbits, n, k, m in CASES:
-        if m not in SAMPLE_MS:
-            continue
+    for wbits, n, k, m in cases:
         if wbits == 1:
             codes = oracle.pack_signs(rng.choice(np.array([-1, 1], dtype=np.int8), size=(n, k)))
         else:
@@ -127,16 +127,26 @@ def cpu_sample(threads: int, min_seconds: float = 10.0, max_seconds: float = 30.
         qs = rng.uniform(0.005, 0.02, size=(1, m)).astype(np.float32)
         alpha = rng.uniform(0.01, 0.05, size=n).astype(np.float16).astype(np.float32)
         work.append((codes, wbits, n, k, q, qs, alpha))
+    return oracle, work
+
+
+def cpu_sample(threads: int, min_seconds: float = 10.0, max_seconds: float = 30.0, repeats: int | None = None):
+    """Times the reference's CPU algorithm on the host cores over the GPU arm's whole workload (the 24 GEMMs of the
+    config-1 sweep; one pass = one step): unpack the export codes, exact integer GEMM through FP32 BLAS (exact: every
+    partial sum is an integer below 2^24), the comb<1> epilogue in FP32, FP16 output - the strong CPU restatement
+    (oracle.gemm_blas) in PyTorch's multi-threaded CPU kernels on `threads` threads.
+    Returns (TOPS, seconds, passes, ops per pass)."""
+    import torch
+
+    torch.set_num_threads(threads)
+    oracle, work = _cpu_work(CASES)
     total_ops = sum(ops(q.shape[1], n, k) for _, _, n, k, q, _, _ in work)
 
     def one_pass():
         for codes, wbits, n, k, q, qs, alpha in work:
-            w, status = oracle.unpack_c(codes, wbits, n, k)
-            assert status == 0
-            y, _ = oracle.gemm(q, qs, w, alpha, threads=threads)
-            oracle.to_f16(y)
+            oracle.gemm_blas(codes, wbits, q, qs, alpha)
 
-    one_pass()  # warm-up (also builds the oracle library if needed)
+    one_pass()  # warm-up
     passes, t0 = 0, time.perf_counter()
     while True:
         one_pass()
@@ -149,49 +159,66 @@ def cpu_sample(threads: int, min_seconds: float = 10.0, max_seconds: float = 30.
     return total_ops * passes / elapsed / 1e12, elapsed, passes, total_ops
 
 
-def cpu_clip_sample(layers: int = 2) -> dict:
-    """The clip's low-bit GEMM chain on the host cores through the reference's CPU algorithm (oracle port: unpack,
-    exact integer GEMM, FP32 epilogue) for `layers` of the 24 layers (8 GEMMs each at M = 125), scaled to 24."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import numpy as np
-    import kea_oracle as oracle
+def cpu_baseline_record(tops: float, seconds: float, passes: int, total: int, threads: int) -> dict:
+    return {"value": tops, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"the whole config-1 sweep ({len(CASES)} GEMMs, {total / 1e9:.1f} GOP per pass, {passes} passes, "
+                      f"{seconds:.1f} s): unpack the export codes, exact integer GEMM through FP32 BLAS, FP32 comb<1> "
+                      "epilogue, fp16 out (oracle.gemm_blas: PyTorch CPU kernels)"}
+
+
+def cpu_literal_sample(threads: int, seconds: float = 5.0) -> dict:
+    """The reference test's literal oracle (unpack, then an integer triple loop with the FP32 epilogue; the C
+    restatement in oracle/, `threads` threads) on the M <= 16 cases of the sweep: context for the strong baseline."""
+    oracle, work = _cpu_work([c for c in CASES if c[3] <= 16], seed=1)
+    total = sum(ops(q.shape[1], n, k) for _, _, n, k, q, _, _ in work)
+    passes, t0 = 0, time.perf_counter()
+    while passes == 0 or time.perf_counter() - t0 < seconds:
+        for codes, wbits, n, k, q, qs, alpha in work:
+            w, status = oracle.unpack_c(codes, wbits, n, k)
+            oracle.gemm(q, qs, w, alpha, threads=threads)
+        passes += 1
+    elapsed = time.perf_counter() - t0
+    return {"value": total * passes / elapsed / 1e12, "unit": UNIT, "cores": threads,
+            "sample": f"M <= 16 cases of the sweep ({total / 1e9:.2f} GOP per pass, {passes} passes, {elapsed:.1f} s): "
+                      "unpack + integer triple loop + FP32 epilogue (oracle/kea_oracle.c)"}
+
+
+def cpu_clip_sample() -> dict:
+    """The clip's low-bit GEMM chain on the host cores through the reference's CPU algorithm: 24 layers x 8 GEMMs at
+    M = 125 (config 2's shapes), each unpack + exact integer GEMM (FP32 BLAS) + FP32 epilogue + fp16 out
+    (oracle.gemm_blas, PyTorch CPU kernels on every host thread)."""
+    import torch
 
     threads = os.cpu_count() or 1
-    rng = np.random.default_rng(1)
+    torch.set_num_threads(threads)
     shapes = [(4096, 1024), (1024, 4096), (3072, 1024), (1024, 1024), (2048, 1024), (1024, 1024), (4096, 1024),
               (1024, 4096)]
-    work = []
-    for n, k in shapes * layers:
-        codes = oracle.pack_signs(rng.choice(np.array([-1, 1], dtype=np.int8), size=(n, k)))
-        q = rng.integers(-127, 128, size=(1, 125, k), dtype=np.int8)
-        qs = rng.uniform(0.005, 0.02, size=(1, 125)).astype(np.float32)
-        alpha = rng.uniform(0.01, 0.05, size=n).astype(np.float32)
-        work.append((codes, n, k, q, qs, alpha))
+    oracle, work = _cpu_work([(1, n, k, 125) for n, k in shapes * 24], seed=1)
     t0 = time.perf_counter()
-    for codes, n, k, q, qs, alpha in work:
-        w, status = oracle.unpack_c(codes, 1, n, k)
-        oracle.gemm(q, qs, w, alpha, threads=threads)
+    for codes, wbits, n, k, q, qs, alpha in work:
+        oracle.gemm_blas(codes, wbits, q, qs, alpha)
     seconds = time.perf_counter() - t0
-    return {"ms_per_clip": seconds * 1e3 * 24 / layers, "cores": threads, "kind": "port",
-            "sample": f"{layers} of 24 layers ({8 * layers} GEMMs at M = 125, unpack + exact integer GEMM + FP32 "
-                      f"epilogue, oracle/kea_oracle.c), {seconds:.2f} s, scaled by 24 / {layers}"}
+    return {"ms_per_clip": seconds * 1e3, "cores": threads, "kind": "port",
+            "sample": f"all 24 layers ({len(work)} GEMMs at M = 125: unpack + exact integer GEMM through FP32 BLAS + "
+                      f"FP32 epilogue + fp16 out, oracle.gemm_blas), {seconds:.2f} s"}
 
 
 def reference_arm(args) -> None:
+    """The reference's CPU algorithm on the host cores, on the GPU arm's own workload and metric: each step one pass
+    over the whole config-1 sweep (the strong FP32-BLAS restatement, every host thread)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    tops_w, _, _, total_ops = cpu_sample(threads, repeats=max(1, args.warmup))
-    tops, seconds, passes, _ = cpu_sample(threads, repeats=max(1, args.steps))
-    sample = (f"the M<=512 cases of the config-1 sweep ({len(SAMPLE_MS) * 4} GEMMs, {total_ops / 1e9:.1f} GOP per "
-              f"step): unpack the packed codes, exact integer GEMM, FP32 epilogue, fp16 cast")
+    cpu_sample(threads, repeats=max(1, args.warmup))
+    tops, seconds, passes, total = cpu_sample(threads, repeats=max(1, args.steps))
+    base = cpu_baseline_record(tops, seconds, passes, total, threads)
     line = {"impl": "reference", "metric": METRIC, "value": tops, "unit": UNIT, "n_gpus": args.gpus,
             "steps": passes, "warmup": args.warmup, "ms_per_step": seconds * 1e3 / passes,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "BASELINE config 1 (M sweep, 1-bit and 2-bit) - bounded CPU sample",
-                       "sample": sample},
-            "cpu_baseline": {"value": tops, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "config": {"workload": WORKLOAD, "gemms_per_step": len(CASES), "gop_per_step": total / 1e9,
+                       "parallelism": "host cores"},
+            "cpu_baseline": base,
             "e2e": {"value": tops, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -377,17 +404,13 @@ def main() -> None:
     cpu = None
     if world == 1:
         threads = os.cpu_count() or 1
-        tops, seconds, passes, total = cpu_sample(threads)
-        cpu = {"value": tops, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"M<=512 cases of the sweep ({total / 1e9:.1f} GOP per pass, {passes} passes, "
-                         f"{seconds:.1f} s): unpack + exact integer GEMM + FP32 epilogue (oracle/kea_oracle.c)"}
+        cpu = cpu_baseline_record(*cpu_sample(threads), threads)
+        cpu["literal_oracle"] = cpu_literal_sample(threads)
 
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "BASELINE config 1: M sweep {1,16,125,512,2048,8192} x (N,K) in "
-                                   "{(4096,1024),(1024,4096)} x {1-bit, 2-bit} weights, 1 INT8 part, fp16 out",
-                       "gemms_per_step": len(CASES), "gop_per_step": step_ops / 1e9,
+            "config": {"workload": WORKLOAD, "gemms_per_step": len(CASES), "gop_per_step": step_ops / 1e9,
                        "l2": "inputs larger than L2: rotating pools of weights/activations, ~220 MB written per step",
                        "parallelism": f"replicas x{world}", "pdl": pdl},
             "roofline": roofline, "roofline_small_m": roofline_small, "cpu_baseline": cpu, "e2e": e2e,

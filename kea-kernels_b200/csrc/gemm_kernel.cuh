@@ -40,31 +40,6 @@ constexpr long long kWaitBudget = 4000000000LL;            // SM clocks (about 2
 
 __device__ uint32_t g_device_error;  // the library's own error word (KEA_DEVERR_* bits)
 
-// Phase timestamps for latency studies: compiled in only with -DKEA_TRACE (one %globaltimer value per CTA and
-// phase, read back by kea_trace_read). The default build has no trace code.
-#ifdef KEA_TRACE
-// Phase 0 holds the CTA's start as %globaltimer ns (slow to read, so read once); the other phases hold SM clock
-// cycles since that start (clock64 is cheap and the whole CTA runs on one SM). The start clock lives in shared
-// memory (written before the kernel's first __syncthreads), so a trace point costs a clock read and one store.
-constexpr int kTraceCtas = 4096, kTracePhases = 32;
-__device__ unsigned long long g_trace[kTraceCtas][kTracePhases];
-__shared__ long long s_trace_clock0;
-KEA_DEVI void trace_point(int phase) {
-    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-    if (cta >= kTraceCtas) return;
-    if (phase == 0) {
-        unsigned long long t;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        s_trace_clock0 = clock64();
-        g_trace[cta][0] = t;
-    } else {
-        g_trace[cta][phase] = (unsigned long long)(clock64() - s_trace_clock0);
-    }
-}
-#define KEA_TRACE_POINT(cond, phase) do { if (cond) trace_point(phase); } while (0)
-#else
-#define KEA_TRACE_POINT(cond, phase) do { } while (0)
-#endif
 
 struct GemmArgs {
     const uint8_t *panels;
@@ -348,7 +323,6 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
     const uint32_t A0 = base, B0 = base + a.b_region, PK0 = base + a.pk_region;
     const uint32_t tx_bytes = a.act_tx + a.pk_stage;
 
-    KEA_TRACE_POINT(threadIdx.x == 0, 0);
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&bar_full[s]), 1);
@@ -370,7 +344,6 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
-    KEA_TRACE_POINT(threadIdx.x == 0, 1);
 
     // With programmatic dependent launch, everything below may read what the previous kernel wrote. In one-shot
     // mode the packed codes (static weights) are loaded and expanded first, while the previous kernel finishes:
@@ -461,14 +434,12 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
             }
             __syncwarp();
             issued = i + 1;
-            KEA_TRACE_POINT(lane == 0 && i == 0, 2);
             if (++kbi == nkb) kbi = 0;
             if (++s == S) {
                 s = 0;
                 ph ^= 1;
             }
         }
-        KEA_TRACE_POINT(lane == 0, 3);
         if (!ok) {
             if (lane == 0) report(a.err, 1u);
             if (a.oneshot) {
@@ -517,9 +488,6 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                 if (lane == 0) report(a.err, 1u);
                 break;
             }
-            KEA_TRACE_POINT(lane == 0 && i == 0, 6);
-            KEA_TRACE_POINT(lane == 0 && i == nkb - 1, 14);
-            KEA_TRACE_POINT(lane == 0 && i < 8, 23 + i);
             // The mbarrier wait orders the operands (TMA writes, or expander writes behind fence.proxy.async) before
             // the MMAs' shared-memory reads; no tcgen05 fence per stage (it would drain the MMA pipe).
             // The whole warp forms the stage's descriptors (warp-uniform values); one elected lane issues the stage's
@@ -548,7 +516,6 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
         }
         if (elect_one()) mma_commit(smem_u32(&bar_acc));
         __syncwarp();
-        KEA_TRACE_POINT(lane == 0, 8);
     } else {
         // ---------------- expanders ----------------
         const int e = threadIdx.x - 64;   // 0 .. 511
@@ -573,14 +540,12 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                 ok = false;
                 if (lane == 0) report(a.err, 1u);
             } else {
-                KEA_TRACE_POINT(threadIdx.x == 64, 4);
                 for (int f = e; f < (nkb << units_log2); f += kEpiThreads) {
                     const int st = f >> units_log2;
                     expand_unit<WBITS>(PK0 + (uint32_t)st * a.pk_stage, B0 + (uint32_t)st * a.b_stage, tn_log2,
                                        f & (units - 1));
                 }
                 fence_async_shared();
-                KEA_TRACE_POINT(threadIdx.x == 64, 5);
                 __syncwarp();
                 if (lane == 0)
                     for (int st = 0; st < nkb; ++st) mbar_arrive(smem_u32(&bar_exp[st]));
@@ -601,14 +566,12 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                     ok = false;
                     if (lane == 0) report(a.err, 1u);
                 } else {
-                    KEA_TRACE_POINT(threadIdx.x == 64 && c == 0, 4);
                     for (int f = e + (i0 << units_log2); f < (i1 << units_log2); f += kEpiThreads) {
                         const int st = f >> units_log2;
                         expand_unit<WBITS>(PK0 + (uint32_t)st * a.pk_stage, B0 + (uint32_t)st * a.b_stage, tn_log2,
                                            f & (units - 1));
                     }
                     fence_async_shared();
-                    KEA_TRACE_POINT(threadIdx.x == 64 && c == 0, 5);
                     __syncwarp();
                     if (lane == 0)
                         for (int st = i0; st < i1; ++st) mbar_arrive(smem_u32(&bar_exp[st]));
@@ -624,12 +587,9 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                 if (lane == 0) report(a.err, 1u);
                 break;
             }
-            KEA_TRACE_POINT(threadIdx.x == 64 && i == 0, 4);
-            KEA_TRACE_POINT(threadIdx.x == 64 && i < 8, 15 + i);
             const uint32_t spk = PK0 + (uint32_t)s * a.pk_stage, sb = B0 + (uint32_t)s * a.b_stage;
             for (int u = e; u < units; u += kEpiThreads) expand_unit<WBITS>(spk, sb, tn_log2, u);
             fence_async_shared();
-            KEA_TRACE_POINT(threadIdx.x == 64 && i == 0, 5);
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&bar_exp[s]));
             if (++s == S) {
@@ -657,7 +617,6 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
         bool done = ok && mbar_wait(smem_u32(&bar_acc), 0, kWaitBudget);
         done = __all_sync(0xFFFFFFFFu, done);
         if (!done && ok && lane == 0) report(a.err, 1u);
-        KEA_TRACE_POINT(threadIdx.x == 64, 9);
         tc_fence_after();
         if (a.stack && a.splits == 1) {
             // Stacked parts: part p of token t sits in TMEM lane p * mp + t, so the lanes of one token live in
@@ -837,10 +796,8 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
         }
     }
 
-    KEA_TRACE_POINT(threadIdx.x == 64, 10);
     if (a.splits > 1) {
         cluster_sync_all();  // every partial has landed in its owner's shared memory
-        KEA_TRACE_POINT(threadIdx.x == 64, 11);
         if (warp >= 2 && a.stack) {
             // Stacked parts: sum the splits per stacked row into the first source slot, then combine each token's
             // parts (rows p * mp + t) for this rank's channel groups.
@@ -915,14 +872,12 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
         }
     }
 
-    KEA_TRACE_POINT(threadIdx.x == 64, 12);
     grid_launch_dependents();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, a.tmem_cols);
-        KEA_TRACE_POINT(lane == 0, 13);
     }
 }
 

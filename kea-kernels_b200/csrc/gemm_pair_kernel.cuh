@@ -74,20 +74,6 @@ struct PairArgs {
     uint32_t *err;
 };
 
-// Per-step timestamps of the first pair (SM clocks since each CTA's start) for latency studies: compiled in only
-// with -DKEA_TRACE and read back by kea_pair_trace_read. The default build has no trace code.
-#ifdef KEA_TRACE
-constexpr int kPairTraceEvents = 16, kPairTraceSteps = 64;
-__device__ long long g_pair_trace[2][kPairTraceEvents][kPairTraceSteps];
-__shared__ long long s_ptrace_clock0;
-#define KEA_PTRACE(cond, ev, i)                                                                                   \
-    do {                                                                                                          \
-        if ((cond) && blockIdx.x < 2 && (i) < kPairTraceSteps)                                                    \
-            g_pair_trace[blockIdx.x][ev][i] = clock64() - s_ptrace_clock0;                                        \
-    } while (0)
-#else
-#define KEA_PTRACE(cond, ev, i) do { } while (0)
-#endif
 
 // INT32 -> FP32 for |a| < 2^22 (|acc| <= 127 K with K <= 32768 here): exact, so equal to cvt.rn.f32.s32, in two
 // full-rate operations. 0x4B400000 is the bit pattern of 1.5 * 2^23, whose mantissa holds a + 2^22 exactly.
@@ -233,10 +219,8 @@ KEA_DEVI void pair_epilogue_tile(const PairArgs &a, const CUtensorMap *ymap, uin
 #pragma unroll
     for (int ci = 0; ci < 4; ci += 2) {
         // chunk ci in va; chunk ci + 1 into vb while va is finished
-        KEA_PTRACE(tr, 10, j * 4 + ci);
         tmem_wait_ld();
         tmem_regs_ready(va);
-        KEA_PTRACE(tr, 11, j * 4 + ci);
         pair_load32(cbase + (uint32_t)(32 * (ci + 1)), vb);
         if (a.acc && t < a.M) {
             int4 *dst = reinterpret_cast<int4 *>(a.acc + (long long)t * a.ld_acc + nbase + 32 * ci);
@@ -246,9 +230,7 @@ KEA_DEVI void pair_epilogue_tile(const PairArgs &a, const CUtensorMap *ymap, uin
         pair_finish_chunk<F16, BIAS, SILU>(va, s_al, s_bi, 32 * ci, sq);
         if constexpr (!F16)
             if (a.res && t < a.M) pair_add_residual(va, a.res + (long long)t * a.ld_res + nbase + 32 * ci, a.res_scale);
-        KEA_PTRACE(tr, 12, j * 4 + ci);
         pair_stage_and_store<F16>(ymap, va, stg, ci, nbase + 32 * ci, trow0);
-        KEA_PTRACE(tr, 13, j * 4 + ci);
         // chunk ci + 1 in vb; chunk ci + 2 into va
         tmem_wait_ld();
         tmem_regs_ready(vb);
@@ -373,14 +355,6 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
     const uint32_t STG0 = (PK0 + (uint32_t)S * PKB + 1023u) & ~1023u;
     const int kbt = a.kb_total;
 
-#ifdef KEA_TRACE
-    if (threadIdx.x == 0) {
-        s_ptrace_clock0 = clock64();
-        long long gt;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt));
-        if (blockIdx.x < 2) g_pair_trace[blockIdx.x][7][0] = gt;
-    }
-#endif
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&bar_full[s]), 1);
@@ -407,7 +381,6 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
     cluster_sync_all();      // barrier initialisation and both CTAs' allocations are visible to the pair
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
-    KEA_PTRACE(threadIdx.x == 0, 7, 1);
 
     // With programmatic dependent launch, everything below may read what the previous kernel wrote.
     if (a.pdl) grid_dependency_wait();
@@ -431,7 +404,6 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                         ok = false;
                         break;
                     }
-                    KEA_PTRACE(true, 0, issued);
                     const uint32_t full = smem_u32(&bar_full[s]);
                     mbar_arrive_expect_tx(full, tx);
 #pragma unroll
@@ -480,7 +452,6 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                         ok = false;
                         break;
                     }
-                    KEA_PTRACE(lane == 0, 3, step);
                     const uint64_t ad = ad0 + (uint64_t)(((uint32_t)sa * ASLOT) >> 4);
                     const uint64_t bd = bd0 + (uint64_t)(((uint32_t)sb * kPairHalfTile) >> 4);
                     if (elect_one()) {
@@ -495,7 +466,6 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                         mma_commit_pair(smem_u32(&bar_bempty[sb]), (uint16_t)3);
                     }
                     __syncwarp();
-                    KEA_PTRACE(lane == 0, 4, step);
                 }
                 if (!ok) break;
                 if (elect_one()) mma_commit_pair(smem_u32(&bar_acc_full[buf]), (uint16_t)3);
@@ -537,14 +507,12 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                 if (lane == 0) report(a.err, 1u);
                 break;
             }
-            KEA_PTRACE(e == 0, 1, step);
             const uint32_t spk = PK0 + (uint32_t)sa * PKB, sbt = B0 + (uint32_t)sb * kPairHalfTile;
 #pragma unroll
             for (int u = e; u < units; u += kPairExpGroupWarps * 32) expand_unit<WBITS>(spk, sbt, 7, u);
             fence_async_shared();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(ready0 + (uint32_t)sb * 8u);
-            KEA_PTRACE(e == 0, 2, step);
         }
     } else {
         // ---------------- epilogue (warps 8-15) ----------------
@@ -586,7 +554,6 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                 break;
             }
             tc_fence_after();
-            KEA_PTRACE(ew == 0 && lane == 0, 5, j);
             const float sq = t < a.M ? __ldg(a.qs + t) : 0.f;
             const float sq1 = (P > 1 && t < a.M) ? __ldg(a.qs + a.qs_stride + t) : 0.f;
             const uint32_t cbase = lane_base + (uint32_t)buf * kPairAccCols + (uint32_t)(half * 128);
@@ -614,7 +581,6 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                 default: KEA_PAIR_EPI(true, true, true); break;
             }
 #undef KEA_PAIR_EPI
-            KEA_PTRACE(ew == 0 && lane == 0, 6, j);
         }
         // The staging buffers must outlive the stores' reads of them; the global writes complete with the grid.
         if (lane == 0) bulk_wait_group_read0();
@@ -630,7 +596,6 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
         tc_fence_after();
         tmem_dealloc_pair(tmem, kPairTmemCols);
     }
-    KEA_PTRACE(threadIdx.x == 0, 7, 2);
 }
 
 // Split-K finish: y[t, n .. n + 3] from the sum over K slices of the pair kernel's INT32 partials

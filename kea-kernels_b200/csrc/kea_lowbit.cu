@@ -1384,19 +1384,6 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     return KEA_OK;
 }
 
-#ifdef KEA_TRACE
-// Trace builds only: copy out / clear the phase timestamps (kTraceCtas x kTracePhases uint64).
-int kea_trace_read(unsigned long long *out) {
-    return cudaMemcpyFromSymbol(out, kea::g_trace, sizeof(kea::g_trace)) == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
-}
-int kea_pair_trace_read(long long *out) {
-    return cudaMemcpyFromSymbol(out, kea::g_pair_trace, sizeof(kea::g_pair_trace)) == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
-}
-int kea_trace_clear(void) {
-    static unsigned long long zeros[kea::kTraceCtas * kea::kTracePhases];
-    return cudaMemcpyToSymbol(kea::g_trace, zeros, sizeof(zeros)) == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
-}
-#endif
 
 int kea_lowbit_read_error(uint32_t *out) {
     if (!out) return KEA_ERR_INVALID_VALUE;

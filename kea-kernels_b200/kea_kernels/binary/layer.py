@@ -60,52 +60,46 @@ class Int8MmaLayer:
         return api.resident_bytes(self.panels, self.scale, self.bias)
 
     # --- calls ------------------------------------------------------------------------------------
+    # Where each entry point keeps the K features: the last axis of a token-major input, or axis 1 of [B, K, T].
+    _FEATURE_AXIS = {"linear": (-1, "[..., {k}]"), "conv": (1, "[B, {k}, T]")}
+
     def _check(self, x: Tensor, kind: str) -> None:
+        """Checks every entry point makes (the reference layer's messages): an FP32 tensor on this layer's device
+        with its features where `kind` puts them, and no autograd."""
+        axis, form = self._FEATURE_AXIS[kind]
         if not isinstance(x, Tensor):
-            raise ValueError("input must be a tensor")
-        if x.dtype != torch.float32:
-            raise ValueError(f"expected FP32 input, got {x.dtype}")
-        if x.device != self.device:
-            raise ValueError(f"input on {x.device}, layer on {self.device}")
-        if kind == "linear" and (x.dim() < 1 or x.shape[-1] != self.in_features):
-            raise ValueError(f"expected [..., {self.in_features}] input, got {tuple(x.shape)}")
-        if kind == "conv" and (x.dim() != 3 or x.shape[1] != self.in_features):
-            raise ValueError(f"expected [B, {self.in_features}, T] input, got {tuple(x.shape)}")
-        if torch.is_grad_enabled() and x.requires_grad:
-            raise RuntimeError("Int8MmaLayer is inference only: input requires grad")
+            problem = ValueError("input must be a tensor")
+        elif x.dtype != torch.float32:
+            problem = ValueError(f"expected FP32 input, got {x.dtype}")
+        elif x.device != self.device:
+            problem = ValueError(f"input on {x.device}, layer on {self.device}")
+        elif x.dim() < 1 or (kind == "conv" and x.dim() != 3) or x.shape[axis] != self.in_features:
+            problem = ValueError(f"expected {form.format(k=self.in_features)} input, got {tuple(x.shape)}")
+        elif torch.is_grad_enabled() and x.requires_grad:
+            problem = RuntimeError("Int8MmaLayer is inference only: input requires grad")
+        else:
+            return
+        raise problem
 
     def linear(self, x: Tensor) -> Tensor:
         self._check(x, "linear")
-        lead = tuple(x.shape[:-1])
-        m = math.prod(lead)
-        if m == 0:
-            return torch.empty(*lead, self.out_features, device=self.device, dtype=torch.float32)
-        if x.dim() == 1:
-            rows = (0, 0, x.stride(0), 1)
-        elif x.dim() == 2:
-            rows = (0, x.stride(0), x.stride(1), m)
-        else:
-            if x.dim() > 3:
-                try:
-                    x = x.view(-1, x.shape[-2], x.shape[-1])
-                except RuntimeError:
-                    x = x.reshape(-1, x.shape[-2], x.shape[-1])
-            rows = (x.stride(0), x.stride(1), x.stride(2), x.shape[1])
-        y = torch.empty(m, self.out_features, device=self.device, dtype=torch.float32)
-        self._run(x, rows, m, y)
-        return y.view(*lead, self.out_features)
+        return self._token_rows_product(x).view(*x.shape[:-1], self.out_features)
 
     def conv(self, x: Tensor) -> Tensor:
         self._check(x, "conv")
         b, _, t = x.shape
-        y = torch.empty(b, t, self.out_features, device=self.device, dtype=torch.float32)
-        if b * t:
-            self._run(x, (x.stride(0), x.stride(2), x.stride(1), t), b * t, y.view(b * t, self.out_features))
-        return y.transpose(1, 2)
+        # [B, K, T] read through its transposed view: the token rows are its T positions
+        return self._token_rows_product(x.transpose(1, 2)).view(b, t, self.out_features).transpose(1, 2)
 
-    def _run(self, x: Tensor, rows: tuple, m: int, y: Tensor) -> None:
-        q, qs, ldq = quantize(x, rows, m, self.in_features)
-        self.dot(q, qs, ldq, m, y)
+    def _token_rows_product(self, xt: Tensor) -> Tensor:
+        """xt [..., K] -> FP32 [rows, N]: its token rows quantized into the layer's PARTS residual INT8 parts, then
+        the GEMM."""
+        y = torch.empty(math.prod(xt.shape[:-1]), self.out_features, device=self.device, dtype=torch.float32)
+        if y.shape[0]:
+            rows, layout = token_rows(xt)
+            q, qs, ldq = quantize(rows, layout, y.shape[0], self.in_features, self.PARTS)
+            self.dot(q, qs, ldq, y.shape[0], y)
+        return y
 
     def dot(self, q: Tensor, qs: Tensor, ldq: int, m: int, y: Tensor, *, silu: bool = False,
             config: configs.DotConfig | None = None, order: int = 0, acc: Tensor | None = None) -> None:
@@ -144,6 +138,14 @@ def _project(layer, x: Tensor, *, conv: bool, parts: int, activation: str, norm,
     if conv:
         return y.transpose(1, 2)
     return y if x.dim() == 3 else y.view(*x.shape[:-1], n)
+
+
+def token_rows(x: Tensor) -> tuple[Tensor, tuple[int, int, int, int]]:
+    """x [..., K] (at least one token) -> (x3 [B, T, K], (XB, XT, XK, T)): the quantizer's addressing of x's token
+    rows, row r at (r // T) * XB + (r % T) * XT. The leading dimensions fold into B with reshape, which copies only
+    when their strides cannot be merged."""
+    x3 = x.reshape(1, 1, x.shape[0]) if x.dim() == 1 else x.reshape(-1, x.shape[-2], x.shape[-1])
+    return x3, (x3.stride(0), x3.stride(1), x3.stride(2), x3.shape[1])
 
 
 def quantize(x: Tensor, rows: tuple, m: int, k: int, parts: int = 3) -> tuple[Tensor, Tensor, int]:

@@ -16,7 +16,7 @@ from torch import Tensor
 
 from kea_kernels import lowbit
 from kea_kernels.binary import configs
-from kea_kernels.binary.layer import Int8MmaLayer, _project, dot, quantize
+from kea_kernels.binary.layer import Int8MmaLayer, _project, dot
 
 
 def _round_up(v: int, m: int) -> int:
@@ -49,10 +49,6 @@ class Int8MmaPartsLayer(Int8MmaLayer):
             raise ValueError(f"components must be 1, 2 or 3, got {components!r}")
         return _project(self, x, conv=conv, parts=parts, activation=activation, norm=norm,
                         input_activation=input_activation)
-
-    def _run(self, x: Tensor, rows: tuple, m: int, y: Tensor) -> None:
-        q, qs, ldq = quantize(x, rows, m, self.in_features, self.PARTS)
-        self.dot(q, qs, ldq, m, y, parts=self.PARTS)
 
 
 def _aligned(q: Tensor, k: int) -> tuple[Tensor, int]:

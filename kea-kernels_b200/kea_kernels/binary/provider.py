@@ -19,61 +19,71 @@ construction from an export (NeMo) is not part of this package.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+import bisect
+from typing import NamedTuple
 
 import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
 
-@dataclass
-class Entry:
-    """One prepared 1-bit layer and the global handle range of its rows."""
+class LayerRows(NamedTuple):
+    """A prepared layer registered in a Table: its rows hold the global row ids first .. first + rows - 1."""
     name: str
     layer: object
     kind: str            # "linear" or "conv"
-    out_features: int
-    in_features: int
-    start: int           # first global row id
-    members: tuple = ()  # for a fused entry (e.g. QKV): the module names
+    first: int
+    rows: int            # output features
+    cols: int            # input features
+    members: tuple = ()  # a fused layer's module names (e.g. Q, K, V)
 
 
-@dataclass
 class Table:
-    entries: list[Entry] = field(default_factory=list)
-    next_row: int = 0
+    """Global row ids -> prepared layers. Each added layer takes the next block of ids; a handle's first id is looked
+    up by bisection over the blocks' first ids (they are added in increasing order)."""
 
-    def add(self, name, layer, kind, n, k, members=()) -> Entry:
-        entry = Entry(name, layer, kind, n, k, self.next_row, tuple(members))
-        self.entries.append(entry)
-        self.next_row += n
-        return entry
+    def __init__(self):
+        self._firsts: list[int] = []
+        self._layers: list[LayerRows] = []
 
-    def resolve(self, start: int, count: int) -> tuple[Entry, int]:
-        for entry in self.entries:
-            if entry.start <= start < entry.start + entry.out_features:
-                if start + count > entry.start + entry.out_features:
-                    raise ValueError("handle range crosses layers")
-                return entry, start - entry.start
-        raise KeyError(f"no layer owns row handle {start}")
+    @property
+    def entries(self) -> list[LayerRows]:
+        return list(self._layers)
+
+    def add(self, name, layer, kind, n, k, members=()) -> LayerRows:
+        first = self._firsts[-1] + self._layers[-1].rows if self._layers else 0
+        rec = LayerRows(name, layer, kind, first, n, k, tuple(members))
+        self._firsts.append(first)
+        self._layers.append(rec)
+        return rec
+
+    def resolve(self, start: int, count: int) -> tuple[LayerRows, int]:
+        """(layer, row offset inside it) of the handle rows start .. start + count - 1, all in one layer."""
+        i = bisect.bisect_right(self._firsts, start) - 1
+        rec = self._layers[i] if i >= 0 else None
+        if rec is None or start >= rec.first + rec.rows:
+            raise KeyError(f"no layer owns row handle {start}")
+        if start + count > rec.first + rec.rows:
+            raise ValueError("handle range crosses layers")
+        return rec, start - rec.first
 
     def weight_bytes(self) -> int:
-        return sum(e.layer.weight_bytes() for e in self.entries)
+        return sum(rec.layer.weight_bytes() for rec in self._layers)
 
 
 def handle(start: int, n: int) -> Tensor:
-    """The CPU row handle of rows [start, start + n) of a Table."""
-    return torch.arange(start, start + n, dtype=torch.int64).view(1, n)
+    """The CPU int64 row handle [1, n] (a module's `packed_t`) of global rows start .. start + n - 1."""
+    return torch.arange(start, start + n, dtype=torch.int64)[None, :]
 
 
 class BinaryLinear(nn.Module):
     """A module standing for rows [offset, offset + n) of a Table entry (a whole layer or a fused member)."""
 
-    def __init__(self, entry: Entry, offset: int, n: int, k: int, scale_cpu: Tensor, bias_cpu: Tensor | None):
+    def __init__(self, entry: LayerRows, offset: int, n: int, k: int, scale_cpu: Tensor, bias_cpu: Tensor | None):
         super().__init__()
         self.in_features, self.out_features, self.mode = k, n, "binary"
         self._entry, self._offset = entry, offset
-        object.__setattr__(self, "packed_t", handle(entry.start + offset, n))
+        object.__setattr__(self, "packed_t", handle(entry.first + offset, n))
         object.__setattr__(self, "scale", scale_cpu.detach().clone().contiguous())
         object.__setattr__(self, "bias", None if bias_cpu is None else bias_cpu.detach().clone().contiguous())
         self.eval()
@@ -81,7 +91,7 @@ class BinaryLinear(nn.Module):
     def _run(self, x: Tensor, conv: bool) -> Tensor:
         e = self._entry
         y = e.layer.conv(x) if conv else e.layer.linear(x)
-        if self.out_features == e.out_features:
+        if self.out_features == e.rows:
             return y
         sl = slice(self._offset, self._offset + self.out_features)
         return y[:, sl] if conv else y[..., sl]
@@ -100,14 +110,14 @@ class BinaryProjection:
 
     def __init__(self, table: Table, names: dict[int, str] | None = None):
         self.table = table
-        self._resolved: dict[tuple, tuple[Entry, int, int]] = {}
+        self._resolved: dict[tuple, tuple[LayerRows, int, int]] = {}
         self.names = names or {}
 
     @property
     def bytes(self) -> int:
         return self.table.weight_bytes()
 
-    def _lookup(self, mod) -> tuple[Entry, int, int]:
+    def _lookup(self, mod) -> tuple[LayerRows, int, int]:
         h = mod.packed_t
         key = (h.data_ptr(), tuple(h.shape))
         hit = self._resolved.get(key)
@@ -143,7 +153,7 @@ class BinaryProjection:
                 y = F.silu(y)
             if conv:
                 y = y.transpose(1, 2)
-        if count != entry.out_features:
+        if count != entry.rows:
             y = y[:, offset:offset + count] if conv else y[..., offset:offset + count]
         return y
 

@@ -131,6 +131,31 @@ def int_acc(q: np.ndarray, w: np.ndarray) -> np.ndarray:
     return out.astype(np.int64).astype(np.int32)
 
 
+def int_acc_f32(q: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """The same exact INT32 [P, M, N] through FP32 BLAS (numpy's sgemm, every host thread): exact because each
+    product and every partial sum is an integer of magnitude <= 128 K < 2^24 (K <= 131072), which FP32 holds exactly in
+    any summation order. The strong CPU baseline of the reference's arithmetic."""
+    k = w.shape[1]
+    if k > 131072:
+        raise ValueError("FP32 accumulation is exact only for K <= 131072")
+    wt = np.ascontiguousarray(w.astype(np.float32).T)
+    out = np.stack([q[p, :, :k].astype(np.float32) @ wt for p in range(q.shape[0])])
+    return out.astype(np.int32)
+
+
+def gemm_blas(codes: np.ndarray, wbits: int, q: np.ndarray, qs: np.ndarray, alpha: np.ndarray) -> np.ndarray:
+    """The reference's CPU path for one part without bias - unpack the export codes, exact integer GEMM, the comb<1>
+    epilogue, FP16 output - as the strong CPU baseline: the GEMM in FP32 BLAS (exact, as int_acc_f32) and the epilogue
+    as two in-place FP32 multiplies (one IEEE rounding each, as epilogue_x1), both in PyTorch's multi-threaded CPU
+    kernels (torch.get_num_threads() threads). Returns y FP16 [M, N]."""
+    import torch
+    k = q.shape[2]
+    w = torch.from_numpy(unpack(codes, wbits, k)).to(torch.float32)
+    acc = torch.from_numpy(q[0, :, :k]).to(torch.float32) @ w.t()          # exact integers in FP32
+    acc.mul_(torch.from_numpy(qs[0]).to(torch.float32)[:, None]).mul_(torch.from_numpy(alpha).to(torch.float32)[None, :])
+    return acc.half().numpy()
+
+
 def gemm(q: np.ndarray, qs: np.ndarray, w: np.ndarray, alpha: np.ndarray, bias: np.ndarray | None = None,
          flags: int = 0, threads: int = 1) -> tuple[np.ndarray, np.ndarray]:
     """(y FP32 [M, N], acc INT32 [P, M, N]) from q int8 [P, M, ldq], qs FP32 [P, M], w int8 [N, K]."""

@@ -14,6 +14,9 @@ for path in (ROOT / "kea-kernels_b200", ROOT / "oracle"):
         sys.path.insert(0, str(path))
 
 GOLDEN = ROOT / "tests" / "golden" / "golden.npz"
+GOLDEN_CONFIG = ROOT / "tests" / "golden" / "golden_config.npz"
+if str(ROOT / "tests" / "golden") not in sys.path:
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
 
 
 def sm100() -> bool:
@@ -37,6 +40,17 @@ def pytest_collection_modifyitems(config, items):
 def golden():
     with np.load(GOLDEN) as data:
         return {k: data[k] for k in data.files}
+
+
+@pytest.fixture(scope="session")
+def golden_config():
+    with np.load(GOLDEN_CONFIG) as data:
+        return {k: data[k] for k in data.files}
+
+
+def sha256(a: np.ndarray) -> np.ndarray:
+    import hashlib
+    return np.frombuffer(hashlib.sha256(np.ascontiguousarray(a).tobytes()).digest(), dtype=np.uint8)
 
 
 def golden_cases(golden):

@@ -705,3 +705,30 @@ def test_pair_split_k_equals_oracle(wbits):
     y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias)
     want, want_acc = oracle.reference(q, qs, w, alpha, bias)
     _check(y, acc, want, want_acc, 0)
+
+
+# ---- config-size cases recorded from the reference (golden_config.npz) -------------------------------------------
+
+@pytest.mark.parametrize("name", ["config0_b1_n4096_k1024_m125", "config1_t2_n1024_k4096_m2048"])
+@pytest.mark.parametrize("route", ["table", "swap", "tile"])
+def test_gemm_equals_the_reference_at_config_size(golden_config, name, route):
+    """BASELINE config 0 (1-bit, M 125, N 4096, K 1024) and config 1's FF-down point (2-bit, M 2048, N 1024, K 4096):
+    the library's INT32 accumulators hash to the reference's own int64 accumulators (make_golden.py ran the
+    reference's pack / unpack and its test oracle on the same draw), and the FP16 / FP32 outputs equal the oracle's
+    epilogue of them bit for bit, within the reference test's tolerance of its FP64 outputs."""
+    from config_cases import CONFIG_CASES, SAMPLE_ROWS, draw
+    from conftest import sha256
+    _, wbits, n, k, m, parts = {c[0]: c for c in CONFIG_CASES}[name]
+    w, q, qs, alpha = (t.numpy() for t in draw(wbits, n, k, m, parts))
+    codes = oracle.pack_signs(w) if wbits == 1 else oracle.pack_ternary(w)
+    config = configs.DotConfig(0, 128, 0, 0, configs.SWAP) if route == "swap" else None
+    if route == "swap" and m > 256:
+        config = configs.DotConfig(0, 128, 4, 0, configs.SWAP)
+    for out in (torch.float16, torch.float32):
+        y, acc = _run(codes, wbits, n, k, q, qs, alpha, None, out=out, config=config, swap=route != "tile",
+                      pair=route != "tile")
+        assert np.array_equal(sha256(acc), golden_config[f"{name}/acc_sha256"]), "accumulators differ from the reference"
+        want = oracle.finish(acc, qs, alpha)
+        _check(y, acc, want, acc, 0)
+        np.testing.assert_allclose(y.double().numpy()[list(SAMPLE_ROWS)], golden_config[f"{name}/y64_rows"],
+                                   rtol=2e-6 if out == torch.float32 else 1e-3, atol=1e-6 if out == torch.float32 else 1e-4)
