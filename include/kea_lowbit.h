@@ -58,9 +58,11 @@ enum {
     KEA_FLAG_FORCE_SWAP = 32,   /* the small-M swapped-operand kernel (weights on the MMA's M axis, tokens on N) at any
                                    shape; `splits` / `stages` (0: the table's) then apply to it, tile_m / tile_n must be 0 */
     KEA_FLAG_NO_SWAP = 64,      /* keep the table off the swapped-operand kernel (128-token tiles run instead) */
-    KEA_FLAG_TEST_STALL = 128   /* tests only, with KEA_FLAG_FORCE_SWAP: the kernel's producer issues no activation
+    KEA_FLAG_TEST_STALL = 128,  /* tests only, with KEA_FLAG_FORCE_SWAP: the kernel's producer issues no activation
                                    copy, so its MMA warp's bounded wait runs out (see wait_clocks), the kernel reports
                                    KEA_DEVERR_TIMEOUT and returns; the output is left undefined */
+    KEA_FLAG_NO_RESIDENT_WEIGHTS = 256   /* the pair kernel re-expands the weights of every tile it visits, also where
+                                            (one part, K <= 1024) it would keep a channel tile's weights resident */
 };
 
 /* Device error word bits (written by kernels into `error_word`, or into the library's own device word). */
@@ -151,8 +153,9 @@ int kea_lowbit_gemm(const KeaGemmDesc *desc, void *stream);
  * every GPU that loads the library until the process exits; desc->workspace / workspace_bytes are ignored.
  * The caller still passes every input and output. A shape whose split would need more scratch is refused with
  * KEA_ERR_SCRATCH_LIMIT (kea_lowbit_workspace_bytes says how much a shape needs); shapes that do not split need none.
- * The first call on a device looks up the buffer's device address (once per device): make that call before any
- * stream capture. All calls on a device share its one buffer, which keeps the last call's contents (nothing in it needs
+ * The buffer's device address is looked up in the one-time set-up of each device, which the first call of any entry
+ * point on that device runs (this one included): make that first call before any stream capture (inside one it
+ * returns KEA_ERR_CAPTURE). All calls on a device share its one buffer, which keeps the last call's contents (nothing in it needs
  * to start at zero: each call writes every partial sum it later reads), so calls on that device that overlap on the
  * GPU (for example on two streams) race: keep them on one stream or order them with events. */
 #define KEA_NOALLOC_SCRATCH_BYTES (16u << 20)

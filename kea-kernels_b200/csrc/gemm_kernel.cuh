@@ -122,14 +122,17 @@ KEA_DEVI void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, u
 // c = u / tile_n (word c % 4 of sub-block c / 4). A chunk is 16 codes = 16 bytes of the B tile, stored at chunk
 // position c ^ (r & 7) of row r (128-byte swizzle). tn_log2 = log2(tile_n).
 template <int WBITS>
-KEA_DEVI void expand_unit(uint32_t pk, uint32_t dst, int tn_log2, int u) {
-    // tile_n and R are powers of two: shifts and masks, never integer division, on this hot path
+KEA_DEVI uint32_t unit_word_addr(uint32_t pk, int tn_log2, int u) {
     const int r_log2 = tn_log2 < 7 ? tn_log2 : 7;          // R = min(tile_n, 128)
     const int r = u & ((1 << tn_log2) - 1), q = u >> tn_log2;
     const int pt = r >> r_log2, rr = r & ((1 << r_log2) - 1);
+    return pk + ((uint32_t)((((pt * (4 * WBITS) + q) << r_log2) | rr)) << 2);
+}
+template <int WBITS>
+KEA_DEVI void expand_word(uint32_t w, uint32_t dst, int tn_log2, int u) {
+    const int r = u & ((1 << tn_log2) - 1), q = u >> tn_log2;
     const uint32_t rowbase = dst + (uint32_t)r * 128;
     const uint32_t sw = (uint32_t)(r & 7);
-    const uint32_t w = ld_shared_u32(pk + ((uint32_t)((((pt * (4 * WBITS) + q) << r_log2) | rr)) << 2));
     if constexpr (WBITS == 1) {   // (w >> j) & 0x11111111: codes 8 j .. 8 j + 7, one per nibble
         const uint32_t s0 = w & 0x11111111u, s1 = (w >> 1) & 0x11111111u;
         const uint32_t s2 = (w >> 2) & 0x11111111u, s3 = (w >> 3) & 0x11111111u;
@@ -141,6 +144,27 @@ KEA_DEVI void expand_unit(uint32_t pk, uint32_t dst, int tn_log2, int u) {
         const uint32_t lo = w & 0x33333333u, hi = (w >> 2) & 0x33333333u;
         st_shared_v4(rowbase + (((uint32_t)q ^ sw) << 4), lookup4(kTernaryTable, lo), lookup4(kTernaryTable, lo >> 16),
                      lookup4(kTernaryTable, hi), lookup4(kTernaryTable, hi >> 16));
+    }
+}
+template <int WBITS>
+KEA_DEVI void expand_unit(uint32_t pk, uint32_t dst, int tn_log2, int u) {
+    expand_word<WBITS>(ld_shared_u32(unit_word_addr<WBITS>(pk, tn_log2, u)), dst, tn_log2, u);
+}
+// Units u0, u0 + stride, ... (< units) of one stage, at most MAXU of them: every word is loaded first, then each is
+// expanded, so the shared-memory loads and the expansion chains of different units overlap instead of running one
+// dependent chain after another.
+template <int WBITS, int MAXU>
+KEA_DEVI void expand_units(uint32_t pk, uint32_t dst, int tn_log2, int u0, int stride, int units) {
+    uint32_t w[MAXU];
+#pragma unroll
+    for (int i = 0; i < MAXU; ++i) {
+        const int u = u0 + i * stride;
+        w[i] = u < units ? ld_shared_u32(unit_word_addr<WBITS>(pk, tn_log2, u)) : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < MAXU; ++i) {
+        const int u = u0 + i * stride;
+        if (u < units) expand_word<WBITS>(w[i], dst, tn_log2, u);
     }
 }
 

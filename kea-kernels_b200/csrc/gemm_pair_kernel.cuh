@@ -61,6 +61,7 @@ struct PairArgs {
     long long ld_acc, acc_stride;
     int M, N, K, kb_total;
     int n_tiles, tiles;          // 256-channel tiles, pair tiles in all
+    int m_tiles;                 // 256-token tiles (the weight-stationary kernel's tile order is channel-tile-major)
     int splits, kbs, items;      // K slices per tile, k-blocks per slice, work items = tiles x splits
     int *ws;                     // splits > 1: INT32 partial sums [splits][P][M][N] (scratch), finished by
                                  // splitk_finish_kernel; null otherwise
@@ -508,8 +509,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                 break;
             }
             const uint32_t spk = PK0 + (uint32_t)sa * PKB, sbt = B0 + (uint32_t)sb * kPairHalfTile;
-#pragma unroll
-            for (int u = e; u < units; u += kPairExpGroupWarps * 32) expand_unit<WBITS>(spk, sbt, 7, u);
+            constexpr int kGroupThreads = kPairExpGroupWarps * 32;
+            expand_units<WBITS, (units + kGroupThreads - 1) / kGroupThreads>(spk, sbt, 7, e, kGroupThreads, units);
             fence_async_shared();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(ready0 + (uint32_t)sb * 8u);

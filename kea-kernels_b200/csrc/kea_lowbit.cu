@@ -11,6 +11,7 @@
 #include "kea_lowbit.h"
 #include "gemm_kernel.cuh"
 #include "gemm_pair_kernel.cuh"
+#include "gemm_pair_ws_kernel.cuh"
 #include "gemm_swap_kernel.cuh"
 #include "gemv_kernel.cuh"
 #include "conv_kernels.cuh"
@@ -101,6 +102,11 @@ int device_setup(int *device_out, void *stream, bool check_capture = true) {
                                        (const void *)kea::lowbit_gemm_pair_kernel<1, 2>,
                                        (const void *)kea::lowbit_gemm_pair_kernel<2, 2>};
         for (const void *k : pair_kernels)
+            if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairMaxDynSmem) != cudaSuccess)
+                status = KEA_ERR_CUDA;
+        const void *ws_kernels[2] = {(const void *)kea::lowbit_gemm_pair_ws_kernel<1>,
+                                     (const void *)kea::lowbit_gemm_pair_ws_kernel<2>};
+        for (const void *k : ws_kernels)
             if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairMaxDynSmem) != cudaSuccess)
                 status = KEA_ERR_CUDA;
         const void *swap_kernels[6] = {
@@ -246,6 +252,18 @@ int pair_splits(int m, int n, int k, int sms) {
 size_t pair_workspace_bytes(int m, int n, int k, int parts, int sms) {
     const int s = pair_splits(m, n, k, sms);
     return s > 1 ? (size_t)s * (size_t)parts * (size_t)m * (size_t)n * 4u : 0u;
+}
+
+// The weight-stationary pair kernel (gemm_pair_ws_kernel.cuh): one part, K <= 1024, every k-block's expanded weights
+// resident: [3 activation slots][kb x 16 KB weights][2 code slots][staging][channel constants].
+int pair_ws_smem_bytes(int wbits, int kb) {
+    const int stg = round_up(kea::kWsStages * (int)kea::kPairHalfTile + kb * (int)kea::kPairHalfTile +
+                             2 * wbits * kea::kPanelSubBytes, 1024);
+    return 1024 + stg + (int)kea::kPairStagingBytes + (int)kea::kPairChannelBytes;
+}
+bool pair_ws_fits(int k, int parts, int wbits) {
+    const int kb = ceil_div(k, kea::kBK);
+    return parts == 1 && kb <= kea::kWsMaxKb && pair_ws_smem_bytes(wbits, kb) <= kPairMaxDynSmem;
 }
 
 KeaGemmConfig pair_config(int wbits, int parts) {
@@ -620,7 +638,8 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
     a.K = d->k;
     a.kb_total = ceil_div(d->k, kea::kBK);
     a.n_tiles = d->n / kea::kPairTileN;
-    a.tiles = a.n_tiles * ceil_div(d->m, kea::kPairTileM);
+    a.m_tiles = ceil_div(d->m, kea::kPairTileM);
+    a.tiles = a.n_tiles * a.m_tiles;
     a.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
     a.res = d->residual;
     a.ld_res = d->ld_residual;
@@ -643,11 +662,13 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
         a.res = nullptr;
     }
     const int pairs = std::min(a.items, std::max(1, sms / 2));
+    // Weight-stationary (one part, K <= 1024, unsplit): runs of tiles keep a channel tile's expanded weights.
+    const bool ws = !split && !(d->flags & KEA_FLAG_NO_RESIDENT_WEIGHTS) && pair_ws_fits(d->k, d->parts, d->wbits);
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
     cfg.blockDim = dim3(kea::kPairThreads, 1, 1);
-    cfg.dynamicSmemBytes = (size_t)c.smem_bytes;
+    cfg.dynamicSmemBytes = (size_t)(ws ? pair_ws_smem_bytes(d->wbits, a.kb_total) : c.smem_bytes);
     cfg.stream = (cudaStream_t)stream;
     cudaLaunchAttribute attrs[2];
     unsigned na = 0;
@@ -664,7 +685,10 @@ int launch_pair(const KeaGemmDesc *d, const KeaGemmConfig &c, int sms, void *str
     cfg.attrs = attrs;
     cfg.numAttrs = na;
     cudaError_t e;
-    switch (d->wbits * 4 + d->parts) {
+    if (ws)
+        e = d->wbits == 1 ? cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_ws_kernel<1>, qmap, ymap, a)
+                          : cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_ws_kernel<2>, qmap, ymap, a);
+    else switch (d->wbits * 4 + d->parts) {
         case 5: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<1, 1>, qmap, ymap, a); break;
         case 6: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<1, 2>, qmap, ymap, a); break;
         case 9: e = cudaLaunchKernelEx(&cfg, kea::lowbit_gemm_pair_kernel<2, 1>, qmap, ymap, a); break;
@@ -726,7 +750,7 @@ int validate_gemm(const KeaGemmDesc *d) {
     if (!aligned16(d->q) || d->ldq % 16 || !aligned16(d->panels)) return KEA_ERR_ALIGNMENT;
     if (d->parts > 1 && (d->q_part_stride % 16 || d->q_part_stride < (int64_t)d->m * d->ldq)) return KEA_ERR_ALIGNMENT;
     if (d->flags & ~(KEA_FLAG_SILU | KEA_FLAG_ORDER1 | KEA_FLAG_PDL | KEA_FLAG_NO_PAIR | KEA_FLAG_FORCE_PAIR |
-                     KEA_FLAG_FORCE_SWAP | KEA_FLAG_NO_SWAP | KEA_FLAG_TEST_STALL))
+                     KEA_FLAG_FORCE_SWAP | KEA_FLAG_NO_SWAP | KEA_FLAG_TEST_STALL | KEA_FLAG_NO_RESIDENT_WEIGHTS))
         return KEA_ERR_INVALID_VALUE;
     if ((d->flags & KEA_FLAG_NO_PAIR) && (d->flags & KEA_FLAG_FORCE_PAIR)) return KEA_ERR_INVALID_VALUE;
     if ((d->flags & KEA_FLAG_FORCE_SWAP) &&

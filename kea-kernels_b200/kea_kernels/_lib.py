@@ -18,7 +18,7 @@ LIB_PATH = Path(os.environ.get("KEA_LOWBIT_LIB", Path(__file__).resolve().parent
 OK, INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES, CUDA, NO_DEVICE, DEVICE_TIMEOUT, CAPTURE, SCRATCH_LIMIT = range(10)
 OUT_F32, OUT_F16 = 0, 1
 FLAG_SILU, FLAG_ORDER1, FLAG_PDL, FLAG_NO_PAIR, FLAG_FORCE_PAIR = 1, 2, 4, 8, 16
-FLAG_FORCE_SWAP, FLAG_NO_SWAP, FLAG_TEST_STALL = 32, 64, 128
+FLAG_FORCE_SWAP, FLAG_NO_SWAP, FLAG_TEST_STALL, FLAG_NO_RESIDENT_WEIGHTS = 32, 64, 128, 256
 QUANT_INPUT_SILU, QUANT_PDL = 1, 2
 DEVERR_TIMEOUT, DEVERR_TAIL_BITS, DEVERR_TERNARY_11 = 1, 2, 4
 

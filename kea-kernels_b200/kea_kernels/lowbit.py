@@ -81,7 +81,8 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
          bias: Tensor | None, y: Tensor, *, parts: int, silu: bool = False, order: int = 0, acc: Tensor | None = None,
          config=None, pdl: bool = False, error_word: Tensor | None = None, pair: bool = True,
          force_pair: bool = False, residual: Tensor | None = None, residual_scale: float = 1.0,
-         workspace: Tensor | None = None, swap: bool = True, wait_clocks: int = 0, test_stall: bool = False) -> None:
+         workspace: Tensor | None = None, swap: bool = True, wait_clocks: int = 0, test_stall: bool = False,
+         resident_weights: bool = True) -> None:
     """y[:m] (row stride y.stride(0); FP32 or FP16) from q int8 [parts, m, ldq] and qs FP32 [parts, m].
     acc, when given, receives the exact INT32 accumulators as int32 [parts, m, n] (any row / part strides).
     `config` forces the per-tile kernel's tiles, or (tile_m <= 16, m <= 16) the CUDA-core kernel's channels per CTA;
@@ -93,7 +94,8 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
     shape splits; a caller's uint8 CUDA tensor is used as given (an empty one runs the GEMM unsplit). swap=False keeps
     the table away from the small-M swapped-operand kernel; a SWAP config (kernel == 3) forces it with its splits and
     stages. wait_clocks bounds each wait of the swap kernel (0: the library's default); test_stall (tests only, with a
-    forced SWAP config) makes the kernel withhold its activation copies so that a wait runs out."""
+    forced SWAP config) makes the kernel withhold its activation copies so that a wait runs out. resident_weights=False
+    keeps the pair kernel re-expanding every tile's weights where it would keep them resident (one part, K <= 1024)."""
     if m == 0:
         return
     if parts not in (1, 2, 3):
@@ -137,7 +139,8 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
     d.m = m
     d.flags = (_lib.FLAG_SILU if silu else 0) | (_lib.FLAG_ORDER1 if order else 0) | (_lib.FLAG_PDL if pdl else 0) \
         | (0 if pair else _lib.FLAG_NO_PAIR) | (_lib.FLAG_FORCE_PAIR if force_pair else 0) \
-        | (0 if swap else _lib.FLAG_NO_SWAP) | (_lib.FLAG_TEST_STALL if test_stall else 0)
+        | (0 if swap else _lib.FLAG_NO_SWAP) | (_lib.FLAG_TEST_STALL if test_stall else 0) \
+        | (0 if resident_weights else _lib.FLAG_NO_RESIDENT_WEIGHTS)
     kernel = getattr(config, "kernel", 0) if config is not None else None
     if kernel == 3:   # the swap kernel with this config's split and stages
         d.flags |= _lib.FLAG_FORCE_SWAP

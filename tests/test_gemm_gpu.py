@@ -732,3 +732,44 @@ def test_gemm_equals_the_reference_at_config_size(golden_config, name, route):
         _check(y, acc, want, acc, 0)
         np.testing.assert_allclose(y.double().numpy()[list(SAMPLE_ROWS)], golden_config[f"{name}/y64_rows"],
                                    rtol=2e-6 if out == torch.float32 else 1e-3, atol=1e-6 if out == torch.float32 else 1e-4)
+
+
+# ---- the weight-stationary pair kernel (one part, K <= 1024) ------------------------------------------------------
+
+@pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("n,k,m", [(4096, 1024, 8192), (4096, 1024, 2048), (256, 1024, 300), (1024, 1024, 1000),
+                                   (512, 640, 1500), (768, 136, 513), (2048, 384, 3000)])
+@pytest.mark.parametrize("flags,out,extras", [(0, torch.float16, False), (2, torch.float32, True),
+                                              (1, torch.float32, True)])
+def test_pair_resident_weights_equal_streamed_and_oracle(wbits, n, k, m, flags, out, extras):
+    """Runs of tiles that keep a channel tile's expanded weights resident (re-expanded when the run reaches the next
+    channel tile, odd k-block counts included) give the bits of the kernel that re-expands every tile, accumulators,
+    bias, SiLU and the residual included; and the oracle's (rows sampled at the largest M)."""
+    assert configs.choose(m, n, k, wbits, 1).kernel == configs.PAIR
+    seed = wbits * 5 + n + k + m + flags
+    codes, w = _codes(wbits, n, k, seed)
+    q, qs = _activations(1, m, k, seed)
+    alpha, bias = _channel(n, seed, extras)
+    panels = lowbit.prepare_panels(torch.from_numpy(codes).to(DEV), wbits, n, k)
+    qd, qsd = torch.from_numpy(q).to(DEV), torch.from_numpy(qs).to(DEV)
+    ad = torch.from_numpy(alpha).to(DEV)
+    bd = None if bias is None else torch.from_numpy(bias).to(DEV)
+    res = torch.randn(m, n, generator=torch.Generator().manual_seed(seed)).to(DEV) if extras else None
+    outs = []
+    for resident in (True, False):
+        y = torch.full((m, n), float("nan"), device=DEV, dtype=out)
+        acc = torch.full((1, m, n), -7, device=DEV, dtype=torch.int32)
+        lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, y, parts=1, silu=bool(flags & 1),
+                    order=(flags >> 1) & 1, acc=acc, residual=res, residual_scale=0.5, resident_weights=resident)
+        outs.append((y, acc))
+    torch.cuda.synchronize()
+    assert _lib.read_device_error() == 0
+    (y0, a0), (y1, a1) = outs
+    assert torch.equal(a0, a1)
+    view = torch.int16 if out == torch.float16 else torch.int32
+    assert torch.equal(y0.view(view), y1.view(view))
+    rows = np.unique(np.linspace(0, m - 1, 48).astype(int)) if m > 2048 else np.arange(m)
+    want, want_acc = oracle.reference(q[:, rows], qs[:, rows], w, alpha, bias, flags)
+    if res is not None:
+        want = (res.cpu().numpy()[rows] + np.float32(0.5) * want).astype(np.float32)
+    _check(y0.cpu()[rows], a0.cpu().numpy()[:, rows], want, want_acc, flags)
