@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define KEA_LOWBIT_VERSION 2
+#define KEA_LOWBIT_VERSION 3
 
 /* Status codes. The Python layer maps 1-4 to ValueError and 5-8 to RuntimeError, as the reference raises
  * ValueError for argument errors (src/kea_kernels/binary/layer.py:66-78,188-189) and RuntimeError for a failed
@@ -205,6 +205,15 @@ typedef struct KeaQuantizeDesc {
     const float *norm_bias;
     float eps;
     int32_t flags;            /* KEA_QUANT_* */
+    /* Optional LayerNorm applied before everything else - a layer's output norm, as the reference's row epilogue
+     * applies OUT_NORM before the next projection's quantizer (src/kea_kernels/ternary/row_fusion.py:27-52) - with
+     * its FP32 result written to normed[m][ld_normed] (the next skip connection's input). Needs unit-stride,
+     * 16-byte aligned rows (x, normed, both norms' parameters); normed may be x itself (in place). NULL: none. */
+    const float *pre_norm_weight;
+    const float *pre_norm_bias;  /* NULL: no bias */
+    float pre_eps;
+    float *normed;
+    int64_t ld_normed;        /* elements, a multiple of 4 */
 } KeaQuantizeDesc;
 
 enum {

@@ -84,6 +84,11 @@ struct QuantArgs {
     const float *nw, *nb;
     float eps;
     int flags;
+    // optional LayerNorm before everything else (a layer's output norm), its result written to `normed` [M][ldn]
+    const float *pnw, *pnb;
+    float peps;
+    float *normed;
+    long long ldn;
 };
 
 constexpr int kQuantThreads = 256;
@@ -139,6 +144,74 @@ KEA_DEVI uint32_t quantize4(const float *e, float s, float inv, float (&r)[4]) {
     return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
 }
 
+// group_reduce with a scratch slot of its own (kQuantThreads / 32 floats) per reduction of the kernel, so no
+// barrier is needed before the slot is written (no earlier reduction can still be reading it). Same order of
+// operations as group_reduce, so the same result bit for bit.
+KEA_DEVI float group_reduce_slot(float v, bool use_max, int tpr, float *slot) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float u = __shfl_xor_sync(0xFFFFFFFFu, v, o);
+        v = use_max ? fmaxf(v, u) : __fadd_rn(v, u);
+    }
+    if (tpr == 32) return v;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wpr = tpr >> 5;
+    if (lane == 0) slot[warp] = v;
+    __syncthreads();
+    const int w0 = warp - warp % wpr;
+    float r = slot[w0];
+    for (int w = 1; w < wpr; ++w) r = use_max ? fmaxf(r, slot[w0 + w]) : __fadd_rn(r, slot[w0 + w]);
+    return r;
+}
+
+// The affine parameters of a LayerNorm for the chunks a thread holds (zeros past K or without a bias): loaded before
+// the kernel waits for the previous grid, since they do not depend on it.
+template <int C>
+KEA_DEVI void load_affine(const float *nw, const float *nb, int K, int tpr, int gt, float4 (&w)[C], float4 (&b)[C]) {
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int i = c * tpr + gt;
+        const bool in = nw && 4 * i < K;
+        w[c] = in ? __ldg(reinterpret_cast<const float4 *>(nw) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        b[c] = in && nb ? __ldg(reinterpret_cast<const float4 *>(nb) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+// LayerNorm of the row group's K values held as float4 chunks at (c * tpr + gt) * 4 (layout of
+// quantize_regs_kernel): mean, then the centred variance (two group reductions in a fixed order, in scratch slots
+// `slots` and `slots` + kQuantThreads / 32), then (v - mean) * rsqrt(var + eps) * w + b chunk by chunk, with w / b
+// from `pw` / `pb` when PRE (loaded early by load_affine), else read here. Chunks past K stay as they are.
+template <int C, bool PRE>
+KEA_DEVI void layer_norm_regs(float4 (&v)[C], int K, int tpr, int gt, float *slots, const float *nw,
+                              const float *nb, float eps, const float4 (&pw)[C], const float4 (&pb)[C]) {
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < C; ++c) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[c].x), v[c].y), v[c].z), v[c].w);
+    const float mean = __fdiv_rn(group_reduce_slot(s, false, tpr, slots), (float)K);
+    float var = 0.f;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        if (4 * (c * tpr + gt) < K) {
+            const float d0 = __fsub_rn(v[c].x, mean), d1 = __fsub_rn(v[c].y, mean);
+            const float d2 = __fsub_rn(v[c].z, mean), d3 = __fsub_rn(v[c].w, mean);
+            var = __fmaf_rn(d3, d3, __fmaf_rn(d2, d2, __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, var))));
+        }
+    }
+    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(group_reduce_slot(var, false, tpr, slots + kQuantThreads / 32), (float)K), eps));
+    // the affine parameters are read here, chunk by chunk, not held for the whole row (registers)
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int i = c * tpr + gt;
+        if (4 * i < K) {
+            const float4 w = PRE ? pw[c] : __ldg(reinterpret_cast<const float4 *>(nw) + i);
+            const float4 b = PRE ? pb[c] : (nb ? __ldg(reinterpret_cast<const float4 *>(nb) + i) : make_float4(0.f, 0.f, 0.f, 0.f));
+            v[c].x = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].x, mean), inv), w.x, b.x);
+            v[c].y = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].y, mean), inv), w.y, b.y);
+            v[c].z = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].z, mean), inv), w.z, b.z);
+            v[c].w = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].w, mean), inv), w.w, b.w);
+        }
+    }
+}
+
 // The register-resident quantizer for unit-stride rows (xk == 1, K a multiple of 4, 16-byte aligned rows): `tpr`
 // threads per row (32 .. 256, 256 / tpr rows per CTA), each holding VPT = K / tpr (rounded up to 4) values as float4
 // chunks at (c * tpr + thread) * 4, so every load and store is a coalesced 16-byte vector. LayerNorm takes two
@@ -146,14 +219,23 @@ KEA_DEVI uint32_t quantize4(const float *e, float s, float inv, float (&r)[4]) {
 // the reductions' partials. This is the path of every encoder call site; other layouts take quantize_kernel.
 template <int VPT>
 __global__ void __launch_bounds__(kQuantThreads) quantize_regs_kernel(const QuantArgs a, int tpr) {
-    __shared__ float scratch[kQuantThreads / 32];
+    // one scratch slot per reduction: pre-norm mean / variance, norm mean / variance, one amax per part
+    constexpr int kSlot = kQuantThreads / 32;
+    __shared__ float scratch[7 * kSlot];
     constexpr int C = VPT / 4;
+    // up to 4 chunks a thread the LayerNorms' affine parameters are held in registers, loaded before the wait
+    constexpr bool PRE = C <= 4;
     const int rows = kQuantThreads / tpr;
     const int g = threadIdx.x / tpr, gt = threadIdx.x % tpr;
     const int m = blockIdx.x * rows + g;
     const bool live = m < a.M;
     const int K = a.K;
     float4 v[C];
+    float4 pw[C], pb[C], nw[C], nb[C];   // unused (and dropped by the compiler) unless PRE
+    if (PRE) {
+        load_affine<C>(a.pnw, a.pnb, K, tpr, gt, pw, pb);
+        load_affine<C>(a.nw, a.nb, K, tpr, gt, nw, nb);
+    }
     grid_dependency_wait();
     // the next kernel may launch now: it loads its static operands, then waits for this grid to complete
     grid_launch_dependents();
@@ -164,35 +246,19 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_regs_kernel(const Quan
         const int i = c * tpr + gt;
         v[c] = (live && 4 * i < K) ? __ldg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (a.nw) {
-        float s = 0.f;
+    if (a.pnw) {
+        layer_norm_regs<C, PRE>(v, K, tpr, gt, scratch, a.pnw, a.pnb, a.peps, pw, pb);
+        if (live) {
+            float4 *dst = reinterpret_cast<float4 *>(a.normed + (long long)m * a.ldn);
 #pragma unroll
-        for (int c = 0; c < C; ++c) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[c].x), v[c].y), v[c].z), v[c].w);
-        const float mean = __fdiv_rn(group_reduce(s, false, tpr, scratch), (float)K);
-        float var = 0.f;
-#pragma unroll
-        for (int c = 0; c < C; ++c) {
-            if (4 * (c * tpr + gt) < K) {
-                const float d0 = __fsub_rn(v[c].x, mean), d1 = __fsub_rn(v[c].y, mean);
-                const float d2 = __fsub_rn(v[c].z, mean), d3 = __fsub_rn(v[c].w, mean);
-                var = __fmaf_rn(d3, d3, __fmaf_rn(d2, d2, __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, var))));
-            }
-        }
-        const float inv = rsqrtf(__fadd_rn(__fdiv_rn(group_reduce(var, false, tpr, scratch), (float)K), a.eps));
-        // the affine parameters are read here, chunk by chunk, not held for the whole row (registers)
-#pragma unroll
-        for (int c = 0; c < C; ++c) {
-            const int i = c * tpr + gt;
-            if (4 * i < K) {
-                const float4 w = __ldg(reinterpret_cast<const float4 *>(a.nw) + i);
-                const float4 b = a.nb ? __ldg(reinterpret_cast<const float4 *>(a.nb) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-                v[c].x = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].x, mean), inv), w.x, b.x);
-                v[c].y = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].y, mean), inv), w.y, b.y);
-                v[c].z = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].z, mean), inv), w.z, b.z);
-                v[c].w = __fmaf_rn(__fmul_rn(__fsub_rn(v[c].w, mean), inv), w.w, b.w);
+            for (int c = 0; c < C; ++c) {
+                const int i = c * tpr + gt;
+                if (4 * i < K) dst[i] = v[c];
             }
         }
     }
+    if (a.nw)
+        layer_norm_regs<C, PRE>(v, K, tpr, gt, scratch + 2 * kSlot, a.nw, a.nb, a.eps, nw, nb);
     if (a.flags & 1) {
 #pragma unroll
         for (int c = 0; c < C; ++c) {
@@ -208,7 +274,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_regs_kernel(const Quan
         if (4 * (c * tpr + gt) < K)
             amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c].x), fabsf(v[c].y)), fmaxf(fabsf(v[c].z), fabsf(v[c].w))));
     for (int p = 0; p < a.parts; ++p) {
-        amax = group_reduce(amax, true, tpr, scratch);
+        amax = group_reduce_slot(amax, true, tpr, scratch + (4 + p) * kSlot);
         const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1.0e-30f);
         const float rcp = __frcp_rn(scale);
         float next = 0.f;   // the residual's amax: the next part's scale

@@ -470,15 +470,40 @@ bool gemv_fits(int m, int parts, int ch) {
     return m >= 1 && m <= kea::kGemvMaxM && kea::gemv_smem_bytes(m * parts, ch) <= kea::kGemvMaxSmem;
 }
 
+// One part on a narrow layer (512 < N <= 1024, K <= 4096: the measured range) just above the pair kernel's M threshold: its 256 x 256 tiles are too few
+// to fill the SMs (8-16 pairs of 74), and the per-tile kernel with 128-token tiles and K split over a cluster of up to
+// 4 fills them instead. Measured (B200, graph-timed cold, one part): N 1024, K 4096, M 300-512: 11.0-11.5 us
+// (128 x 128 tiles, 4 slices) against 16.0-16.5 for the pair kernel; M 768-1024: 15.3 against 18.8-19.1 (2 slices);
+// N 1024, K 1024, M 300-512: 6.3-6.8 (128 x 64 tiles, 2 slices) against 8.4-8.5. From M 768 at K 1024 and M 1536 at
+// K 4096 the pair kernel is as fast or faster.
+bool narrow_mid_m(int m, int n, int k, int parts) {
+    return parts == 1 && n > 512 && n <= 1024 && k <= 4096 && m >= kPairMinM && m <= (k >= 2048 ? 1024 : 512);
+}
+KeaGemmConfig narrow_mid_config(int m, int n, int k, int wbits, int sms) {
+    KeaGemmConfig c{};
+    const int kb = ceil_div(k, kea::kBK);
+    c.tile_m = kea::kBM;
+    c.tile_n = k >= 2048 ? 128 : 64;
+    const int tiles = ceil_div(m, kea::kBM) * ceil_div(n, c.tile_n);
+    int splits = 1;
+    while (splits < 4 && tiles * splits * 2 <= sms && splits * 2 <= kb) splits *= 2;
+    c.splits = splits;
+    c.stages = std::max(1, std::min({4, ceil_div(kb, splits), max_stages(c.tile_m, c.tile_n, 1, wbits)}));
+    c.smem_bytes = dyn_smem_bytes(c.tile_m, c.tile_n, 1, wbits, splits, c.stages);
+    c.kernel = 0;
+    return c;
+}
+
 // The full table: the CUDA-core kernel for M x parts <= 4, the swap kernel up to 256 tokens, the pair kernel where its
-// shape rule holds, else the per-tile kernel's entry.
+// shape rule holds (except narrow layers just above its M threshold), else the per-tile kernel's entry.
 KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
     KeaGemmConfig c = choose_tile(m, n, k, wbits, parts, sms);
     if (swap_shape(m, n, k, parts)) {
         const KeaGemmConfig s = swap_config(m, n, k, wbits, parts, sms);
         if (s.kernel == 3) c = s;
     }
-    if (pair_shape(m, n, k, parts)) c = pair_config(wbits, parts);
+    if (pair_shape(m, n, k, parts)) c = narrow_mid_m(m, n, k, parts) ? narrow_mid_config(m, n, k, wbits, sms)
+                                                                     : pair_config(wbits, parts);
     if (m * parts <= kGemvTableRows && gemv_fits(m, parts, gemv_channels(n, k, wbits, m, parts))) {
         c.kernel = 2;
         c.tile_m = m;
@@ -1123,6 +1148,17 @@ int kea_lowbit_quantize(const KeaQuantizeDesc *d, void *stream) {
     // codes are written as 32-bit words
     if ((reinterpret_cast<uintptr_t>(d->q) & 3u) || d->ldq % 4 || (d->parts > 1 && d->q_part_stride % 4))
         return KEA_ERR_ALIGNMENT;
+    const bool unit_rows = d->xk == 1 && d->k % 4 == 0 && (reinterpret_cast<uintptr_t>(d->x) & 15u) == 0 &&
+                           d->xt % 4 == 0 && (d->t == 1 || d->xb % 4 == 0) && d->k <= 32 * kea::kQuantThreads &&
+                           (!d->norm_weight || (reinterpret_cast<uintptr_t>(d->norm_weight) & 15u) == 0) &&
+                           (!d->norm_bias || (reinterpret_cast<uintptr_t>(d->norm_bias) & 15u) == 0);
+    if (d->pre_norm_weight) {   // the pre-norm keeps rows in registers: unit-stride, aligned rows only
+        const bool aligned = d->normed && (reinterpret_cast<uintptr_t>(d->normed) & 15u) == 0 && d->ld_normed % 4 == 0 &&
+                             d->ld_normed >= d->k && (reinterpret_cast<uintptr_t>(d->pre_norm_weight) & 15u) == 0 &&
+                             (!d->pre_norm_bias || (reinterpret_cast<uintptr_t>(d->pre_norm_bias) & 15u) == 0);
+        if (!aligned) return d->normed ? KEA_ERR_ALIGNMENT : KEA_ERR_INVALID_VALUE;
+        if (!unit_rows) return KEA_ERR_UNSUPPORTED;
+    }
     if (d->m == 0) return KEA_OK;
     int dev = 0;
     const int st = device_setup(&dev, stream);
@@ -1145,15 +1181,16 @@ int kea_lowbit_quantize(const KeaQuantizeDesc *d, void *stream) {
     a.nb = d->norm_bias;
     a.eps = d->eps;
     a.flags = d->flags & KEA_QUANT_INPUT_SILU;
+    a.pnw = d->pre_norm_weight;
+    a.pnb = d->pre_norm_bias;
+    a.peps = d->pre_eps;
+    a.normed = d->normed;
+    a.ldn = d->ld_normed;
     // Threads per row: enough CTAs to give every SM two (few rows: up to 256 threads on a row, for latency), as few
     // as one warp per row when rows are many.
     int tpr = 32;
     while (tpr < kea::kQuantThreads && (long long)ceil_div(d->m, kea::kQuantThreads / tpr) < 2LL * g_devices[dev].sms) tpr *= 2;
     cudaLaunchAttribute attr[1];
-    const bool unit_rows = d->xk == 1 && d->k % 4 == 0 && (reinterpret_cast<uintptr_t>(d->x) & 15u) == 0 &&
-                           d->xt % 4 == 0 && (d->t == 1 || d->xb % 4 == 0) && d->k <= 32 * kea::kQuantThreads &&
-                           (!d->norm_weight || (reinterpret_cast<uintptr_t>(d->norm_weight) & 15u) == 0) &&
-                           (!d->norm_bias || (reinterpret_cast<uintptr_t>(d->norm_bias) & 15u) == 0);
     if (unit_rows) {
         // registers: at most 32 values a thread
         while (tpr < kea::kQuantThreads && d->k > 32 * tpr) tpr *= 2;

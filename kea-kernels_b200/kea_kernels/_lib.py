@@ -59,6 +59,8 @@ class QuantizeDesc(ctypes.Structure):
         ("qs", ctypes.c_void_p), ("qs_part_stride", ctypes.c_int64),
         ("norm_weight", ctypes.c_void_p), ("norm_bias", ctypes.c_void_p), ("eps", ctypes.c_float),
         ("flags", ctypes.c_int32),
+        ("pre_norm_weight", ctypes.c_void_p), ("pre_norm_bias", ctypes.c_void_p), ("pre_eps", ctypes.c_float),
+        ("normed", ctypes.c_void_p), ("ld_normed", ctypes.c_int64),
     ]
 
 

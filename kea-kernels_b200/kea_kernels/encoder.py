@@ -52,9 +52,12 @@ class LowBitLinear(nn.Module):
         self.bias = None if bias is None else bias.to(device=device, dtype=torch.float32).contiguous()
 
     def forward(self, x: Tensor, *, norm: nn.LayerNorm | None = None, input_silu: bool = False,
-                silu: bool = False, residual: Tensor | None = None, residual_scale: float = 1.0) -> Tensor:
+                silu: bool = False, residual: Tensor | None = None, residual_scale: float = 1.0,
+                pre_norm: nn.LayerNorm | None = None, normed: Tensor | None = None) -> Tensor:
         """x [B, T, K] (any strides) -> [B, T, N]; with `residual` ([B, T, N] contiguous FP32) the GEMM's epilogue
-        returns residual + residual_scale * projection (the layer's skip connection, same roundings as unfused)."""
+        returns residual + residual_scale * projection (the layer's skip connection, same roundings as unfused).
+        `pre_norm`: a LayerNorm applied to x before `norm`, its output written to `normed` ([B, T, K] contiguous;
+        x itself allowed) - the previous layer's output norm folded into this quantizer."""
         b, t, k = x.shape
         m = b * t
         y = torch.empty(b, t, self.out_features, device=x.device, dtype=torch.float32)
@@ -63,7 +66,8 @@ class LowBitLinear(nn.Module):
         # the quantizer launches plainly: with programmatic dependent launch its CTAs would sit on the SMs while the
         # previous GEMM drains (measured slower on the clip); the GEMM after it does use it
         q, qs, ldq = lowbit.quantize(x, (x.stride(0), x.stride(1), x.stride(2), t), m, k, self.parts, norm=norm,
-                                     input_silu=input_silu)
+                                     input_silu=input_silu, pre_norm=pre_norm,
+                                     normed=None if normed is None else normed.view(m, k))
         res = None if residual is None else residual.reshape(m, self.out_features)
         lowbit.gemm(q, qs, ldq, m, self.panels, self.wbits, self.out_features, k, self.scale, self.bias,
                     y.view(m, self.out_features), parts=self.parts, silu=silu, pdl=self.pdl, residual=res,
@@ -202,14 +206,21 @@ class ConformerLayer(nn.Module):
         return self.lin["pw2"](h, input_silu=True, residual=x)          # SiLU in the quantizer; x + pw2(...)
 
     def forward(self, x: Tensor, lengths: Tensor | None = None) -> Tensor:
+        return self.norms["out"](self.body(x, lengths))
+
+    def body(self, x: Tensor, lengths: Tensor | None = None, pre_norm: nn.LayerNorm | None = None) -> Tensor:
+        """The layer without its output LayerNorm. `pre_norm` (the previous layer's output norm) is applied to x
+        inside FF1's quantizer, which writes the normalized rows back into x: the skip connection's input."""
         # every skip connection is added in the epilogue of the GEMM that ends its branch (x + 0.5 ff, x + att, ...)
-        x = self.lin["ff1_down"](self.lin["ff1_up"](x, norm=self.norms["ff1"], silu=True), residual=x,
-                                 residual_scale=0.5)
+        if pre_norm is not None and not x.is_contiguous():
+            x = x.contiguous()
+        h = self.lin["ff1_up"](x, norm=self.norms["ff1"], silu=True, pre_norm=pre_norm,
+                               normed=x if pre_norm is not None else None)
+        x = self.lin["ff1_down"](h, residual=x, residual_scale=0.5)
         x = self.attention(x, lengths)
         x = self.conv(x, lengths)
-        x = self.lin["ff2_down"](self.lin["ff2_up"](x, norm=self.norms["ff2"], silu=True), residual=x,
-                                 residual_scale=0.5)
-        return self.norms["out"](x)
+        return self.lin["ff2_down"](self.lin["ff2_up"](x, norm=self.norms["ff2"], silu=True), residual=x,
+                                    residual_scale=0.5)
 
 
 class Subsampling(nn.Module):
@@ -276,9 +287,12 @@ class FastConformerEncoder(nn.Module):
         length-bucketed batches of mixed-length clips)."""
         x = self.pre(mel)
         lens = None if lengths is None else lengths.to(device=x.device, dtype=torch.int32)
+        # each layer's output LayerNorm runs inside the next layer's first quantizer; the last one here
+        pre = None
         for layer in self.layers:
-            x = layer(x, lens)
-        return x
+            x = layer.body(x, lens, pre)
+            pre = layer.norms["out"]
+        return pre(x) if pre is not None else x
 
     def gemm_shapes(self, batch: int, t: int) -> list[tuple[str, int, int, int]]:
         """(name, M, N, K) of every low-bit GEMM one forward issues once linear_pos is cached."""

@@ -49,10 +49,13 @@ def prepare_panels(codes: Tensor, wbits: int, n: int, k: int) -> Tensor:
 
 
 def quantize(x: Tensor, rows: tuple[int, int, int, int], m: int, k: int, parts: int, *, ldq: int | None = None,
-             norm=None, input_silu: bool = False, pdl: bool = False) -> tuple[Tensor, Tensor, int]:
+             norm=None, input_silu: bool = False, pdl: bool = False, pre_norm=None,
+             normed: Tensor | None = None) -> tuple[Tensor, Tensor, int]:
     """x[m', kk] at x + (m' // T) * XB + (m' % T) * XT + kk * XK for rows = (XB, XT, XK, T) ->
     (q int8 [parts, m, ldq] zero-padded past k, qs FP32 [parts, m], ldq). pdl lets the kernel start while the
-    previous kernel on the stream finishes (it waits for that kernel's results before reading x)."""
+    previous kernel on the stream finishes (it waits for that kernel's results before reading x).
+    `pre_norm` (a LayerNorm) is applied first and its output written to `normed` (FP32 [m, k] rows, unit stride; may
+    be x itself): a layer's output norm folded into the next projection's quantizer."""
     _require_cuda(x, "x")
     if x.dtype != torch.float32:
         raise ValueError(f"expected FP32 input, got {x.dtype}")
@@ -71,6 +74,15 @@ def quantize(x: Tensor, rows: tuple[int, int, int, int], m: int, k: int, parts: 
         d.norm_weight = norm.weight.data_ptr()
         d.norm_bias = None if norm.bias is None else norm.bias.data_ptr()
         d.eps = float(norm.eps)
+    if pre_norm is not None:
+        if normed is None or normed.dtype != torch.float32 or normed.dim() != 2 or normed.shape[0] < m \
+                or normed.shape[1] < k or normed.stride(1) != 1:
+            raise ValueError("pre_norm needs `normed`, an FP32 [m, k] tensor with unit-stride rows")
+        _require_cuda(normed, "normed")
+        d.pre_norm_weight = pre_norm.weight.data_ptr()
+        d.pre_norm_bias = None if pre_norm.bias is None else pre_norm.bias.data_ptr()
+        d.pre_eps = float(pre_norm.eps)
+        d.normed, d.ld_normed = normed.data_ptr(), normed.stride(0)
     d.flags = (_lib.QUANT_INPUT_SILU if input_silu else 0) | (_lib.QUANT_PDL if pdl else 0)
     with torch.cuda.device(x.device):
         _lib.check(_lib.lib().kea_lowbit_quantize(ctypes.byref(d), _lib.stream_handle(x.device)), "quantize")

@@ -22,7 +22,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.kea_lowbit_version() == 2
+    assert lib.kea_lowbit_version() == 3
     assert lib.kea_lowbit_status_string(0) == b"success"
     assert lib.kea_lowbit_status_string(4) == b"invalid packed codes"
 
@@ -137,6 +137,30 @@ def test_c_abi_argument_errors_are_reported_before_any_device_work():
         _lib.check(_lib.ALIGNMENT, "gemm")
     with pytest.raises(RuntimeError):
         _lib.check(_lib.CUDA, "gemm")
+
+
+def _qdesc(**kw):
+    """A quantizer descriptor with plausible (never dereferenced) addresses: 125 unit-stride rows of 1024."""
+    d = _lib.QuantizeDesc()
+    d.x, d.xb, d.xt, d.xk, d.t, d.m, d.k, d.parts = 1 << 20, 0, 1024, 1, 125, 125, 1024, 1
+    d.q, d.q_part_stride, d.ldq, d.qs, d.qs_part_stride = 2 << 20, 125 * 1024, 1024, 3 << 20, 125
+    for key, value in kw.items():
+        setattr(d, key, value)
+    return d
+
+
+def test_quantizer_pre_norm_argument_errors_are_reported_before_any_device_work():
+    lib = _lib.lib()
+    pre = dict(pre_norm_weight=4 << 20, pre_eps=1e-5, normed=5 << 20, ld_normed=1024)
+    assert lib.kea_lowbit_quantize(ctypes.byref(_qdesc(**pre, m=0)), None) == _lib.OK        # empty: a no-op
+    assert lib.kea_lowbit_quantize(ctypes.byref(_qdesc(**{**pre, "normed": 0})), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_quantize(ctypes.byref(_qdesc(**{**pre, "normed": (5 << 20) + 4})), None) == _lib.ALIGNMENT
+    assert lib.kea_lowbit_quantize(ctypes.byref(_qdesc(**{**pre, "ld_normed": 1022})), None) == _lib.ALIGNMENT
+    assert lib.kea_lowbit_quantize(ctypes.byref(_qdesc(**{**pre, "ld_normed": 1020})), None) == _lib.ALIGNMENT
+    assert lib.kea_lowbit_quantize(ctypes.byref(_qdesc(**{**pre, "pre_norm_weight": (4 << 20) + 8})), None) == \
+        _lib.ALIGNMENT
+    # the pre-norm keeps rows in registers: the strided (conv layout) path refuses it
+    assert lib.kea_lowbit_quantize(ctypes.byref(_qdesc(**pre, xt=1, xk=125)), None) == _lib.UNSUPPORTED
 
 
 def test_python_boundary_refuses_host_tensors():
@@ -256,9 +280,10 @@ def test_encoder_layer_shapes_are_the_parakeet_linears():
 def test_split_k_workspace_only_where_pair_tiles_are_few():
     """Pair tiles filling at most a quarter of the SM pairs, with >= 16 k-blocks, split K through scratch: slices x
     parts x M x N INT32; every other shape needs none."""
-    assert _lib.workspace_bytes(512, 1024, 4096, 1, 1) == 8 * 512 * 1024 * 4       # 8 tiles, 32 k-blocks: 8 slices
+    assert _lib.workspace_bytes(512, 2048, 4096, 1, 1) == 4 * 512 * 2048 * 4       # 16 tiles, 32 k-blocks: 4 slices
     assert _lib.workspace_bytes(1000, 1024, 8192, 2, 1) == 4 * 1000 * 1024 * 4     # 16 tiles: 4 slices
     assert _lib.workspace_bytes(600, 256, 2100, 1, 1) == 4 * 600 * 256 * 4         # 3 tiles, 17 k-blocks: 4 slices
+    # (512, 1024, 4096), (300, 1024, 4096): a narrow layer just above the pair kernel's M runs on the per-tile kernel
     for shape in ((8192, 4096, 1024), (2048, 1024, 4096), (512, 4096, 1024), (125, 4096, 1024), (1, 1024, 4096),
-                  (512, 1024, 1024)):
+                  (512, 1024, 1024), (512, 1024, 4096), (300, 1024, 4096)):
         assert _lib.workspace_bytes(*shape, 1, 1) == 0, shape
