@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define KEA_LOWBIT_VERSION 3
+#define KEA_LOWBIT_VERSION 4
 
 /* Status codes. The Python layer maps 1-4 to ValueError and 5-8 to RuntimeError, as the reference raises
  * ValueError for argument errors (src/kea_kernels/binary/layer.py:66-78,188-189) and RuntimeError for a failed
@@ -236,10 +236,23 @@ typedef struct KeaConvDesc {
     const float *bias;        /* [C] or NULL */
     const int32_t *lengths;   /* [B] frames per clip, or NULL */
     int32_t b, t, c, kw;
-    int32_t flags;            /* KEA_CONV_PDL */
+    int32_t flags;            /* KEA_CONV_* */
+    /* Optional: the next projection's quantizer fused in (pw2's: residual INT8 parts of y, or of SiLU(y) with
+     * KEA_CONV_QUANT_SILU, with kea_lowbit_quantize's arithmetic, bit for bit): q int8 [parts][b * t][ldq] (columns
+     * c .. ldq - 1 written as 0; 4-byte aligned, ldq and the part stride multiples of 4), qs FP32 [parts][b * t].
+     * Needs c % 4 == 0, c <= 1024 and 16-byte aligned h. y may then be NULL (not written). q NULL: no quantizer. */
+    int8_t *q;
+    int64_t q_part_stride;
+    int32_t ldq;
+    float *qs;
+    int64_t qs_part_stride;
+    int32_t parts;
 } KeaConvDesc;
 
-enum { KEA_CONV_PDL = 1 };
+enum {
+    KEA_CONV_PDL = 1,
+    KEA_CONV_QUANT_SILU = 2       /* SiLU before the fused quantizer (the conv module's activation) */
+};
 
 int kea_lowbit_glu_depthwise(const KeaConvDesc *desc, void *stream);
 

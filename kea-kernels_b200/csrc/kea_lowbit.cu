@@ -973,6 +973,11 @@ template <int KW>
 cudaError_t launch_glu_dw(cudaLaunchConfig_t *cfg, const kea::ConvArgs &a) {
     return cudaLaunchKernelEx(cfg, kea::glu_depthwise_kernel<KW>, a);
 }
+template <int KW>
+cudaError_t launch_glu_dw_quant(cudaLaunchConfig_t *cfg, const kea::ConvQuantArgs &a, int frames) {
+    return frames == 4 ? cudaLaunchKernelEx(cfg, kea::glu_depthwise_quant_kernel<KW, 4>, a)
+                       : cudaLaunchKernelEx(cfg, kea::glu_depthwise_quant_kernel<KW, 8>, a);
+}
 
 extern "C" {
 
@@ -1100,9 +1105,19 @@ int kea_lowbit_rel_attention(const KeaAttentionDesc *d, void *stream) {
 }
 
 int kea_lowbit_glu_depthwise(const KeaConvDesc *d, void *stream) {
-    if (!d || !d->h || !d->y || !d->weight || d->b < 0 || d->t < 0 || d->c < 1 || d->kw < 1 || d->kw % 2 == 0 ||
-        d->kw > kea::kConvMaxKw || (d->flags & ~KEA_CONV_PDL))
+    if (!d || !d->h || (!d->y && !d->q) || !d->weight || d->b < 0 || d->t < 0 || d->c < 1 || d->kw < 1 ||
+        d->kw % 2 == 0 || d->kw > kea::kConvMaxKw || (d->flags & ~(KEA_CONV_PDL | KEA_CONV_QUANT_SILU)))
         return KEA_ERR_INVALID_VALUE;
+    const bool quant = d->q != nullptr;
+    if (quant) {
+        if (!d->qs || d->parts < 1 || d->parts > 3 || d->ldq < d->c) return KEA_ERR_INVALID_VALUE;
+        if ((reinterpret_cast<uintptr_t>(d->q) & 3u) || d->ldq % 4 || (d->parts > 1 && d->q_part_stride % 4) ||
+            (reinterpret_cast<uintptr_t>(d->h) & 15u) || (d->y && (reinterpret_cast<uintptr_t>(d->y) & 15u)))
+            return KEA_ERR_ALIGNMENT;
+        if (d->c % 4 || d->c > kea::kConvQMaxC || d->kw != 9) return KEA_ERR_UNSUPPORTED;   // the built fused form
+    } else if (d->flags & KEA_CONV_QUANT_SILU) {
+        return KEA_ERR_INVALID_VALUE;
+    }
     if (d->kw != 9 && d->kw != 3 && d->kw != 31) return KEA_ERR_UNSUPPORTED;   // the built widths
     if (d->b == 0 || d->t == 0) return KEA_OK;
     if (d->b > 65535) return KEA_ERR_UNSUPPORTED;
@@ -1120,6 +1135,35 @@ int kea_lowbit_glu_depthwise(const KeaConvDesc *d, void *stream) {
     a.C = d->c;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = {};
+    if (quant) {
+        kea::ConvQuantArgs qa{};
+        qa.c = a;
+        qa.q = d->q;
+        qa.q_stride = d->q_part_stride;
+        qa.ldq = d->ldq;
+        qa.qs = d->qs;
+        qa.qs_stride = d->qs_part_stride;
+        qa.parts = d->parts;
+        qa.silu = (d->flags & KEA_CONV_QUANT_SILU) ? 1 : 0;
+        // 4 frames a CTA while that keeps the grid within a few waves (one clip: 32 CTAs), else 8 (fewer halo
+        // re-reads for large batches)
+        const int frames = (long long)d->b * ceil_div(d->t, 4) <= 4LL * g_devices[dev].sms ? 4 : 8;
+        cfg.gridDim = dim3((unsigned)ceil_div(d->t, frames), (unsigned)d->b, 1);
+        cfg.blockDim = dim3(kea::kConvQThreads, 1, 1);
+        cfg.stream = (cudaStream_t)stream;
+        cfg.attrs = attr;
+        if (d->flags & KEA_CONV_PDL) {
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.numAttrs = 1;
+        }
+        const cudaError_t e = launch_glu_dw_quant<9>(&cfg, qa, frames);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return KEA_ERR_CUDA;
+        }
+        return KEA_OK;
+    }
     cfg.gridDim = dim3((unsigned)ceil_div(d->c, kea::kConvThreads), (unsigned)ceil_div(d->t, kea::kConvChunk),
                        (unsigned)d->b);
     cfg.blockDim = dim3(kea::kConvThreads, 1, 1);

@@ -27,7 +27,7 @@ EXPORTS = ("kea_lowbit_gemm", "kea_lowbit_gemm_noalloc", "kea_lowbit_choose_conf
            "kea_lowbit_prepare",
            "kea_lowbit_quantize", "kea_lowbit_glu_depthwise", "kea_lowbit_rel_attention", "kea_lowbit_read_error",
            "kea_lowbit_status_string", "kea_lowbit_version")
-CONV_PDL = 1
+CONV_PDL, CONV_QUANT_SILU = 1, 2
 
 
 class GemmDesc(ctypes.Structure):
@@ -67,7 +67,9 @@ class QuantizeDesc(ctypes.Structure):
 class ConvDesc(ctypes.Structure):
     _fields_ = [("h", ctypes.c_void_p), ("y", ctypes.c_void_p), ("weight", ctypes.c_void_p), ("bias", ctypes.c_void_p),
                 ("lengths", ctypes.c_void_p), ("b", ctypes.c_int32), ("t", ctypes.c_int32), ("c", ctypes.c_int32),
-                ("kw", ctypes.c_int32), ("flags", ctypes.c_int32)]
+                ("kw", ctypes.c_int32), ("flags", ctypes.c_int32),
+                ("q", ctypes.c_void_p), ("q_part_stride", ctypes.c_int64), ("ldq", ctypes.c_int32),
+                ("qs", ctypes.c_void_p), ("qs_part_stride", ctypes.c_int64), ("parts", ctypes.c_int32)]
 
 
 class AttentionDesc(ctypes.Structure):

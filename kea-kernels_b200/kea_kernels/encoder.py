@@ -60,17 +60,26 @@ class LowBitLinear(nn.Module):
         x itself allowed) - the previous layer's output norm folded into this quantizer."""
         b, t, k = x.shape
         m = b * t
-        y = torch.empty(b, t, self.out_features, device=x.device, dtype=torch.float32)
         if m == 0:
-            return y
+            return torch.empty(b, t, self.out_features, device=x.device, dtype=torch.float32)
         # the quantizer launches plainly: with programmatic dependent launch its CTAs would sit on the SMs while the
         # previous GEMM drains (measured slower on the clip); the GEMM after it does use it
         q, qs, ldq = lowbit.quantize(x, (x.stride(0), x.stride(1), x.stride(2), t), m, k, self.parts, norm=norm,
                                      input_silu=input_silu, pre_norm=pre_norm,
                                      normed=None if normed is None else normed.view(m, k))
+        return self.from_quantized(q, qs, ldq, b, t, silu=silu, residual=residual, residual_scale=residual_scale)
+
+    def from_quantized(self, q: Tensor, qs: Tensor, ldq: int, b: int, t: int, *, silu: bool = False,
+                       residual: Tensor | None = None, residual_scale: float = 1.0) -> Tensor:
+        """The GEMM on activations already quantized into `parts` INT8 parts (q [parts, b*t, ldq], qs [parts, b*t])
+        -> FP32 [b, t, N], with forward's epilogue options."""
+        m = b * t
+        y = torch.empty(b, t, self.out_features, device=q.device, dtype=torch.float32)
+        if m == 0:
+            return y
         res = None if residual is None else residual.reshape(m, self.out_features)
-        lowbit.gemm(q, qs, ldq, m, self.panels, self.wbits, self.out_features, k, self.scale, self.bias,
-                    y.view(m, self.out_features), parts=self.parts, silu=silu, pdl=self.pdl, residual=res,
+        lowbit.gemm(q, qs, ldq, m, self.panels, self.wbits, self.out_features, self.in_features, self.scale,
+                    self.bias, y.view(m, self.out_features), parts=self.parts, silu=silu, pdl=self.pdl, residual=res,
                     residual_scale=residual_scale)
         return y
 
@@ -202,8 +211,13 @@ class ConformerLayer(nn.Module):
         GLU, padding mask and the depthwise conv (BatchNorm folded in) are one kernel between the two GEMMs, reading
         and writing token-major rows, so pw2's quantizer (with the conv module's SiLU fused) reads unit-stride rows."""
         h = self.lin["pw1"](x, norm=self.norms["conv"])                 # [b, t, 2d]
+        pw2 = self.lin["pw2"]
+        if self.kernel == 9 and self.d % 4 == 0 and self.d <= 1024:
+            # pw2's quantizer (input SiLU) fused into the conv kernel: the FP32 conv output is never written
+            q, qs, ldq = lowbit.glu_depthwise_quantized(h, self.dw_weight, self.dw_bias, lengths, pw2.parts)
+            return pw2.from_quantized(q, qs, ldq, x.shape[0], x.shape[1], residual=x)   # x + pw2(...)
         h = lowbit.glu_depthwise(h, self.dw_weight, self.dw_bias, lengths)   # [b, t, d]
-        return self.lin["pw2"](h, input_silu=True, residual=x)          # SiLU in the quantizer; x + pw2(...)
+        return pw2(h, input_silu=True, residual=x)                      # SiLU in the quantizer; x + pw2(...)
 
     def forward(self, x: Tensor, lengths: Tensor | None = None) -> Tensor:
         return self.norms["out"](self.body(x, lengths))

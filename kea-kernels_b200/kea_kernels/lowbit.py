@@ -203,6 +203,45 @@ def glu_depthwise(h: Tensor, weight: Tensor, bias: Tensor | None = None, lengths
     return y
 
 
+def glu_depthwise_quantized(h: Tensor, weight: Tensor, bias: Tensor | None, lengths: Tensor | None, parts: int, *,
+                            silu: bool = True, ldq: int | None = None, pdl: bool = False) -> tuple[Tensor, Tensor, int]:
+    """glu_depthwise with the next projection's quantizer fused in: the conv output y [B, T, C] (never written) ->
+    (q int8 [parts, B*T, ldq], qs FP32 [parts, B*T], ldq), bit for bit quantize(y, input_silu=silu). Kernel width 9,
+    C % 4 == 0 and C <= 1024 (the Parakeet conv module); other shapes raise ValueError."""
+    _require_cuda(h, "h")
+    if h.dtype != torch.float32 or h.dim() != 3 or h.shape[2] % 2 or not h.is_contiguous():
+        raise ValueError("h must be contiguous FP32 [B, T, 2C]")
+    b, t, c2 = h.shape
+    c = c2 // 2
+    if weight.dim() == 3:
+        weight = weight.reshape(weight.shape[0], weight.shape[-1])
+    if weight.dtype != torch.float32 or weight.shape[0] != c or weight.device != h.device:
+        raise ValueError(f"weight must be FP32 [{c}, kw] on {h.device}")
+    if weight.shape[1] != 9 or c % 4 or c > 1024:
+        raise ValueError("the fused conv quantizer needs kernel width 9 and C % 4 == 0, C <= 1024")
+    weight = weight.contiguous()
+    if bias is not None and (bias.dtype != torch.float32 or tuple(bias.shape) != (c,) or bias.device != h.device):
+        raise ValueError(f"bias must be FP32 [{c}] on {h.device}")
+    if lengths is not None:
+        if tuple(lengths.shape) != (b,) or lengths.device != h.device:
+            raise ValueError(f"lengths must be [{b}] on {h.device}")
+        lengths = lengths.to(torch.int32).contiguous()
+    m = b * t
+    ldq = _round_up(c, 16) if ldq is None else ldq
+    q = torch.empty(parts, m, ldq, device=h.device, dtype=torch.int8)
+    qs = torch.empty(parts, m, device=h.device, dtype=torch.float32)
+    if m == 0:
+        return q, qs, ldq
+    flags = (_lib.CONV_PDL if pdl else 0) | (_lib.CONV_QUANT_SILU if silu else 0)
+    d = _lib.ConvDesc(h=h.data_ptr(), y=None, weight=weight.data_ptr(), bias=_lib.ptr(bias),
+                      lengths=_lib.ptr(lengths), b=b, t=t, c=c, kw=weight.shape[1], flags=flags, q=q.data_ptr(),
+                      q_part_stride=m * ldq, ldq=ldq, qs=qs.data_ptr(), qs_part_stride=m, parts=parts)
+    with torch.cuda.device(h.device):
+        _lib.check(_lib.lib().kea_lowbit_glu_depthwise(ctypes.byref(d), _lib.stream_handle(h.device)),
+                   "glu_depthwise_quantized")
+    return q, qs, ldq
+
+
 def rel_attention(qkv: Tensor, pos: Tensor, bias_u: Tensor, bias_v: Tensor, heads: int,
                   lengths: Tensor | None = None, *, pdl: bool = False) -> Tensor:
     """Relative-position self-attention in one kernel: qkv FP32 [B, T, 3 * H * DK] (q, k, v of each token, heads

@@ -153,6 +153,55 @@ def test_glu_depthwise_rejects_bad_arguments():
         lowbit.glu_depthwise(h.transpose(1, 2), torch.randn(4, 1, 9, device=DEV))
 
 
+@pytest.mark.parametrize("b,t,c", [(1, 125, 1024), (3, 37, 1000), (40, 125, 256), (2, 1, 4)])
+@pytest.mark.parametrize("parts", [1, 3])
+@pytest.mark.parametrize("silu,masked", [(True, True), (True, False), (False, True)])
+@torch.inference_mode()
+def test_glu_depthwise_with_fused_quantizer_equals_the_two_kernels(b, t, c, parts, silu, masked):
+    """pw2's quantizer fused into the conv kernel: the INT8 parts and scales equal glu_depthwise followed by the
+    quantizer (input SiLU) bit for bit - four and eight frames per CTA (40 clips take the wider chunks), ragged C
+    (padding columns of ldq zeroed), padded frames, one and three parts; the FP32 output, when the C ABI is given
+    one, equals glu_depthwise's."""
+    import ctypes
+    from kea_kernels import _lib, lowbit
+    g = torch.Generator().manual_seed(b * 1000 + t + c + parts)
+    h = torch.randn(b, t, 2 * c, generator=g).to(DEV)
+    w = (torch.randn(c, 1, 9, generator=g) / 3).to(DEV)
+    bias = (0.1 * torch.randn(c, generator=g)).to(DEV)
+    lengths = torch.randint(1, t + 1, (b,), generator=g).to(DEV) if masked else None
+    q, qs, ldq = lowbit.glu_depthwise_quantized(h, w, bias, lengths, parts, silu=silu)
+    y = lowbit.glu_depthwise(h, w, bias, lengths)
+    q2, qs2, ldq2 = lowbit.quantize(y, (y.stride(0), y.stride(1), 1, t), b * t, c, parts, input_silu=silu)
+    torch.cuda.synchronize()
+    assert ldq == ldq2
+    assert torch.equal(q, q2)
+    assert torch.equal(qs.view(torch.int32), qs2.view(torch.int32))
+    # through the C ABI with the FP32 output requested as well
+    yf = torch.full_like(y, float("nan"))
+    q3 = torch.full_like(q, 7)
+    qs3 = torch.empty_like(qs)
+    wc = w.reshape(c, 9).contiguous()
+    lens32 = None if lengths is None else lengths.to(torch.int32).contiguous()
+    d = _lib.ConvDesc(h=h.data_ptr(), y=yf.data_ptr(), weight=wc.data_ptr(), bias=bias.data_ptr(),
+                      lengths=_lib.ptr(lens32), b=b, t=t, c=c, kw=9, flags=_lib.CONV_QUANT_SILU if silu else 0,
+                      q=q3.data_ptr(), q_part_stride=b * t * ldq, ldq=ldq, qs=qs3.data_ptr(), qs_part_stride=b * t,
+                      parts=parts)
+    assert _lib.lib().kea_lowbit_glu_depthwise(ctypes.byref(d), _lib.stream_handle(h.device)) == _lib.OK
+    torch.cuda.synchronize()
+    assert torch.equal(yf.view(torch.int32), y.view(torch.int32))
+    assert torch.equal(q3, q) and torch.equal(qs3.view(torch.int32), qs.view(torch.int32))
+
+
+def test_glu_depthwise_fused_quantizer_rejects_other_shapes():
+    from kea_kernels import lowbit
+    h = torch.randn(1, 4, 12, device=DEV)
+    with pytest.raises(ValueError):
+        lowbit.glu_depthwise_quantized(h, torch.randn(6, 1, 9, device=DEV), None, None, 1)    # C % 4
+    with pytest.raises(ValueError):
+        lowbit.glu_depthwise_quantized(torch.randn(1, 4, 16, device=DEV), torch.randn(8, 1, 3, device=DEV), None,
+                                       None, 1)                                                  # width 3
+
+
 def _torch_rel_attention(qkv, pos, u, v, heads, lengths=None):
     b, t, w3 = qkv.shape
     d = w3 // 3

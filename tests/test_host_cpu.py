@@ -22,7 +22,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.kea_lowbit_version() == 3
+    assert lib.kea_lowbit_version() == 4
     assert lib.kea_lowbit_status_string(0) == b"success"
     assert lib.kea_lowbit_status_string(4) == b"invalid packed codes"
 
@@ -161,6 +161,29 @@ def test_quantizer_pre_norm_argument_errors_are_reported_before_any_device_work(
         _lib.ALIGNMENT
     # the pre-norm keeps rows in registers: the strided (conv layout) path refuses it
     assert lib.kea_lowbit_quantize(ctypes.byref(_qdesc(**pre, xt=1, xk=125)), None) == _lib.UNSUPPORTED
+
+
+def test_fused_conv_quantizer_argument_errors_are_reported_before_any_device_work():
+    lib = _lib.lib()
+
+    def conv(**kw):
+        base = dict(h=1 << 20, y=0, weight=2 << 20, b=1, t=125, c=1024, kw=9, flags=0, q=3 << 20,
+                    q_part_stride=125 * 1024, ldq=1024, qs=4 << 20, qs_part_stride=125, parts=1)
+        base.update(kw)
+        return lib.kea_lowbit_glu_depthwise(ctypes.byref(_lib.ConvDesc(**base)), None)
+
+    assert conv(q=0) == _lib.INVALID_VALUE                                  # neither y nor q
+    assert conv(q=0, y=5 << 20, flags=_lib.CONV_QUANT_SILU) == _lib.INVALID_VALUE   # SiLU flag without q
+    assert conv(qs=0) == _lib.INVALID_VALUE
+    assert conv(parts=4) == _lib.INVALID_VALUE
+    assert conv(ldq=1020) == _lib.INVALID_VALUE                             # ldq < c
+    assert conv(q=(3 << 20) + 2) == _lib.ALIGNMENT
+    assert conv(ldq=1030) == _lib.ALIGNMENT
+    assert conv(h=(1 << 20) + 4) == _lib.ALIGNMENT
+    assert conv(c=1022, ldq=1024) == _lib.UNSUPPORTED                       # c % 4
+    assert conv(c=1028, ldq=1040) == _lib.UNSUPPORTED                       # c > 1024
+    assert conv(kw=3) == _lib.UNSUPPORTED                                   # the fused form is built for width 9
+    assert conv(b=0) == _lib.OK                                             # empty: a no-op
 
 
 def test_python_boundary_refuses_host_tensors():
