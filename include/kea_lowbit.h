@@ -218,10 +218,40 @@ typedef struct KeaQuantizeDesc {
 
 enum {
     KEA_QUANT_INPUT_SILU = 1,
-    KEA_QUANT_PDL = 2             /* launch with programmatic dependent launch (overlap with the previous kernel) */
+    KEA_QUANT_PDL = 2,            /* launch with programmatic dependent launch (overlap with the previous kernel) */
+    KEA_QUANT_NARROW_ROWS = 4     /* as few threads per row as registers allow (one warp for K <= 1024): the
+                                     reduction order of the GEMM's fused prologue quantizer (kea_lowbit_project) */
 };
 
 int kea_lowbit_quantize(const KeaQuantizeDesc *desc, void *stream);
+
+/* Quantize + GEMM in one call: the reference's Int8MmaLayer.project (src/kea_kernels/binary/layer.py:118-151;
+ * src/kea_kernels/binary/layer_parts.py:65-90), x -> residual INT8 parts -> the low-bit GEMM with its epilogue.
+ * `quant` gives the input rows and the quantizer's options (pre-norm, LayerNorm, input SiLU); its m, k, parts, q, ldq,
+ * qs (and the part strides when parts > 1) must equal `gemm`'s, whose q / qs receive the parts. By default the two
+ * kernels run back to back (kea_lowbit_quantize with quant's flags, then kea_lowbit_gemm): measured the faster form
+ * on B200, since the GEMM's set-up and weight expansion overlap the quantizer kernel under programmatic dependent
+ * launch. With KEA_PROJECT_FUSE, where the shape allows - one part, 33 <= m <= 128 (the per-tile route), k a multiple
+ * of 128 up to 1024, channel tiles in whole clusters of 8, unit-stride 16-byte-aligned rows, a pre-norm output apart
+ * from x - the quantizer runs inside the GEMM kernel, one launch: each cluster of 8 CTAs quantizes the token rows
+ * (one warp a row, the arithmetic of kea_lowbit_quantize with KEA_QUANT_NARROW_ROWS, bit for bit) into `scratch`,
+ * then reads them back as its activation boxes. scratch: 16-byte aligned, kea_lowbit_project_scratch_bytes(...)
+ * bytes (0 = the fused form never applies; a smaller scratch falls back to the two kernels). */
+typedef struct KeaProjectDesc {
+    KeaGemmDesc gemm;
+    KeaQuantizeDesc quant;
+    void *scratch;
+    size_t scratch_bytes;
+    int32_t flags;            /* KEA_PROJECT_* */
+} KeaProjectDesc;
+
+enum { KEA_PROJECT_FUSE = 1 };
+
+int kea_lowbit_project(const KeaProjectDesc *desc, void *stream);
+/* Which form kea_lowbit_project takes for this descriptor (with its flags): 1 one fused kernel, 0 the two kernels,
+ * -(status) when the arguments are refused. Launches nothing. */
+int kea_lowbit_project_fuses(const KeaProjectDesc *desc);
+size_t kea_lowbit_project_scratch_bytes(int32_t m, int32_t n, int32_t k, int32_t wbits, int32_t parts);
 
 /* The convolution module's middle between its pointwise GEMMs, in one pass over pw1's output:
  *   g[b, t, c] = h[b, t, c] * sigmoid(h[b, t, C + c]), zero where t >= lengths[b] (padding);

@@ -112,38 +112,6 @@ KEA_DEVI float group_reduce(float v, bool use_max, int tpr, float *scratch) {
     return r;
 }
 
-// rint(v / s) with the IEEE round-to-nearest quotient, without a division on the common path. Here |v| <= 127 s
-// (s is the part's amax / 127, or larger), so |v / s| <= 127 + 1e-4, and q = RN(v * RN(1 / s)) differs from v / s
-// by at most 2 * 2^-24 * 127 < 1.6e-5 while the IEEE quotient differs from v / s by at most 7.6e-6: the two round to
-// the same integer unless a half-integer lies within 2.4e-5 of q. Values within 1e-4 of a half-integer (and anything
-// non-finite or out of range) take the exact division.
-KEA_DEVI float round_quotient(float v, float s, float inv) {
-    const float q = __fmul_rn(v, inv);
-    const float f = fabsf(q - truncf(q));
-    if (fabsf(f - 0.5f) > 1.0e-4f && fabsf(q) < 128.0f) return rintf(q);
-    return rintf(__fdiv_rn(v, s));
-}
-
-// Four codes rint(e[j] / s) (the IEEE quotient, as round_quotient) packed little-endian into a word; r[j] gets the
-// codes as floats. Branch-free on the common path: the four products e[j] * RN(1 / s) are rounded together and one
-// flag records whether any lies within 1e-4 of a half-integer (or is not a number); only then are the four redone
-// with the exact division.
-KEA_DEVI uint32_t quantize4(const float *e, float s, float inv, float (&r)[4]) {
-    bool odd = false;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float t = __fmul_rn(e[j], inv);
-        r[j] = rintf(t);
-        odd |= !(fabsf(__fsub_rn(t, r[j])) < 0.4999f);
-    }
-    if (odd) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) r[j] = rintf(__fdiv_rn(e[j], s));
-    }
-    const int b0 = __float2int_rn(r[0]), b1 = __float2int_rn(r[1]), b2 = __float2int_rn(r[2]), b3 = __float2int_rn(r[3]);
-    return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
-}
-
 // group_reduce with a scratch slot of its own (kQuantThreads / 32 floats) per reduction of the kernel, so no
 // barrier is needed before the slot is written (no earlier reduction can still be reading it). Same order of
 // operations as group_reduce, so the same result bit for bit.

@@ -22,6 +22,7 @@
 #include <cuda_fp16.h>
 
 #include "ptx.cuh"
+#include "quant_common.cuh"
 
 namespace kea {
 
@@ -84,7 +85,29 @@ struct GemmArgs {
                                  // qmap is then (k, row, part, k-block) with boxes of mp rows x P parts
     int mp;                      // stacked rows per part: M rounded up to the 8-row swizzle atom
     uint32_t *err;
+    // Fused prologue quantizer (fq = 1; one-shot, one token tile, one part, K unsplit, K <= 1024): the CTAs of a
+    // thread-block cluster of kFqCluster along N quantize the FP32 rows themselves - CTA rank r's epilogue warp w takes
+    // token row r + kFqCluster * w - into the cluster's scratch [128][K] INT8 + [128] scales, then a cluster barrier,
+    // then the activation boxes are read from that scratch (qmap covers [clusters * 128][K]).
+    int fq;
+    const float *fq_x;           // row m at fq_x + (m / fq_t) * fq_xb + (m % fq_t) * fq_xt, unit stride along K
+    long long fq_xb, fq_xt;
+    int fq_t;
+    int fq_silu;                 // input SiLU
+    const float *fq_nw, *fq_nb;  // LayerNorm (fq_nw null: none), staged in shared memory at fq_off
+    float fq_eps;
+    const float *fq_pnw, *fq_pnb;   // pre-norm applied first (null: none), staged at fq_off + 2 K floats
+    float fq_peps;
+    uint32_t fq_off;             // within the activation region (empty until the quantized rows are loaded)
+    int8_t *fq_scr;              // [cluster][128][K]
+    float *fq_qs_scr;            // [cluster][128]
+    int8_t *fq_q;                // optional copies for the caller, written by cluster 0: codes [M][fq_ldq], scales
+    float *fq_qs;                // [M], pre-norm output [M][fq_ldn]
+    int fq_ldq;
+    float *fq_normed;
+    long long fq_ldn;
 };
+constexpr int kFqCluster = 8;
 
 // ---- weight expansion --------------------------------------------------------------------------------------
 KEA_DEVI uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -313,6 +336,52 @@ KEA_DEVI void named_barrier_sync(uint32_t id, uint32_t threads) {
 
 KEA_DEVI void report(uint32_t *err, uint32_t bits) { atomicOr(err ? err : &g_device_error, bits); }
 
+// The fused prologue quantizer's row work for one epilogue warp (w = 0 .. 15 of CTA rank r in its cluster): token
+// row r + kFqCluster * w of the cluster's 128-row block, quantized with quantize_regs_kernel's arithmetic at 32
+// threads per row (pre-norm, LayerNorm, input SiLU, one part) into the cluster's scratch; cluster 0 also writes the
+// caller's copies (codes with zeroed padding columns, scales, pre-norm output). `ln` holds the staged parameters:
+// norm weight, norm bias, pre-norm weight, pre-norm bias, K floats each.
+KEA_DEVI void fused_quantize_rows(const GemmArgs &a, int w, int lane, const float *ln) {
+    const int cid = (int)(blockIdx.x / kFqCluster), rank = (int)(blockIdx.x % kFqCluster);
+    const int row = rank + kFqCluster * w;
+    if (row >= a.M) return;
+    const int K = a.K;
+    const float4 *src = reinterpret_cast<const float4 *>(a.fq_x + (long long)(row / a.fq_t) * a.fq_xb +
+                                                         (long long)(row % a.fq_t) * a.fq_xt);
+    float4 v[kRowChunks];
+#pragma unroll
+    for (int c = 0; c < kRowChunks; ++c) {
+        const int i = c * 32 + lane;
+        v[c] = 4 * i < K ? __ldg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const bool first = cid == 0;
+    if (a.fq_pnw) {
+        warp_layer_norm(v, K, lane, ln + 2 * K, a.fq_pnb ? ln + 3 * K : nullptr, a.fq_peps);
+        if (first && a.fq_normed) {
+            float4 *dst = reinterpret_cast<float4 *>(a.fq_normed + (long long)row * a.fq_ldn);
+#pragma unroll
+            for (int c = 0; c < kRowChunks; ++c)
+                if (4 * (c * 32 + lane) < K) dst[c * 32 + lane] = v[c];
+        }
+    }
+    if (a.fq_nw) warp_layer_norm(v, K, lane, ln, a.fq_nb ? ln + K : nullptr, a.fq_eps);
+    uint32_t words[kRowChunks];
+    const float scale = warp_quantize_row(v, K, lane, a.fq_silu != 0, words);
+    uint32_t *scr = reinterpret_cast<uint32_t *>(a.fq_scr + ((long long)cid * kBM + row) * K);
+#pragma unroll
+    for (int c = 0; c < kRowChunks; ++c)
+        if (4 * (c * 32 + lane) < K) scr[c * 32 + lane] = words[c];
+    if (lane == 0) a.fq_qs_scr[cid * kBM + row] = scale;
+    if (first && a.fq_q) {
+        uint32_t *q = reinterpret_cast<uint32_t *>(a.fq_q + (long long)row * a.fq_ldq);
+#pragma unroll
+        for (int c = 0; c < kRowChunks; ++c)
+            if (4 * (c * 32 + lane) < K) q[c * 32 + lane] = words[c];
+        for (int i = K / 4 + lane; i < a.fq_ldq / 4; i += 32) q[i] = 0u;   // padding columns
+        if (lane == 0) a.fq_qs[row] = scale;
+    }
+}
+
 template <int WBITS, int P>
 __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                    const __grid_constant__ CUtensorMap ymap,
@@ -372,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
     // With programmatic dependent launch, everything below may read what the previous kernel wrote. In one-shot
     // mode the packed codes (static weights) are loaded and expanded first, while the previous kernel finishes:
     // only the producer's activation boxes and the expanders' token-scale loads wait for it.
-    const bool early_w = a.pdl && a.oneshot;
+    const bool early_w = a.oneshot && (a.pdl || a.fq);
     if (a.pdl && !early_w) grid_dependency_wait();
 
     bool ok = true;
@@ -392,16 +461,24 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
         if (a.oneshot) {
             // Every k-block of this CTA at once: one TMA box of the panels (kbox k-blocks x wbits x 4 word planes
             // of this CTA's R rows) and one 4-D box of activations (128 rows x kbox k-blocks), both on bar_full[0].
-            if (lane == 0) {
-                if (early_w) {   // every chunk's codes on bar_w now; the activations once the previous kernel is done
-                    const uint32_t wbar = smem_u32(&bar_w);
-                    mbar_arrive_expect_tx(wbar, (uint32_t)(a.chunks * a.kbox) * a.pk_stage);
-                    for (int c = 0; c < a.chunks; ++c) {
-                        const int plane0 = ((n0 / kPanelN) * a.kb_total + kb0 + c * a.kbox) * WBITS * 4;
-                        tma_load_2d(PK0 + (uint32_t)(c * a.kbox) * a.pk_stage, &wmap, wbar, (n0 % kPanelN) * 4, plane0);
-                    }
-                    grid_dependency_wait();
+            if (lane == 0 && early_w) {   // every chunk's codes on bar_w now; the activations once the previous
+                const uint32_t wbar = smem_u32(&bar_w);   // kernel is done
+                mbar_arrive_expect_tx(wbar, (uint32_t)(a.chunks * a.kbox) * a.pk_stage);
+                for (int c = 0; c < a.chunks; ++c) {
+                    const int plane0 = ((n0 / kPanelN) * a.kb_total + kb0 + c * a.kbox) * WBITS * 4;
+                    tma_load_2d(PK0 + (uint32_t)(c * a.kbox) * a.pk_stage, &wmap, wbar, (n0 % kPanelN) * 4, plane0);
                 }
+                grid_dependency_wait();
+            }
+            __syncwarp();
+            if (a.fq) {   // the cluster's epilogue warps have quantized its token rows into the scratch
+                cluster_arrive();
+                cluster_wait();
+            }
+            // the activation rows: this token tile's, or the cluster's scratch block
+            const int arow = a.fq ? (int)(blockIdx.x / kFqCluster) * kBM : t0;
+            if (lane == 0) {
+                if (a.fq) fence_proxy_async_global();   // generic-proxy stores of the peers, read by TMA below
                 for (int c = 0; c < a.chunks; ++c) {
                     const uint32_t full = smem_u32(&bar_full[c]);
                     const int kbc = kb0 + c * a.kbox;
@@ -412,9 +489,9 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                     }
                     const uint32_t adst = A0 + (uint32_t)(c * a.kbox) * a.a_stride;
                     if (a.stack)
-                        tma_load_4d(adst, &qmap, full, 0, t0, 0, kbc);
+                        tma_load_4d(adst, &qmap, full, 0, arow, 0, kbc);
                     else
-                        tma_load_4d(adst, &qmap, full, 0, t0, kbc, 0);
+                        tma_load_4d(adst, &qmap, full, 0, arow, kbc, 0);
                 }
             }
             __syncwarp();
@@ -476,6 +553,10 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer: the whole warp waits, lane 0 issues ----------------
+        if (a.fq) {   // the fused quantizer's cluster barrier (every thread of the cluster takes part)
+            cluster_arrive();
+            cluster_wait();
+        }
         const uint32_t idesc = idesc_i8(kBM, (uint32_t)TN);
         const uint64_t a_desc0 = sw128_kmajor_desc(A0), b_desc0 = sw128_kmajor_desc(B0);
         if (a.oneshot && nkb > 0) {
@@ -574,10 +655,30 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_gemm_kernel(const __grid_c
                 if (lane == 0)
                     for (int st = 0; st < nkb; ++st) mbar_arrive(smem_u32(&bar_exp[st]));
             }
-            grid_dependency_wait();
-            for (int i = e; i < P * TMB * kBM; i += kEpiThreads) {
-                const int p = i / (TMB * kBM), t = t0 + (i - p * TMB * kBM);
-                s_qs[i] = t < a.M ? a.qs[p * a.qs_stride + t] : 0.f;
+            if (a.fq) {
+                // the LayerNorms' parameters (static) into shared memory before the wait
+                float *ln = reinterpret_cast<float *>(dyn_smem + (base - raw) + a.fq_off);
+                for (int i = e; i < a.K; i += kEpiThreads) {
+                    ln[i] = a.fq_nw ? a.fq_nw[i] : 0.f;
+                    ln[a.K + i] = a.fq_nb ? a.fq_nb[i] : 0.f;
+                    ln[2 * a.K + i] = a.fq_pnw ? a.fq_pnw[i] : 0.f;
+                    ln[3 * a.K + i] = a.fq_pnb ? a.fq_pnb[i] : 0.f;
+                }
+                named_barrier_sync(4, kEpiThreads);
+                grid_dependency_wait();
+                fused_quantize_rows(a, (warp - 2), lane, ln);
+                fence_proxy_async_global();
+                fence_async_shared();   // the parameters' reads before the activation boxes land over them
+                cluster_arrive();
+                cluster_wait();
+                const float *qs_scr = a.fq_qs_scr + (blockIdx.x / kFqCluster) * kBM;
+                for (int i = e; i < kBM; i += kEpiThreads) s_qs[i] = i < a.M ? qs_scr[i] : 0.f;
+            } else {
+                grid_dependency_wait();
+                for (int i = e; i < P * TMB * kBM; i += kEpiThreads) {
+                    const int p = i / (TMB * kBM), t = t0 + (i - p * TMB * kBM);
+                    s_qs[i] = t < a.M ? a.qs[p * a.qs_stride + t] : 0.f;
+                }
             }
         } else if (a.oneshot) {
             // Each chunk's k-blocks are resident at once: spread them over the 512 threads, then one proxy fence and

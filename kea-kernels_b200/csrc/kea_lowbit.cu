@@ -1183,26 +1183,38 @@ int kea_lowbit_glu_depthwise(const KeaConvDesc *d, void *stream) {
     return KEA_OK;
 }
 
-int kea_lowbit_quantize(const KeaQuantizeDesc *d, void *stream) {
+static bool quant_unit_rows(const KeaQuantizeDesc *d) {
+    return d->xk == 1 && d->k % 4 == 0 && (reinterpret_cast<uintptr_t>(d->x) & 15u) == 0 && d->xt % 4 == 0 &&
+           (d->t == 1 || d->xb % 4 == 0) && d->k <= 32 * kea::kQuantThreads &&
+           (!d->norm_weight || (reinterpret_cast<uintptr_t>(d->norm_weight) & 15u) == 0) &&
+           (!d->norm_bias || (reinterpret_cast<uintptr_t>(d->norm_bias) & 15u) == 0);
+}
+
+// Argument checks of the quantizer (KEA_OK: launchable).
+static int validate_quantize(const KeaQuantizeDesc *d) {
     if (!d || !d->x || !d->q || !d->qs || d->m < 0 || d->k < 1 || d->parts < 1 || d->parts > 3 || d->t < 1 ||
         d->ldq < d->k)
         return KEA_ERR_INVALID_VALUE;
-    if (d->flags & ~(KEA_QUANT_INPUT_SILU | KEA_QUANT_PDL)) return KEA_ERR_INVALID_VALUE;
+    if (d->flags & ~(KEA_QUANT_INPUT_SILU | KEA_QUANT_PDL | KEA_QUANT_NARROW_ROWS)) return KEA_ERR_INVALID_VALUE;
     if ((long long)d->k * 4 > 64 * 1024) return KEA_ERR_UNSUPPORTED;
     // codes are written as 32-bit words
     if ((reinterpret_cast<uintptr_t>(d->q) & 3u) || d->ldq % 4 || (d->parts > 1 && d->q_part_stride % 4))
         return KEA_ERR_ALIGNMENT;
-    const bool unit_rows = d->xk == 1 && d->k % 4 == 0 && (reinterpret_cast<uintptr_t>(d->x) & 15u) == 0 &&
-                           d->xt % 4 == 0 && (d->t == 1 || d->xb % 4 == 0) && d->k <= 32 * kea::kQuantThreads &&
-                           (!d->norm_weight || (reinterpret_cast<uintptr_t>(d->norm_weight) & 15u) == 0) &&
-                           (!d->norm_bias || (reinterpret_cast<uintptr_t>(d->norm_bias) & 15u) == 0);
     if (d->pre_norm_weight) {   // the pre-norm keeps rows in registers: unit-stride, aligned rows only
         const bool aligned = d->normed && (reinterpret_cast<uintptr_t>(d->normed) & 15u) == 0 && d->ld_normed % 4 == 0 &&
                              d->ld_normed >= d->k && (reinterpret_cast<uintptr_t>(d->pre_norm_weight) & 15u) == 0 &&
                              (!d->pre_norm_bias || (reinterpret_cast<uintptr_t>(d->pre_norm_bias) & 15u) == 0);
         if (!aligned) return d->normed ? KEA_ERR_ALIGNMENT : KEA_ERR_INVALID_VALUE;
-        if (!unit_rows) return KEA_ERR_UNSUPPORTED;
+        if (!quant_unit_rows(d)) return KEA_ERR_UNSUPPORTED;
     }
+    return KEA_OK;
+}
+
+int kea_lowbit_quantize(const KeaQuantizeDesc *d, void *stream) {
+    const int vq = validate_quantize(d);
+    if (vq != KEA_OK) return vq;
+    if ((long long)d->k * 4 > 64 * 1024) return KEA_ERR_UNSUPPORTED;
+    const bool unit_rows = quant_unit_rows(d);
     if (d->m == 0) return KEA_OK;
     int dev = 0;
     const int st = device_setup(&dev, stream);
@@ -1236,6 +1248,7 @@ int kea_lowbit_quantize(const KeaQuantizeDesc *d, void *stream) {
     while (tpr < kea::kQuantThreads && (long long)ceil_div(d->m, kea::kQuantThreads / tpr) < 2LL * g_devices[dev].sms) tpr *= 2;
     cudaLaunchAttribute attr[1];
     if (unit_rows) {
+        if (d->flags & KEA_QUANT_NARROW_ROWS) tpr = 32;
         // registers: at most 32 values a thread
         while (tpr < kea::kQuantThreads && d->k > 32 * tpr) tpr *= 2;
         const int vpt = round_up(ceil_div(d->k, tpr), 4);
@@ -1259,23 +1272,67 @@ int kea_lowbit_quantize(const KeaQuantizeDesc *d, void *stream) {
     return e == cudaSuccess ? KEA_OK : KEA_ERR_CUDA;
 }
 
-int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
-    const int v = validate_gemm(d);
-    if (v != KEA_OK || d->m == 0) return v;
-    int dev = 0;
-    const int st = device_setup(&dev, stream);
-    if (st != KEA_OK) return st;
+}  // extern "C"
 
+// The fused prologue quantizer of the per-tile kernel: the quantizer descriptor's input rows and options, and the
+// caller's scratch for the clusters' quantized blocks.
+struct FusedQuant {
+    const KeaQuantizeDesc *q;
+    void *scratch;
+    size_t scratch_bytes;
+    bool dry_run;                 // decide only: KEA_OK if the fused form applies, nothing launched
+};
+constexpr int kNotFused = 1000;   // launch_tile's answer when the fused form does not apply (nothing launched)
+
+size_t fused_scratch_bytes(int clusters, int k) { return (size_t)clusters * kea::kBM * ((size_t)k + 4); }
+
+// Clusters of kFqCluster CTAs of the per-tile kernel (wbits, one part) with `smem` bytes of dynamic shared memory
+// that fit on the device at once (one wave), looked up once per (device, wbits, size) and cached.
+int fused_max_clusters(int dev, int wbits, int smem) {
+    struct Entry { int dev, wbits, smem, clusters; };
+    static Entry cache[32];
+    static int used = 0;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    for (int i = 0; i < used; ++i)
+        if (cache[i].dev == dev && cache[i].wbits == wbits && cache[i].smem == smem) return cache[i].clusters;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kea::kFqCluster, 1, 1);
+    cfg.blockDim = dim3(kea::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kea::kFqCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    const void *fn = wbits == 1 ? (const void *)kea::lowbit_gemm_kernel<1, 1> : (const void *)kea::lowbit_gemm_kernel<2, 1>;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    if (used < 32) cache[used++] = Entry{dev, wbits, smem, n};
+    return n;
+}
+
+// The fused form stages the LayerNorms' parameters (4 K floats) in the activation region, empty until the
+// quantized rows are loaded there, so it needs no more shared memory than the plain launch.
+constexpr uint32_t kFqParamOffset = 0;
+
+// The per-tile kernel's launch for the table's (or the caller's forced) tiles; with `fq`, only the fused form (one
+// launch quantizing and multiplying) or kNotFused.
+int launch_tile(const KeaGemmDesc *d, KeaGemmConfig c, int dev, void *stream, const FusedQuant *fq) {
     const bool forced = d->tile_m || d->tile_n || d->splits || d->stages;
-    Route route;
-    KeaGemmConfig c{};
-    SwapPlan sp;
-    const int rs = route_gemm(d, g_devices[dev].sms, &route, &c, &sp);
-    if (rs != KEA_OK) return rs;
-    if (route == kRouteGemv) return launch_gemv(d, c, stream);
-    if (route == kRouteSwap) return launch_swap(d, sp, stream);
-    if (route == kRoutePair) return launch_pair(d, c, g_devices[dev].sms, stream);
     if (c.kernel) c = choose_tile(d->m, d->n, d->k, d->wbits, d->parts, g_devices[dev].sms);
+    // the channel tile widened to 64 where the fused form's clusters would not all fit on the device at once (N 4096
+    // at 32 channels: 16 clusters of 8 against 15 that fit at one CTA per SM)
+    if (fq && !forced && c.tile_n == 32 && d->parts == 1 && c.splits == 1 &&
+        ceil_div(d->n, 32) / kea::kFqCluster > fused_max_clusters(dev, d->wbits, c.smem_bytes)) {
+        c.tile_n = 64;
+        c.stages = std::max(1, std::min(c.stages, max_stages(c.tile_m, 64, 1, d->wbits)));
+        c.smem_bytes = dyn_smem_bytes(c.tile_m, 64, 1, d->wbits, c.splits, c.stages);
+    }
     // Stacked parts (one 128-row tile holds every part's tokens): pe is the parts the tile's footprint counts.
     // forced tiles may stack whenever the shape allows; the table stacks where it chose to
     int pe = (forced ? stackable(d->m, d->parts, d->k) : use_stack(d->m, d->n, d->k, d->parts, g_devices[dev].sms))
@@ -1319,6 +1376,34 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     // two chunks when they fit the stages: the second lands while the first is expanded and multiplied
     const int chunks = oneshot && nkb_max >= 4 && 2 * ceil_div(nkb_max, 2) <= c.stages ? 2 : 1;
     const int kbox = oneshot ? ceil_div(nkb_max, chunks) : 1;
+    // The fused quantizer: one token tile of one part, the whole K (<= 1024, whole 128-blocks) in one shot, channel
+    // tiles in whole clusters of kFqCluster, unit-stride 16-byte-aligned input rows.
+    int fq_clusters = 0;
+    uint32_t fq_off = 0;
+    if (fq) {
+        const KeaQuantizeDesc *x = fq->q;
+        const int ctas_n = ceil_div(d->n, c.tile_n);
+        const bool shape_ok = oneshot && !stack && pe == 1 && d->parts == 1 && c.splits == 1 && tmb == 1 &&
+                              d->m <= kea::kBM && d->k % kea::kBK == 0 && d->k <= kea::kRowChunks * 128 &&
+                              ctas_n % kea::kFqCluster == 0;
+        bool rows_ok = x->xk == 1 && aligned16(x->x) && x->xt % 4 == 0 && (x->t == 1 || x->xb % 4 == 0) &&
+                       (!x->pre_norm_weight || (x->normed && aligned16(x->normed) && x->ld_normed % 4 == 0));
+        if (rows_ok && x->pre_norm_weight) {
+            // cluster 0 writes the pre-norm output while other clusters still read the input rows: not in place
+            const long long last = (long long)(d->m - 1) / x->t * x->xb + (long long)(x->t - 1) * x->xt + d->k;
+            const uintptr_t x0 = reinterpret_cast<uintptr_t>(x->x), x1 = x0 + (uintptr_t)last * 4;
+            const uintptr_t n0 = reinterpret_cast<uintptr_t>(x->normed);
+            const uintptr_t n1 = n0 + ((uintptr_t)(d->m - 1) * x->ld_normed + d->k) * 4;
+            if (x0 < n1 && n0 < x1) rows_ok = false;
+        }
+        fq_clusters = ctas_n / kea::kFqCluster;
+        fq_off = kFqParamOffset;
+        const bool room = c.stages * a_stage_bytes(c.tile_m, 1) >= 4 * d->k * 4;   // the activation region
+        if (!shape_ok || !rows_ok || !room || !fq->scratch || !aligned16(fq->scratch) ||
+            fq->scratch_bytes < fused_scratch_bytes(fq_clusters, d->k))
+            return kNotFused;
+        if (fq->dry_run) return KEA_OK;
+    }
     CUtensorMap qmap;
     const long long pstride = d->parts > 1 ? d->q_part_stride : (long long)d->m * d->ldq;
     // Rows past m only feed accumulator rows that are never stored, so a single token tile loads just the rows
@@ -1340,11 +1425,16 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
             return KEA_ERR_CUDA;
     } else if (q4d) {
         act_tx = (uint32_t)(d->parts * box_rows4 * kea::kBK);
-        const cuuint64_t dims[4] = {(cuuint64_t)kea::kBK, (cuuint64_t)d->m, (cuuint64_t)kb_total, (cuuint64_t)d->parts};
-        const cuuint64_t strides[3] = {(cuuint64_t)d->ldq, (cuuint64_t)kea::kBK, (cuuint64_t)std::max<long long>(pstride, 16)};
+        // fused: the clusters' scratch blocks [cluster][128 rows][K] stand in for q
+        const cuuint64_t rows = fq ? (cuuint64_t)fq_clusters * kea::kBM : (cuuint64_t)d->m;
+        const cuuint64_t ld = fq ? (cuuint64_t)d->k : (cuuint64_t)d->ldq;
+        void *src = fq ? fq->scratch : const_cast<int8_t *>(d->q);
+        const long long ps = fq ? (long long)rows * d->k : pstride;
+        const cuuint64_t dims[4] = {(cuuint64_t)kea::kBK, rows, (cuuint64_t)kb_total, (cuuint64_t)d->parts};
+        const cuuint64_t strides[3] = {ld, (cuuint64_t)kea::kBK, (cuuint64_t)std::max<long long>(ps, 16)};
         const cuuint32_t box[4] = {(cuuint32_t)kea::kBK, (cuuint32_t)box_rows4, (cuuint32_t)kbox, 1};
         const cuuint32_t estr[4] = {1, 1, 1, 1};
-        if (g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t *>(d->q), dims, strides, box, estr,
+        if (g_encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, src, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return KEA_ERR_CUDA;
@@ -1450,6 +1540,30 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     a.vec_y = aligned16(d->y) && ((d->ldy * esize) % 16 == 0);
     a.vec_acc = d->acc && aligned16(d->acc) && ((d->ld_acc * 4) % 16 == 0) && ((d->acc_part_stride * 4) % 16 == 0);
     a.err = d->error_word;
+    if (fq) {
+        const KeaQuantizeDesc *x = fq->q;
+        a.fq = 1;
+        a.fq_x = x->x;
+        a.fq_xb = x->xb;
+        a.fq_xt = x->xt;
+        a.fq_t = x->t;
+        a.fq_silu = (x->flags & KEA_QUANT_INPUT_SILU) ? 1 : 0;
+        a.fq_nw = x->norm_weight;
+        a.fq_nb = x->norm_bias;
+        a.fq_eps = x->eps;
+        a.fq_pnw = x->pre_norm_weight;
+        a.fq_pnb = x->pre_norm_bias;
+        a.fq_peps = x->pre_eps;
+        a.fq_off = fq_off;
+        a.fq_scr = static_cast<int8_t *>(fq->scratch);
+        a.fq_qs_scr = reinterpret_cast<float *>(static_cast<int8_t *>(fq->scratch) +
+                                                (size_t)fq_clusters * kea::kBM * d->k);
+        a.fq_q = const_cast<int8_t *>(d->q);
+        a.fq_qs = const_cast<float *>(d->qs);
+        a.fq_ldq = d->ldq;
+        a.fq_normed = x->pre_norm_weight ? x->normed : nullptr;
+        a.fq_ldn = x->ld_normed;
+    }
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ceil_div(d->n, c.tile_n),
@@ -1459,11 +1573,11 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     cfg.stream = (cudaStream_t)stream;
     cudaLaunchAttribute attrs[2];
     unsigned na = 0;
-    if (c.splits > 1) {
+    if (c.splits > 1 || fq) {
         attrs[na].id = cudaLaunchAttributeClusterDimension;
-        attrs[na].val.clusterDim.x = 1;
+        attrs[na].val.clusterDim.x = fq ? (unsigned)kea::kFqCluster : 1u;
         attrs[na].val.clusterDim.y = 1;
-        attrs[na].val.clusterDim.z = (unsigned)c.splits;
+        attrs[na].val.clusterDim.z = fq ? 1u : (unsigned)c.splits;
         ++na;
     }
     if (d->flags & KEA_FLAG_PDL) {
@@ -1487,6 +1601,88 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
         return KEA_ERR_CUDA;
     }
     return KEA_OK;
+}
+
+extern "C" {
+
+int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
+    const int v = validate_gemm(d);
+    if (v != KEA_OK || d->m == 0) return v;
+    int dev = 0;
+    const int st = device_setup(&dev, stream);
+    if (st != KEA_OK) return st;
+    Route route;
+    KeaGemmConfig c{};
+    SwapPlan sp;
+    const int rs = route_gemm(d, g_devices[dev].sms, &route, &c, &sp);
+    if (rs != KEA_OK) return rs;
+    if (route == kRouteGemv) return launch_gemv(d, c, stream);
+    if (route == kRouteSwap) return launch_swap(d, sp, stream);
+    if (route == kRoutePair) return launch_pair(d, c, g_devices[dev].sms, stream);
+    return launch_tile(d, c, dev, stream, nullptr);
+}
+
+size_t kea_lowbit_project_scratch_bytes(int32_t m, int32_t n, int32_t k, int32_t wbits, int32_t parts) {
+    (void)wbits;
+    if (m < 1 || m > kea::kBM || n < 1 || parts != 1 || k < 1 || k % kea::kBK || k > kea::kRowChunks * 128) return 0;
+    // at most one cluster per kFqCluster channel tiles of the narrowest (32-channel) tile
+    return fused_scratch_bytes(ceil_div(ceil_div(n, 32), kea::kFqCluster), k);
+}
+
+// The route kea_lowbit_project takes (fused 1: one fused kernel; 0: quantizer then GEMM) after its argument checks,
+// with the per-tile configuration and device the fused launch uses.
+static int project_route(const KeaProjectDesc *p, void *stream, int *fused, KeaGemmConfig *cfg, int *device) {
+    *fused = 0;
+    if (!p) return KEA_ERR_INVALID_VALUE;
+    const KeaGemmDesc *d = &p->gemm;
+    const KeaQuantizeDesc *x = &p->quant;
+    const int v = validate_gemm(d);
+    if (v != KEA_OK) return v;
+    const int vq = validate_quantize(x);
+    if (vq != KEA_OK) return vq;
+    if (p->flags & ~KEA_PROJECT_FUSE) return KEA_ERR_INVALID_VALUE;
+    // the quantizer's output is the GEMM's input
+    if (x->m != d->m || x->k != d->k || x->parts != d->parts || x->q != d->q || x->ldq != d->ldq || x->qs != d->qs ||
+        (d->parts > 1 && (x->q_part_stride != d->q_part_stride || x->qs_part_stride != d->qs_part_stride)))
+        return KEA_ERR_INVALID_VALUE;
+    if (d->m == 0) return KEA_OK;
+    int dev = 0;
+    const int st = device_setup(&dev, stream);
+    if (st != KEA_OK) return st;
+    Route route;
+    KeaGemmConfig c{};
+    SwapPlan sp;
+    const int rs = route_gemm(d, g_devices[dev].sms, &route, &c, &sp);
+    if (rs != KEA_OK) return rs;
+    if ((p->flags & KEA_PROJECT_FUSE) && route == kRouteTile && quant_unit_rows(x)) {
+        const FusedQuant fq{x, p->scratch, p->scratch_bytes, true};
+        *fused = launch_tile(d, c, dev, stream, &fq) == KEA_OK ? 1 : 0;
+    }
+    *cfg = c;
+    *device = dev;
+    return KEA_OK;
+}
+
+int kea_lowbit_project_fuses(const KeaProjectDesc *p) {
+    int fused = 0, dev = 0;
+    KeaGemmConfig c{};
+    const int st = project_route(p, nullptr, &fused, &c, &dev);
+    return st != KEA_OK ? -st : fused;
+}
+
+int kea_lowbit_project(const KeaProjectDesc *p, void *stream) {
+    int fused = 0, dev = 0;
+    KeaGemmConfig c{};
+    const int st = project_route(p, stream, &fused, &c, &dev);
+    if (st != KEA_OK || p->gemm.m == 0) return st;
+    if (fused) {
+        const FusedQuant fq{&p->quant, p->scratch, p->scratch_bytes, false};
+        const int r = launch_tile(&p->gemm, c, dev, stream, &fq);
+        if (r != kNotFused) return r;
+    }
+    const int q = kea_lowbit_quantize(&p->quant, stream);
+    if (q != KEA_OK) return q;
+    return kea_lowbit_gemm(&p->gemm, stream);
 }
 
 

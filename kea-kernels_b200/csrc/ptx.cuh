@@ -70,6 +70,8 @@ KEA_DEVI bool mbar_wait_sleep(uint32_t bar, uint32_t parity, long long budget, u
 KEA_DEVI void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 // Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA / tcgen05) accesses.
 KEA_DEVI void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// orders this thread's generic-proxy global accesses with later async-proxy (TMA) accesses
+KEA_DEVI void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // One lane of the (converged) warp gets true: elect.sync, which lets the compiler keep warp-uniform operands of the
 // elected lane's instructions in uniform registers.

@@ -19,13 +19,14 @@ OK, INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES, CUDA, NO_DEVICE, DEVIC
 OUT_F32, OUT_F16 = 0, 1
 FLAG_SILU, FLAG_ORDER1, FLAG_PDL, FLAG_NO_PAIR, FLAG_FORCE_PAIR = 1, 2, 4, 8, 16
 FLAG_FORCE_SWAP, FLAG_NO_SWAP, FLAG_TEST_STALL, FLAG_NO_RESIDENT_WEIGHTS = 32, 64, 128, 256
-QUANT_INPUT_SILU, QUANT_PDL = 1, 2
+QUANT_INPUT_SILU, QUANT_PDL, QUANT_NARROW_ROWS = 1, 2, 4
+PROJECT_FUSE = 1
 DEVERR_TIMEOUT, DEVERR_TAIL_BITS, DEVERR_TERNARY_11 = 1, 2, 4
 
 # Every symbol include/kea_lowbit.h declares.
 EXPORTS = ("kea_lowbit_gemm", "kea_lowbit_gemm_noalloc", "kea_lowbit_choose_config", "kea_lowbit_panel_bytes", "kea_lowbit_workspace_bytes",
            "kea_lowbit_prepare",
-           "kea_lowbit_quantize", "kea_lowbit_glu_depthwise", "kea_lowbit_rel_attention", "kea_lowbit_read_error",
+           "kea_lowbit_quantize", "kea_lowbit_project", "kea_lowbit_project_fuses", "kea_lowbit_project_scratch_bytes", "kea_lowbit_glu_depthwise", "kea_lowbit_rel_attention", "kea_lowbit_read_error",
            "kea_lowbit_status_string", "kea_lowbit_version")
 CONV_PDL, CONV_QUANT_SILU = 1, 2
 
@@ -62,6 +63,11 @@ class QuantizeDesc(ctypes.Structure):
         ("pre_norm_weight", ctypes.c_void_p), ("pre_norm_bias", ctypes.c_void_p), ("pre_eps", ctypes.c_float),
         ("normed", ctypes.c_void_p), ("ld_normed", ctypes.c_int64),
     ]
+
+
+class ProjectDesc(ctypes.Structure):
+    _fields_ = [("gemm", GemmDesc), ("quant", QuantizeDesc), ("scratch", ctypes.c_void_p),
+                ("scratch_bytes", ctypes.c_size_t), ("flags", ctypes.c_int32)]
 
 
 class ConvDesc(ctypes.Structure):
@@ -105,6 +111,12 @@ def lib() -> ctypes.CDLL:
         handle.kea_lowbit_prepare.restype = ctypes.c_int
         handle.kea_lowbit_quantize.argtypes = [ctypes.POINTER(QuantizeDesc), ctypes.c_void_p]
         handle.kea_lowbit_quantize.restype = ctypes.c_int
+        handle.kea_lowbit_project.argtypes = [ctypes.POINTER(ProjectDesc), ctypes.c_void_p]
+        handle.kea_lowbit_project.restype = ctypes.c_int
+        handle.kea_lowbit_project_fuses.argtypes = [ctypes.POINTER(ProjectDesc)]
+        handle.kea_lowbit_project_fuses.restype = ctypes.c_int
+        handle.kea_lowbit_project_scratch_bytes.argtypes = [ctypes.c_int32] * 5
+        handle.kea_lowbit_project_scratch_bytes.restype = ctypes.c_size_t
         handle.kea_lowbit_glu_depthwise.argtypes = [ctypes.POINTER(ConvDesc), ctypes.c_void_p]
         handle.kea_lowbit_glu_depthwise.restype = ctypes.c_int
         handle.kea_lowbit_rel_attention.argtypes = [ctypes.POINTER(AttentionDesc), ctypes.c_void_p]

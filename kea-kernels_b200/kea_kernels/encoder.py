@@ -57,17 +57,23 @@ class LowBitLinear(nn.Module):
         """x [B, T, K] (any strides) -> [B, T, N]; with `residual` ([B, T, N] contiguous FP32) the GEMM's epilogue
         returns residual + residual_scale * projection (the layer's skip connection, same roundings as unfused).
         `pre_norm`: a LayerNorm applied to x before `norm`, its output written to `normed` ([B, T, K] contiguous;
-        x itself allowed) - the previous layer's output norm folded into this quantizer."""
+        x itself allowed, which keeps the quantizer out of the GEMM kernel) - the previous layer's output norm folded
+        into this quantizer."""
         b, t, k = x.shape
         m = b * t
+        y = torch.empty(b, t, self.out_features, device=x.device, dtype=torch.float32)
         if m == 0:
-            return torch.empty(b, t, self.out_features, device=x.device, dtype=torch.float32)
-        # the quantizer launches plainly: with programmatic dependent launch its CTAs would sit on the SMs while the
-        # previous GEMM drains (measured slower on the clip); the GEMM after it does use it
-        q, qs, ldq = lowbit.quantize(x, (x.stride(0), x.stride(1), x.stride(2), t), m, k, self.parts, norm=norm,
-                                     input_silu=input_silu, pre_norm=pre_norm,
-                                     normed=None if normed is None else normed.view(m, k))
-        return self.from_quantized(q, qs, ldq, b, t, silu=silu, residual=residual, residual_scale=residual_scale)
+            return y
+        # one call: the library runs the quantizer inside the GEMM kernel where the shape allows, else the two
+        # kernels back to back (the quantizer launched plainly: with programmatic dependent launch its CTAs would
+        # sit on the SMs while the previous GEMM drains, measured slower on the clip; the GEMM after it does use it)
+        res = None if residual is None else residual.reshape(m, self.out_features)
+        lowbit.project(x, (x.stride(0), x.stride(1), x.stride(2), t), m, k, self.panels, self.wbits,
+                       self.out_features, self.scale, self.bias, y.view(m, self.out_features), parts=self.parts,
+                       norm=norm, input_silu=input_silu, pre_norm=pre_norm,
+                       normed=None if normed is None else normed.view(m, k), silu=silu, pdl=self.pdl, residual=res,
+                       residual_scale=residual_scale)
+        return y
 
     def from_quantized(self, q: Tensor, qs: Tensor, ldq: int, b: int, t: int, *, silu: bool = False,
                        residual: Tensor | None = None, residual_scale: float = 1.0) -> Tensor:
@@ -224,12 +230,12 @@ class ConformerLayer(nn.Module):
 
     def body(self, x: Tensor, lengths: Tensor | None = None, pre_norm: nn.LayerNorm | None = None) -> Tensor:
         """The layer without its output LayerNorm. `pre_norm` (the previous layer's output norm) is applied to x
-        inside FF1's quantizer, which writes the normalized rows back into x: the skip connection's input."""
+        inside FF1's quantizer, which writes the normalized rows out: the skip connection's input."""
         # every skip connection is added in the epilogue of the GEMM that ends its branch (x + 0.5 ff, x + att, ...)
-        if pre_norm is not None and not x.is_contiguous():
-            x = x.contiguous()
-        h = self.lin["ff1_up"](x, norm=self.norms["ff1"], silu=True, pre_norm=pre_norm,
-                               normed=x if pre_norm is not None else None)
+        xn = torch.empty_like(x, memory_format=torch.contiguous_format) if pre_norm is not None else None
+        h = self.lin["ff1_up"](x, norm=self.norms["ff1"], silu=True, pre_norm=pre_norm, normed=xn)
+        if xn is not None:
+            x = xn
         x = self.lin["ff1_down"](h, residual=x, residual_scale=0.5)
         x = self.attention(x, lengths)
         x = self.conv(x, lengths)

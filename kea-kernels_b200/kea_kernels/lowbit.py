@@ -50,21 +50,31 @@ def prepare_panels(codes: Tensor, wbits: int, n: int, k: int) -> Tensor:
 
 def quantize(x: Tensor, rows: tuple[int, int, int, int], m: int, k: int, parts: int, *, ldq: int | None = None,
              norm=None, input_silu: bool = False, pdl: bool = False, pre_norm=None,
-             normed: Tensor | None = None) -> tuple[Tensor, Tensor, int]:
+             normed: Tensor | None = None, narrow_rows: bool = False) -> tuple[Tensor, Tensor, int]:
     """x[m', kk] at x + (m' // T) * XB + (m' % T) * XT + kk * XK for rows = (XB, XT, XK, T) ->
     (q int8 [parts, m, ldq] zero-padded past k, qs FP32 [parts, m], ldq). pdl lets the kernel start while the
     previous kernel on the stream finishes (it waits for that kernel's results before reading x).
     `pre_norm` (a LayerNorm) is applied first and its output written to `normed` (FP32 [m, k] rows, unit stride; may
-    be x itself): a layer's output norm folded into the next projection's quantizer."""
+    be x itself): a layer's output norm folded into the next projection's quantizer. narrow_rows: as few threads per
+    row as registers allow (one warp up to K = 1024), the reduction order of project()'s fused quantizer."""
     _require_cuda(x, "x")
     if x.dtype != torch.float32:
         raise ValueError(f"expected FP32 input, got {x.dtype}")
-    xb, xt, xk, t = rows
     ldq = _round_up(k, 16) if ldq is None else ldq
     q = torch.empty(parts, m, ldq, device=x.device, dtype=torch.int8)
     qs = torch.empty(parts, m, device=x.device, dtype=torch.float32)
     if m == 0:
         return q, qs, ldq
+    d = _quant_desc(x, rows, m, k, parts, q, qs, ldq, norm=norm, input_silu=input_silu, pdl=pdl, pre_norm=pre_norm,
+                    normed=normed, narrow=narrow_rows)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().kea_lowbit_quantize(ctypes.byref(d), _lib.stream_handle(x.device)), "quantize")
+    return q, qs, ldq
+
+
+def _quant_desc(x: Tensor, rows, m: int, k: int, parts: int, q: Tensor, qs: Tensor, ldq: int, *, norm, input_silu,
+                pdl, pre_norm, normed, narrow) -> _lib.QuantizeDesc:
+    xb, xt, xk, t = rows
     d = _lib.QuantizeDesc()
     d.x, d.xb, d.xt, d.xk, d.t = x.data_ptr(), xb, xt, xk, max(t, 1)
     d.m, d.k, d.parts = m, k, parts
@@ -83,10 +93,9 @@ def quantize(x: Tensor, rows: tuple[int, int, int, int], m: int, k: int, parts: 
         d.pre_norm_bias = None if pre_norm.bias is None else pre_norm.bias.data_ptr()
         d.pre_eps = float(pre_norm.eps)
         d.normed, d.ld_normed = normed.data_ptr(), normed.stride(0)
-    d.flags = (_lib.QUANT_INPUT_SILU if input_silu else 0) | (_lib.QUANT_PDL if pdl else 0)
-    with torch.cuda.device(x.device):
-        _lib.check(_lib.lib().kea_lowbit_quantize(ctypes.byref(d), _lib.stream_handle(x.device)), "quantize")
-    return q, qs, ldq
+    d.flags = (_lib.QUANT_INPUT_SILU if input_silu else 0) | (_lib.QUANT_PDL if pdl else 0) \
+        | (_lib.QUANT_NARROW_ROWS if narrow else 0)
+    return d
 
 
 def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n: int, k: int, alpha: Tensor,
@@ -110,6 +119,20 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
     keeps the pair kernel re-expanding every tile's weights where it would keep them resident (one part, K <= 1024)."""
     if m == 0:
         return
+    d, keep = _gemm_desc(q, qs, ldq, m, panels, wbits, n, k, alpha, bias, y, parts=parts, silu=silu, order=order,
+                         acc=acc, config=config, pdl=pdl, error_word=error_word, pair=pair, force_pair=force_pair,
+                         residual=residual, residual_scale=residual_scale, workspace=workspace, swap=swap,
+                         wait_clocks=wait_clocks, test_stall=test_stall, resident_weights=resident_weights)
+    with torch.cuda.device(y.device):
+        _lib.check(_lib.lib().kea_lowbit_gemm(ctypes.byref(d), _lib.stream_handle(y.device)), "gemm")
+
+
+def _gemm_desc(q, qs, ldq, m, panels, wbits, n, k, alpha, bias, y, *, parts, silu=False, order=0, acc=None,
+               config=None, pdl=False, error_word=None, pair=True, force_pair=False, residual=None,
+               residual_scale=1.0, workspace=None, swap=True, wait_clocks=0, test_stall=False,
+               resident_weights=True):
+    """The C descriptor of gemm()'s arguments (checked), and the workspace tensor it points into (keep it alive
+    until the launch)."""
     if parts not in (1, 2, 3):
         raise ValueError(f"parts must be 1, 2 or 3, got {parts!r}")
     if order not in (0, 1):
@@ -170,8 +193,48 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
         if workspace.device != y.device or not workspace.is_contiguous():
             raise ValueError("workspace must be a contiguous tensor on y's device")
         d.workspace, d.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    return d, workspace
+
+
+def project(x: Tensor, rows: tuple[int, int, int, int], m: int, k: int, panels: Tensor, wbits: int, n: int,
+            alpha: Tensor, bias: Tensor | None, y: Tensor, *, parts: int, norm=None, input_silu: bool = False,
+            pre_norm=None, normed: Tensor | None = None, ldq: int | None = None, quant_pdl: bool = False,
+            fuse: bool = False, require_fused: bool = False, **gemm_options) -> tuple[Tensor, Tensor, int]:
+    """quantize() then gemm() in one call (the reference's Int8MmaLayer.project): x rows as quantize() takes them ->
+    y[:m] with gemm()'s epilogue options (silu, residual, acc, pdl, ...). By default the two kernels run back to back
+    (quantize with quant_pdl, then the GEMM; the faster form measured on B200). fuse=True asks for one kernel whose
+    thread-block clusters quantize the rows themselves where the shape allows (one part, 33 <= m <= 128, k a
+    multiple of 128 up to 1024: one warp a row, quantize(..., narrow_rows=True)'s arithmetic, bit for bit);
+    require_fused=True demands it (ValueError where it does not apply). Returns the parts it multiplied
+    (q int8 [parts, m, ldq], qs FP32 [parts, m], ldq)."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.float32:
+        raise ValueError(f"expected FP32 input, got {x.dtype}")
+    ldq = _round_up(k, 16) if ldq is None else ldq
+    q = torch.empty(parts, m, ldq, device=x.device, dtype=torch.int8)
+    qs = torch.empty(parts, m, device=x.device, dtype=torch.float32)
+    if m == 0:
+        return q, qs, ldq
+    pd = _lib.ProjectDesc()
+    pd.quant = _quant_desc(x, rows, m, k, parts, q, qs, ldq, norm=norm, input_silu=input_silu, pdl=quant_pdl,
+                           pre_norm=pre_norm, normed=normed, narrow=False)
+    g, keep = _gemm_desc(q, qs, ldq, m, panels, wbits, n, k, alpha, bias, y, parts=parts, **gemm_options)
+    pd.gemm = g
+    fuse = fuse or require_fused
+    pd.flags = _lib.PROJECT_FUSE if fuse else 0
+    need = _lib.lib().kea_lowbit_project_scratch_bytes(m, n, k, wbits, parts) if fuse else 0
+    scratch = torch.empty(need, dtype=torch.uint8, device=x.device) if need else None
+    if scratch is not None:
+        pd.scratch, pd.scratch_bytes = scratch.data_ptr(), need
     with torch.cuda.device(y.device):
-        _lib.check(_lib.lib().kea_lowbit_gemm(ctypes.byref(d), _lib.stream_handle(y.device)), "gemm")
+        if require_fused:
+            route = _lib.lib().kea_lowbit_project_fuses(ctypes.byref(pd))
+            if route < 0:
+                _lib.check(-route, "project")
+            if route != 1:
+                raise ValueError("the fused quantizer does not apply to this projection")
+        _lib.check(_lib.lib().kea_lowbit_project(ctypes.byref(pd), _lib.stream_handle(y.device)), "project")
+    return q, qs, ldq
 
 
 def glu_depthwise(h: Tensor, weight: Tensor, bias: Tensor | None = None, lengths: Tensor | None = None, *,

@@ -1,7 +1,8 @@
 """Accumulator parity of a whole clip: one synthetic 10 s clip (log-mel N(0, 1) [1, 128, 1000] ->
 125 encoder frames) through the 24-layer random-init 1-bit FastConformer. Every low-bit GEMM the clip issues - 8 per
 layer at M = 125 (fused QKV, out, 2 x FF up, 2 x FF down, conv pw1, pw2) plus linear_pos at M = 249, 216 in all - is
-recorded with its INT8 parts and scales (the quantizer's output, as the GEMM consumed them) and its INT32
+recorded with its INT8 parts and scales (the quantizer's output as the GEMM consumed them: from the quantizer inside
+the GEMM kernel where the library fuses it, from the conv kernel for pw2, else from the quantizer kernel) and its INT32
 accumulators, and checked on the host:
   * the accumulators equal the reference's exact integer product of those parts and the layer's codes bit for bit
     (its GPU test oracle `_exact_epilogue`, tests/test_kernels_gpu.py:23-27, restated by the oracle and pinned to the
@@ -45,7 +46,21 @@ def test_config2_clip_accumulators_are_bit_exact(monkeypatch):
         records.append(dict(panels=panels.data_ptr(), q=q[:, :m, :k].clone(), qs=qs[:, :m].clone(), acc=acc,
                             y=y[:m, :n].clone(), res=res, scale=residual_scale, silu=silu))
 
+    real_project = lowbit.project
+
+    def recording_project(x, rows, m, k, panels, wbits, n, alpha, bias, y, *, parts, silu=False, residual=None,
+                          residual_scale=1.0, **kw):
+        assert kw.get("acc") is None
+        acc = torch.empty(parts, m, n, dtype=torch.int32, device=y.device)
+        res = None if residual is None else residual[:m, :n].clone()
+        q, qs, ldq = real_project(x, rows, m, k, panels, wbits, n, alpha, bias, y, parts=parts, silu=silu, acc=acc,
+                                  residual=residual, residual_scale=residual_scale, **kw)
+        records.append(dict(panels=panels.data_ptr(), q=q[:, :m, :k].clone(), qs=qs[:, :m].clone(), acc=acc,
+                            y=y[:m, :n].clone(), res=res, scale=residual_scale, silu=silu))
+        return q, qs, ldq
+
     monkeypatch.setattr(lowbit, "gemm", recording_gemm)
+    monkeypatch.setattr(lowbit, "project", recording_project)
     mel = torch.randn(1, 128, 1000, generator=torch.Generator().manual_seed(2)).to(DEV)
     out = enc(mel)
     torch.cuda.synchronize()

@@ -163,6 +163,31 @@ def test_quantizer_pre_norm_argument_errors_are_reported_before_any_device_work(
     assert lib.kea_lowbit_quantize(ctypes.byref(_qdesc(**pre, xt=1, xk=125)), None) == _lib.UNSUPPORTED
 
 
+def test_project_argument_errors_are_reported_before_any_device_work():
+    lib = _lib.lib()
+    p = _lib.ProjectDesc()
+    p.gemm = _desc()
+    p.quant = _qdesc(m=p.gemm.m, k=p.gemm.k, q=p.gemm.q, ldq=p.gemm.ldq, qs=p.gemm.qs,
+                     q_part_stride=p.gemm.q_part_stride, qs_part_stride=p.gemm.qs_part_stride)
+    assert lib.kea_lowbit_project(None, None) == _lib.INVALID_VALUE
+    p.flags = 2                                                    # unknown flag
+    assert lib.kea_lowbit_project(ctypes.byref(p), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_project_fuses(ctypes.byref(p)) == -_lib.INVALID_VALUE
+    p.flags = _lib.PROJECT_FUSE
+    p.quant.qs = p.gemm.qs + 64                                    # the quantizer's output is not the GEMM's input
+    assert lib.kea_lowbit_project(ctypes.byref(p), None) == _lib.INVALID_VALUE
+    p.quant.qs = p.gemm.qs
+    p.quant.m = p.gemm.m + 1
+    assert lib.kea_lowbit_project(ctypes.byref(p), None) == _lib.INVALID_VALUE
+    p.quant.m = p.gemm.m
+    p.quant.flags = 64                                             # the quantizer's own checks apply
+    assert lib.kea_lowbit_project(ctypes.byref(p), None) == _lib.INVALID_VALUE
+    # the fused form's scratch: one part, M <= 128, K a multiple of 128 up to 1024
+    assert lib.kea_lowbit_project_scratch_bytes(125, 4096, 1024, 1, 1) == 16 * 128 * (1024 + 4)
+    for shape in ((129, 4096, 1024, 1, 1), (125, 4096, 1024, 1, 2), (125, 4096, 1000, 1, 1), (125, 1024, 4096, 1, 1)):
+        assert lib.kea_lowbit_project_scratch_bytes(*shape) == 0, shape
+
+
 def test_fused_conv_quantizer_argument_errors_are_reported_before_any_device_work():
     lib = _lib.lib()
 
