@@ -4,7 +4,8 @@ The reference's CPU arithmetic for the low-bit GEMM path is its own Python:
   * bits.pack_signs / bits.unpack_signs (src/kea_kernels/binary/bits.py:41-64),
   * formats.pack_ternary / formats.unpack_ternary (src/kea_kernels/formats.py:62-81),
   * the GPU test's oracle `_exact_epilogue` (tests/test_kernels_gpu.py:23-27): integer accumulators from an int64
-    matmul of the unpacked codes, then sum_c acc_c * s_c * alpha in FP64.
+    matmul of the unpacked codes, then sum_c acc_c * s_c * alpha in FP64;
+  * kernels.relayout (src/kea_kernels/binary/kernels.py:726-742), the fragment layout its b1_dot kernels read.
 This script imports exactly those functions, draws seeded inputs the way the reference's tests do
 (tests/test_kernels_gpu.py:16-20: torch.Generator().manual_seed, signs with p = 0.5), and stores codes, activations,
 scales, the reference's int64 accumulators and its FP64 outputs. The oracle (oracle/kea_oracle.py) is checked
@@ -75,6 +76,12 @@ def main(root: Path) -> None:
     out["rt_sign_signs"], out["rt_sign_codes"] = s.numpy(), bits.pack_signs(s).numpy()
     t = torch.randint(-1, 2, (4, 13), generator=g, dtype=torch.int8)
     out["rt_ternary_values"], out["rt_ternary_codes"] = t.numpy(), formats.pack_ternary(t).numpy()
+    # The reference's mma fragment layout of sign bits (src/kea_kernels/binary/kernels.py:726-742), which its own
+    # b1_dot kernels read: ragged N and K (padding), pinning oracle/ref_kernels.py's restatement.
+    from kea_kernels.binary import kernels as ref_kernels  # noqa: E402  (the reference package)
+    lay = torch.where(torch.rand(20, 300, generator=g) < 0.5, -1, 1).to(torch.int8)
+    out["relayout_signs"] = lay.numpy()
+    out["relayout_words"] = ref_kernels.relayout((lay > 0).to(torch.uint8)).numpy()
 
     names = []
     for name, wbits, n, k, m, parts, has_bias in CASES:
