@@ -38,7 +38,9 @@ COLD_BYTES = 512 << 20                   # per (wbits, N, K): distinct weights s
 L2_BYTES = 126 << 20
 # dram__bytes_read.sum + dram__bytes_write.sum of one cold launch, from the committed ncu captures of those cases
 # (keyed by (wbits, N, K, M)); None for a case without a capture.
-NCU_TRAFFIC = {(2, 4096, 1024, 8192): 9_578_752 + 15_821_312, (1, 4096, 1024, 125): 738_816}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu captures (profiles/): the
+# weight-stationary pair kernel at N 4096, K 1024, M 8192 (1-bit), the per-tile kernel at M 125
+NCU_TRAFFIC = {(1, 4096, 1024, 8192): 9_068_032 + 18_014_208, (1, 4096, 1024, 125): 738_816}
 
 
 def ops(m, n, k, parts=1):
@@ -385,7 +387,8 @@ def main() -> None:
         roofline = {"bound": "tensor", "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
                     "frac": achieved / tensor_peak,
                     "traffic": NCU_TRAFFIC.get((share["wbits"], share["n"], share["k"], share["m"])),
-                    "kernel": f"lowbit_gemm_pair_kernel<{share['wbits']}> M={share['m']} N={share['n']} K={share['k']}",
+                    "kernel": (f"lowbit_gemm_pair_ws_kernel<{share['wbits']}>" if share["k"] <= 1024 else
+                               f"lowbit_gemm_pair_kernel<{share['wbits']}, 1>") + f" M={share['m']} N={share['n']} K={share['k']}",
                     "peak_kind": int8_kind or f"2 x bf16 ({peak_kind})",
                     "note": "INT8 ops/s; peak = dense INT8 measured with torch._int_mm 8192^3 on this GPU"}
     else:
