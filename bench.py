@@ -38,9 +38,11 @@ COLD_BYTES = 512 << 20                   # per (wbits, N, K): distinct weights s
 L2_BYTES = 126 << 20
 # dram__bytes_read.sum + dram__bytes_write.sum of one cold launch, from the committed ncu captures of those cases
 # (keyed by (wbits, N, K, M)); None for a case without a capture.
-# dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu captures (profiles/): the
-# weight-stationary pair kernel at N 4096, K 1024, M 8192 (1-bit), the per-tile kernel at M 125
-NCU_TRAFFIC = {(1, 4096, 1024, 8192): 9_068_032 + 18_014_208, (1, 4096, 1024, 125): 738_816}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu captures (profiles/): the M = 8192
+# cases that can be a step's longest (pair kernels, weight-stationary at K 1024), the per-tile kernel at M 125
+NCU_TRAFFIC = {(1, 4096, 1024, 8192): 9_068_032 + 18_014_208, (2, 4096, 1024, 8192): 9_599_232 + 15_053_568,
+               (1, 1024, 4096, 8192): 34_213_632 + 245_504, (2, 1024, 4096, 8192): 34_738_688 + 207_360,
+               (1, 4096, 1024, 125): 738_816}
 
 
 def ops(m, n, k, parts=1):
