@@ -56,7 +56,8 @@ enum {
     KEA_FLAG_FORCE_PAIR = 16,   /* the pair kernel wherever its shape allows (1-2 parts, N % 256 == 0, m > 256,
                                    k <= 32768), also where the table would take the per-tile kernel */
     KEA_FLAG_FORCE_SWAP = 32,   /* the small-M swapped-operand kernel (weights on the MMA's M axis, tokens on N) at any
-                                   shape; `splits` / `stages` (0: the table's) then apply to it, tile_m / tile_n must be 0 */
+                                   shape; `tile_m` (its token tile: a multiple of 16 up to 256 / parts), `splits` and
+                                   `stages` (0: the table's) then apply to it; tile_n must be 0 */
     KEA_FLAG_NO_SWAP = 64,      /* keep the table off the swapped-operand kernel (128-token tiles run instead) */
     KEA_FLAG_TEST_STALL = 128,  /* tests only, with KEA_FLAG_FORCE_SWAP: the kernel's producer issues no activation
                                    copy, so its MMA warp's bounded wait runs out (see wait_clocks), the kernel reports

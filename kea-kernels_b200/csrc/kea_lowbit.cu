@@ -359,6 +359,13 @@ void swap_tokens(int m, int parts, int *mt, int *tiles) {
     *tiles = ceil_div(std::max(m, 1), swap_max_tokens(parts));
     *mt = round_up(ceil_div(std::max(m, 1), *tiles), 16);
 }
+// A caller's token tile (a multiple of 16 up to swap_max_tokens): tiles of mt tokens, the last one ragged.
+bool swap_tokens_forced(int m, int parts, int forced_mt, int *mt, int *tiles) {
+    if (forced_mt % 16 || forced_mt < 16 || forced_mt > swap_max_tokens(parts)) return false;
+    *mt = forced_mt;
+    *tiles = ceil_div(std::max(m, 1), forced_mt);
+    return true;
+}
 // Per stage: the activation box (every part's tokens x 128 k), the expanded weights (128 rows x 128 k), the codes.
 int swap_stage_bytes(int rows, int wbits) { return rows * kea::kBK + (int)kea::kSwapWTile + wbits * kea::kPanelSubBytes; }
 // Split-K receive buffer: [peer slot (splits - 1)][owned unit][part][4 token quarters][32 channels] x 16 bytes.
@@ -377,13 +384,19 @@ struct SwapPlan {
 constexpr int kSwapStaging = kea::kSwapEpiWarps * kea::kSwapStagingBytes;
 int swap_epilogue_bytes(int recv) { return round_up(recv, 1024) + kSwapStaging; }
 
-// The swap kernel's plan for a shape. forced_splits / forced_stages 0 take the table's choice: K split over a cluster
-// (<= 8 CTAs) until the channel tiles x token tiles x splits approach the SM count; as many stages as the CTA's
-// k-blocks, while two CTAs still fit on an SM. False when a forced plan does not fit.
-bool swap_plan(int m, int n, int k, int wbits, int parts, int sms, int forced_splits, int forced_stages, SwapPlan *out) {
+// The swap kernel's plan for a shape. forced_splits / forced_stages / forced_mt 0 take the table's choice: K split over
+// a cluster (<= 8 CTAs) until the channel tiles x token tiles x splits approach the SM count; as many stages as the
+// CTA's k-blocks, while two CTAs still fit on an SM; the fewest equal token tiles. False when a forced plan does not
+// fit.
+bool swap_plan(int m, int n, int k, int wbits, int parts, int sms, int forced_splits, int forced_stages, SwapPlan *out,
+               int forced_mt = 0) {
     if (k > 32768) return false;   // |acc| <= 127 K < 2^22: the epilogue's exact two-operation INT32 -> FP32 conversion
     SwapPlan p;
-    swap_tokens(m, parts, &p.mt, &p.token_tiles);
+    if (forced_mt) {
+        if (!swap_tokens_forced(m, parts, forced_mt, &p.mt, &p.token_tiles)) return false;
+    } else {
+        swap_tokens(m, parts, &p.mt, &p.token_tiles);
+    }
     p.rows = parts * p.mt;
     const int kb = ceil_div(k, kea::kBK);
     const int tiles = ceil_div(n, kea::kPanelN) * p.token_tiles;
@@ -778,8 +791,9 @@ int validate_gemm(const KeaGemmDesc *d) {
                      KEA_FLAG_FORCE_SWAP | KEA_FLAG_NO_SWAP | KEA_FLAG_TEST_STALL | KEA_FLAG_NO_RESIDENT_WEIGHTS))
         return KEA_ERR_INVALID_VALUE;
     if ((d->flags & KEA_FLAG_NO_PAIR) && (d->flags & KEA_FLAG_FORCE_PAIR)) return KEA_ERR_INVALID_VALUE;
+    // forced swap: tile_m is its token tile (0, or a multiple of 16), tile_n unused
     if ((d->flags & KEA_FLAG_FORCE_SWAP) &&
-        (d->tile_m || d->tile_n || (d->flags & (KEA_FLAG_NO_SWAP | KEA_FLAG_FORCE_PAIR))))
+        (d->tile_m % 16 || d->tile_m < 0 || d->tile_n || (d->flags & (KEA_FLAG_NO_SWAP | KEA_FLAG_FORCE_PAIR))))
         return KEA_ERR_INVALID_VALUE;
     if ((d->flags & KEA_FLAG_TEST_STALL) && !(d->flags & KEA_FLAG_FORCE_SWAP)) return KEA_ERR_INVALID_VALUE;
     if (d->wait_clocks < 0) return KEA_ERR_INVALID_VALUE;
@@ -791,8 +805,9 @@ enum Route { kRouteGemv, kRoutePair, kRouteSwap, kRouteTile };
 
 int route_gemm(const KeaGemmDesc *d, int sms, Route *route, KeaGemmConfig *c, SwapPlan *sp) {
     const bool forced = d->tile_m || d->tile_n || d->splits || d->stages;
-    if (d->flags & KEA_FLAG_FORCE_SWAP) {   // splits / stages (0: the table's) apply to the swap kernel
-        if (!swap_plan(d->m, d->n, d->k, d->wbits, d->parts, sms, d->splits, d->stages, sp)) return KEA_ERR_UNSUPPORTED;
+    if (d->flags & KEA_FLAG_FORCE_SWAP) {   // token tile / splits / stages (0: the table's) apply to the swap kernel
+        if (!swap_plan(d->m, d->n, d->k, d->wbits, d->parts, sms, d->splits, d->stages, sp, d->tile_m))
+            return KEA_ERR_UNSUPPORTED;
         *route = kRouteSwap;
         return KEA_OK;
     }

@@ -53,7 +53,7 @@ class DotConfig:
                 raise ValueError(f"invalid config {self}")
             return
         if self.kernel == SWAP:
-            if not (1 <= self.splits <= 16 and 1 <= self.stages <= 8):
+            if not (1 <= self.splits <= 16 and 1 <= self.stages <= 8 and self.tile_m % 16 == 0 and self.tile_m >= 0):
                 raise ValueError(f"invalid config {self}")
             return
         if not (self.tile_m in (128, 256) and self.tile_n in (32, 64, 128, 256) and 1 <= self.splits <= 16

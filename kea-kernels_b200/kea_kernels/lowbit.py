@@ -177,9 +177,9 @@ def _gemm_desc(q, qs, ldq, m, panels, wbits, n, k, alpha, bias, y, *, parts, sil
         | (0 if swap else _lib.FLAG_NO_SWAP) | (_lib.FLAG_TEST_STALL if test_stall else 0) \
         | (0 if resident_weights else _lib.FLAG_NO_RESIDENT_WEIGHTS)
     kernel = getattr(config, "kernel", 0) if config is not None else None
-    if kernel == 3:   # the swap kernel with this config's split and stages
+    if kernel == 3:   # the swap kernel with this config's token tile, split and stages (0: the table's)
         d.flags |= _lib.FLAG_FORCE_SWAP
-        d.splits, d.stages = config.splits, config.stages
+        d.tile_m, d.splits, d.stages = config.tile_m, config.splits, config.stages
     elif config is not None and kernel != 1:   # a pair config from the table forces nothing
         d.tile_m, d.tile_n, d.splits, d.stages = config.tile_m, config.tile_n, config.splits, config.stages
     d.wait_clocks = int(wait_clocks)

@@ -123,7 +123,8 @@ def test_c_abi_argument_errors_are_reported_before_any_device_work():
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(ldq=1032, k=1030)), None) == _lib.ALIGNMENT  # ldq % 16
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=512)), None) == _lib.INVALID_VALUE
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_TEST_STALL)), None) == _lib.INVALID_VALUE
-    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_FORCE_SWAP, tile_m=128)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_FORCE_SWAP, tile_m=100)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_FORCE_SWAP, tile_n=32)), None) == _lib.INVALID_VALUE
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_FORCE_SWAP | _lib.FLAG_NO_SWAP)), None) == \
         _lib.INVALID_VALUE
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(wait_clocks=-1)), None) == _lib.INVALID_VALUE

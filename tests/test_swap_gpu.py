@@ -54,6 +54,23 @@ def test_token_tiles(wbits, parts, m, splits, flags):
 
 
 @pytest.mark.parametrize("wbits", [1, 2])
+@pytest.mark.parametrize("parts,m", [(1, 125), (3, 38), (2, 64)])
+@pytest.mark.parametrize("tile,splits", [(16, 1), (16, 4), (32, 2), (48, 1)])
+def test_forced_token_tiles(wbits, parts, m, tile, splits):
+    """A caller's token tile (a multiple of 16; the last tile ragged) with or without a K split gives the oracle's
+    bits: the grid's token-tile axis, out-of-range rows of the last tile read as zero and clipped on store."""
+    n, k = 384, 1024
+    seed = wbits * 7 + parts * 11 + m + tile + splits
+    codes, w = _codes(wbits, n, k, seed)
+    q, qs = _activations(parts, m, k, seed)
+    alpha, bias = _channel(n, seed, True)
+    y, acc = _run(codes, wbits, n, k, q, qs, alpha, bias,
+                  config=configs.DotConfig(tile, 128, splits, 0, configs.SWAP))
+    want, want_acc = oracle.reference(q, qs, w, alpha, bias)
+    _check(y, acc, want, want_acc, 0)
+
+
+@pytest.mark.parametrize("wbits", [1, 2])
 @pytest.mark.parametrize("n,k,m,parts", [(5, 300, 3, 2), (200, 21, 7, 1), (130, 4097, 1, 1), (129, 129, 129, 3),
                                          (1, 128, 33, 1), (300, 1000, 250, 1), (4096, 1024, 125, 1)])
 @pytest.mark.parametrize("splits", [1, 3])
