@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define KEA_LOWBIT_VERSION 4
+#define KEA_LOWBIT_VERSION 5
 
 /* Status codes. The Python layer maps 1-4 to ValueError and 5-8 to RuntimeError, as the reference raises
  * ValueError for argument errors (src/kea_kernels/binary/layer.py:66-78,188-189) and RuntimeError for a failed
@@ -62,8 +62,13 @@ enum {
     KEA_FLAG_TEST_STALL = 128,  /* tests only, with KEA_FLAG_FORCE_SWAP: the kernel's producer issues no activation
                                    copy, so its MMA warp's bounded wait runs out (see wait_clocks), the kernel reports
                                    KEA_DEVERR_TIMEOUT and returns; the output is left undefined */
-    KEA_FLAG_NO_RESIDENT_WEIGHTS = 256   /* the pair kernel re-expands the weights of every tile it visits, also where
+    KEA_FLAG_NO_RESIDENT_WEIGHTS = 256,  /* the pair kernel re-expands the weights of every tile it visits, also where
                                             (one part, K <= 1024) it would keep a channel tile's weights resident */
+    KEA_FLAG_FORCE_REG = 512,   /* the small-M register-operand kernel (warp-level MMAs, weights expanded in registers) at
+                                   any shape; `tile_n` (channels per CTA: 16, 32, 64 or 128), `tile_m` (activation rows
+                                   per CTA, tokens x parts: 16 or 32) and `splits` (K-slices among its 8 warps: 1, 2, 4
+                                   or 8) then apply to it (0: the table's); stages must be 0 */
+    KEA_FLAG_NO_REG = 1024      /* keep the table off the register-operand kernel (its tcgen05 choice runs instead) */
 };
 
 /* Device error word bits (written by kernels into `error_word`, or into the library's own device word). */
@@ -140,7 +145,9 @@ typedef struct KeaGemmConfig {
     int32_t kernel;           /* 0: the per-tile tcgen05 kernel; 1: the persistent CTA-pair kernel (tcgen05
                                  cta_group::2, 256 x 256 tiles per pair of SMs, double-buffered accumulators); 2: the
                                  CUDA-core kernel for M <= 16 (tile_n = channels per CTA); 3: the small-M swapped-operand
-                                 kernel (tile_m = tokens per token tile, tile_n = 128 channels, splits = cluster along K) */
+                                 kernel (tile_m = tokens per token tile, tile_n = 128 channels, splits = cluster along K);
+                                 4: the small-M register-operand kernel (tile_m = activation rows per CTA, tile_n =
+                                 channels per CTA, splits = K-slices among its warps) */
 } KeaGemmConfig;
 
 int kea_lowbit_gemm(const KeaGemmDesc *desc, void *stream);

@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(kAttnThreads * KG) rel_attention_kernel(const 
     for (int e = threadIdx.x; e < kAttnQ * V4; e += kAttnThreads * KG) {
         const int r = e / V4, c4 = e - r * V4, i = i0 + r;
         float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < T) q = __ldg(reinterpret_cast<const float4 *>(qkv_b + (long long)i * row3 + (long long)h * DK) + c4);
+        if (i < T) q = reinterpret_cast<const float4 *>(qkv_b + (long long)i * row3 + (long long)h * DK)[c4];
         const float4 u = __ldg(reinterpret_cast<const float4 *>(a.bias_u + h * DK) + c4);
         const float4 v = __ldg(reinterpret_cast<const float4 *>(a.bias_v + h * DK) + c4);
         *reinterpret_cast<float4 *>(Qu + r * LD + 4 * c4) =
@@ -110,8 +110,8 @@ __global__ void __launch_bounds__(kAttnThreads * KG) rel_attention_kernel(const 
             float4 kk = make_float4(0.f, 0.f, 0.f, 0.f), vv = kk;
             if (j < T) {
                 const float *src = qkv_b + (long long)j * row3 + (long long)h * DK;
-                kk = __ldg(reinterpret_cast<const float4 *>(src + (long long)H * DK) + c4);
-                vv = __ldg(reinterpret_cast<const float4 *>(src + 2LL * H * DK) + c4);
+                kk = reinterpret_cast<const float4 *>(src + (long long)H * DK)[c4];
+                vv = reinterpret_cast<const float4 *>(src + 2LL * H * DK)[c4];
             }
             *reinterpret_cast<float4 *>(Ks + swz<DK>(r, c4)) = kk;
             *reinterpret_cast<float4 *>(Vs + r * LD + 4 * c4) = vv;
@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(kAttnThreads * KG) rel_attention_kernel(const 
             const int s = e / V4, c4 = e - s * V4, pr = rel0 + s + T - 1;
             float4 pp = make_float4(0.f, 0.f, 0.f, 0.f);
             if (pr >= 0 && pr < 2 * T - 1)
-                pp = __ldg(reinterpret_cast<const float4 *>(a.pos + ((long long)pr * H + h) * DK) + c4);
+                pp = reinterpret_cast<const float4 *>(a.pos + ((long long)pr * H + h) * DK)[c4];
             *reinterpret_cast<float4 *>(Ps + swz<DK>(s, c4)) = pp;
         }
         __syncthreads();

@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_regs_kernel(const Quan
 #pragma unroll
     for (int c = 0; c < C; ++c) {
         const int i = c * tpr + gt;
-        v[c] = (live && 4 * i < K) ? __ldg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[c] = (live && 4 * i < K) ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (a.pnw) {
         layer_norm_regs<C, PRE>(v, K, tpr, gt, scratch, a.pnw, a.pnb, a.peps, pw, pb);
@@ -302,10 +302,10 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantArgs
                 const float4 *s4 = reinterpret_cast<const float4 *>(src);
                 float4 *d4 = reinterpret_cast<float4 *>(dst);
 #pragma unroll 4
-                for (int i = gt; i < K / 4; i += tpr) d4[i] = __ldg(s4 + i);
+                for (int i = gt; i < K / 4; i += tpr) d4[i] = s4[i];
             } else {
 #pragma unroll 4
-                for (int k = gt; k < K; k += tpr) dst[k] = __ldg(src + k);
+                for (int k = gt; k < K; k += tpr) dst[k] = src[k];
             }
         }
     } else {
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantArgs
             const float *src = bases[r];
             float *dst = xrows + r * K;
 #pragma unroll 4
-            for (int k = k0; k < K; k += per) dst[k] = __ldg(src + (long long)k * a.xk);
+            for (int k = k0; k < K; k += per) dst[k] = src[(long long)k * a.xk];
         }
     }
     __syncthreads();

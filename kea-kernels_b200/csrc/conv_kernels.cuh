@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(kConvThreads) glu_depthwise_kernel(const ConvA
     float win[KW];   // win[j] = g at frame t - H + j for the output frame t being formed
     auto glu = [&](int t) -> float {
         if (t < 0 || t >= live) return 0.f;
-        const float x = __ldg(hb + (long long)t * row2 + c), gate = __ldg(hb + (long long)t * row2 + a.C + c);
+        const float x = hb[(long long)t * row2 + c], gate = hb[(long long)t * row2 + a.C + c];
         return __fmul_rn(x, __frcp_rn(__fadd_rn(1.0f, expf(-gate))));
     };
 #pragma unroll
@@ -114,8 +114,8 @@ __global__ void __launch_bounds__(kConvQThreads) glu_depthwise_quant_kernel(cons
     for (int i = 0; i < W; ++i) {
         const int t = t0 - H + i;
         const bool in = has && t >= 0 && t < live;
-        xv[i] = in ? __ldg(reinterpret_cast<const float4 *>(hb + (long long)t * row2 + c0)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        gv[i] = in ? __ldg(reinterpret_cast<const float4 *>(hb + (long long)t * row2 + C + c0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        xv[i] = in ? *reinterpret_cast<const float4 *>(hb + (long long)t * row2 + c0) : make_float4(0.f, 0.f, 0.f, 0.f);
+        gv[i] = in ? *reinterpret_cast<const float4 *>(hb + (long long)t * row2 + C + c0) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float g[W][4];   // GLU values; zero outside the clip's live frames (as glu_depthwise_kernel)
 #pragma unroll

@@ -241,7 +241,7 @@ KEA_DEVI void finish_store(const GemmArgs &a, int t, int n, int c, const int (&a
         const float *r = a.res + (long long)t * a.ld_res + n;
 #pragma unroll
         for (int j = 0; j < CNT; ++j)
-            if (full || n + j < a.N) v[j] = __fadd_rn(__ldg(r + j), __fmul_rn(a.res_scale, v[j]));
+            if (full || n + j < a.N) v[j] = __fadd_rn(r[j], __fmul_rn(a.res_scale, v[j]));
     }
     const long long off = (long long)t * a.ldy + n;
     if (a.y_f16) {
@@ -352,7 +352,7 @@ KEA_DEVI void fused_quantize_rows(const GemmArgs &a, int w, int lane, const floa
 #pragma unroll
     for (int c = 0; c < kRowChunks; ++c) {
         const int i = c * 32 + lane;
-        v[c] = 4 * i < K ? __ldg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[c] = 4 * i < K ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     const bool first = cid == 0;
     if (a.fq_pnw) {

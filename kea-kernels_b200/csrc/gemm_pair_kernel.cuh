@@ -165,7 +165,7 @@ KEA_DEVI void pair_finish_chunk2(uint32_t (&lo)[32], const uint32_t (&hi)[32], u
 KEA_DEVI void pair_add_residual(uint32_t (&v)[32], const float *row, float scale) {
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-        const float4 r = __ldg(reinterpret_cast<const float4 *>(row) + q);
+        const float4 r = reinterpret_cast<const float4 *>(row)[q];
         v[4 * q] = __float_as_uint(__fadd_rn(r.x, __fmul_rn(scale, __uint_as_float(v[4 * q]))));
         v[4 * q + 1] = __float_as_uint(__fadd_rn(r.y, __fmul_rn(scale, __uint_as_float(v[4 * q + 1]))));
         v[4 * q + 2] = __float_as_uint(__fadd_rn(r.z, __fmul_rn(scale, __uint_as_float(v[4 * q + 2]))));
@@ -555,8 +555,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_kernel(const
                 break;
             }
             tc_fence_after();
-            const float sq = t < a.M ? __ldg(a.qs + t) : 0.f;
-            const float sq1 = (P > 1 && t < a.M) ? __ldg(a.qs + a.qs_stride + t) : 0.f;
+            const float sq = t < a.M ? a.qs[t] : 0.f;
+            const float sq1 = (P > 1 && t < a.M) ? a.qs[a.qs_stride + t] : 0.f;
             const uint32_t cbase = lane_base + (uint32_t)buf * kPairAccCols + (uint32_t)(half * 128);
             const uint32_t acc_empty = acc_empty0 + (uint32_t)buf * 8u;
             if (a.splits > 1) {   // a K slice: raw sums to the scratch partials, finished by splitk_finish_kernel
@@ -631,7 +631,7 @@ __global__ void __launch_bounds__(256) splitk_finish_kernel(const SplitFinishArg
     for (int p = 0; p < 3; ++p) {
         if (p >= a.parts) break;
         for (int s = 0; s < a.splits; ++s) {
-            const int4 v = __ldg(reinterpret_cast<const int4 *>(a.ws + (((long long)s * a.parts + p) * a.M + t) * a.N + n));
+            const int4 v = *reinterpret_cast<const int4 *>(a.ws + (((long long)s * a.parts + p) * a.M + t) * a.N + n);
             tot[p][0] += v.x;
             tot[p][1] += v.y;
             tot[p][2] += v.z;
@@ -641,13 +641,13 @@ __global__ void __launch_bounds__(256) splitk_finish_kernel(const SplitFinishArg
     float sq[3] = {0.f, 0.f, 0.f};
 #pragma unroll
     for (int p = 0; p < 3; ++p)
-        if (p < a.parts) sq[p] = __ldg(a.qs + p * a.qs_stride + t);
+        if (p < a.parts) sq[p] = a.qs[p * a.qs_stride + t];
     const bool has_bias = a.bias != nullptr;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         float v = finish_value(tot[0][j], tot[1][j], tot[2][j], sq[0], sq[1], sq[2], a.parts, a.flags,
                                __ldg(a.alpha + n + j), has_bias, has_bias ? __ldg(a.bias + n + j) : 0.f, true);
-        if (a.res) v = __fadd_rn(__ldg(a.res + (long long)t * a.ld_res + n + j), __fmul_rn(a.res_scale, v));
+        if (a.res) v = __fadd_rn(a.res[(long long)t * a.ld_res + n + j], __fmul_rn(a.res_scale, v));
         if (a.y_f16)
             reinterpret_cast<__half *>(a.y)[(long long)t * a.ldy + n + j] = __float2half_rn(v);
         else

@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) lowbit_gemm_pair_ws_kernel(co
                 break;
             }
             tc_fence_after();
-            const float sq = t < a.M ? __ldg(a.qs + t) : 0.f;
+            const float sq = t < a.M ? a.qs[t] : 0.f;
             const uint32_t cbase = lane_base + (uint32_t)buf * kPairAccCols + (uint32_t)(half * 128);
             const uint32_t acc_empty = acc_empty0 + (uint32_t)buf * 8u;
             const int variant = (a.y_f16 ? 4 : 0) | (has_bias ? 2 : 0) | (a.flags & 1);

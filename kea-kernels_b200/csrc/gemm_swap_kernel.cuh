@@ -164,7 +164,7 @@ KEA_DEVI void swap_finish_unit(const SwapArgs &a, const uint32_t (&acc)[P][16], 
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             const int t = t0 + tl0 + j;
-            if (live_n && t < a.M) v[j] = __fadd_rn(__ldg(res + (long long)t * a.ld_res + n), __fmul_rn(a.res_scale, v[j]));
+            if (live_n && t < a.M) v[j] = __fadd_rn(res[(long long)t * a.ld_res + n], __fmul_rn(a.res_scale, v[j]));
         }
     }
     if (tma) {

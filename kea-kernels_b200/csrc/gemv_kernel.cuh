@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) lowbit_gemv_kern
                     const uint4 *row = reinterpret_cast<const uint4 *>(a.q + p * a.q_stride + (long long)m * a.ldq + k0);
 #pragma unroll
                     for (int h = 0; h < CPW / 16; ++h)
-                        v[b][h] = (row_live && 16 * h < valid) ? __ldg(row + h) : make_uint4(0, 0, 0, 0);
+                        v[b][h] = (row_live && 16 * h < valid) ? row[h] : make_uint4(0, 0, 0, 0);
                 }
 #pragma unroll
                 for (int b = 0; b < kGemvRowBatch; ++b) {
@@ -179,12 +179,12 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) lowbit_gemv_kern
 #pragma unroll
             for (int w = 0; w < kGemvThreads / 32; ++w) v += red[(w * rows + p * a.M + m) * CH + cc];
             tot[p] = v;
-            s[p] = __ldg(a.qs + p * a.qs_stride + m);
+            s[p] = a.qs[p * a.qs_stride + m];
         }
         const bool has_bias = a.bias != nullptr;
         float v = finish_value(tot[0], tot[1], tot[2], s[0], s[1], s[2], P, a.flags, __ldg(a.alpha + nn), has_bias,
                                has_bias ? __ldg(a.bias + nn) : 0.f, a.K <= 32768);
-        if (a.res) v = __fadd_rn(__ldg(a.res + (long long)m * a.ld_res + nn), __fmul_rn(a.res_scale, v));
+        if (a.res) v = __fadd_rn(a.res[(long long)m * a.ld_res + nn], __fmul_rn(a.res_scale, v));
         if (a.y_f16)
             reinterpret_cast<__half *>(a.y)[(long long)m * a.ldy + nn] = __float2half_rn(v);
         else

@@ -14,6 +14,7 @@
 #include "gemm_pair_ws_kernel.cuh"
 #include "gemm_swap_kernel.cuh"
 #include "gemv_kernel.cuh"
+#include "gemm_reg_kernel.cuh"
 #include "conv_kernels.cuh"
 #include "attention_kernels.cuh"
 #include "aux_kernels.cuh"
@@ -29,6 +30,7 @@ constexpr int kMaxDynSmem = 227 * 1024 - 8192;  // leave room for the kernel's s
 // The pair kernel's static shared memory is a few hundred bytes, so its dynamic share may reach 226 KB.
 constexpr int kPairMaxDynSmem = 227 * 1024 - 1024;
 constexpr int kMaxPortableCluster = 8;
+constexpr int kRegMaxSmem = 64 * 1024;   // the register-operand kernel's partial sums (at most ~37 KB in use)
 constexpr int kMaxCluster = 16;
 
 int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
@@ -140,6 +142,17 @@ int device_setup(int *device_out, void *stream, bool check_capture = true) {
         };
         for (const void *k : gemv_kernels)
             if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kea::kGemvMaxSmem) != cudaSuccess)
+                status = KEA_ERR_CUDA;
+        const void *reg_kernels[24] = {
+#define KEA_REG_P(W, P) (const void *)kea::lowbit_gemm_reg_kernel<W, P, 1, 4, 2>, \
+                        (const void *)kea::lowbit_gemm_reg_kernel<W, P, 2, 4, 2>, \
+                        (const void *)kea::lowbit_gemm_reg_kernel<W, P, 2, 2, 3>, \
+                        (const void *)kea::lowbit_gemm_reg_kernel<W, P, 4, 2, 2>
+            KEA_REG_P(1, 1), KEA_REG_P(1, 2), KEA_REG_P(1, 3), KEA_REG_P(2, 1), KEA_REG_P(2, 2), KEA_REG_P(2, 3)
+#undef KEA_REG_P
+        };
+        for (const void *k : reg_kernels)
+            if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kRegMaxSmem) != cudaSuccess)
                 status = KEA_ERR_CUDA;
     }
     if (status == KEA_OK) {
@@ -509,7 +522,45 @@ KeaGemmConfig narrow_mid_config(int m, int n, int k, int wbits, int sms) {
 
 // The full table: the CUDA-core kernel for M x parts <= 4, the swap kernel up to 256 tokens, the pair kernel where its
 // shape rule holds (except narrow layers just above its M threshold), else the per-tile kernel's entry.
-KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
+// The register-operand kernel's tiles for a shape: tile_n channels x tile_m activation rows (tokens x parts) per CTA,
+// splits K-slices among its 8 warps. Measured (B200, graph-timed, 4 rotating weight sets): about 256 CTAs is best,
+// and of two tiles with the same count the one with more channels (fewer re-reads of the activation rows); 16 rows x
+// 32 channels is the base tile, 32 x 32 where it would exceed ~320 CTAs, 32 x 16 for 16 rows or fewer where it
+// would give fewer than ~160.
+KeaGemmConfig reg_config(int m, int n, int k, int parts, int sms) {
+    (void)k;
+    (void)sms;
+    KeaGemmConfig c{};
+    c.kernel = 4;
+    c.tile_m = 16;
+    c.tile_n = 32;
+    c.splits = 8;
+    c.stages = 0;
+    const long long rows = (long long)m * parts;
+    const long long ctas = (long long)ceil_div(n, 32) * ceil_div(m, 16 / parts);
+    if (ctas > 320) c.tile_m = 32;
+    else if (ctas < 160 && rows <= 16) {
+        c.tile_m = 32;
+        c.tile_n = 16;
+    }
+    c.smem_bytes = kea::reg_smem_bytes(c.splits, c.tile_m, c.tile_n);
+    return c;
+}
+
+// Where the table takes the register kernel (activation rows = tokens x parts, above the CUDA-core kernel's 4). Measured
+// against the tcgen05 table's choice (graph-timed, with and without programmatic dependent launch): faster while
+// rows x N <= 160 K at up to 256 rows (e.g. N 1024, K 1024, M 125: 4.3 / 3.2 us against 6.7 / 4.6; N 4096, K 1024, M 16: 3.8 / 2.8
+// against 6.6 / 4.9; three parts, N 1024, K 1024, M 38: 3.9 / 2.8 against 6.2 / 4.0) and on narrow layers with long K
+// (N 1024, K 4096, M 125: 6.9 / 5.8 against 7.8 / 6.7; three parts at M 126: 12.9 / 12.0 against 14.2 / 13.0) up to
+// 128 rows, or 400 rows of three parts. Wider layers at M 125 (N 2048-4096, 6.7 / 4.6-5.5 us on the tcgen05 kernels)
+// stay there: their activation rows are re-read by N / 32 CTAs.
+bool reg_shape(int m, int n, int k, int parts) {
+    const long long rows = (long long)m * parts;
+    if (rows <= 256 && rows * n <= 160LL * 1024) return true;
+    return n <= 1024 && k >= 4096 && (rows <= 128 || (parts == 3 && rows <= 400));
+}
+
+KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms, bool allow_reg = true) {
     KeaGemmConfig c = choose_tile(m, n, k, wbits, parts, sms);
     if (swap_shape(m, n, k, parts)) {
         const KeaGemmConfig s = swap_config(m, n, k, wbits, parts, sms);
@@ -524,6 +575,8 @@ KeaGemmConfig choose(int m, int n, int k, int wbits, int parts, int sms) {
         c.splits = 1;
         c.stages = 1;
         c.smem_bytes = kea::gemv_smem_bytes(m * parts, c.tile_n);
+    } else if (allow_reg && reg_shape(m, n, k, parts)) {
+        c = reg_config(m, n, k, parts, sms);
     }
     return c;
 }
@@ -616,6 +669,94 @@ int launch_gemv(const KeaGemmDesc *d, const KeaGemmConfig &c, void *stream) {
         case 9: e = launch_gemv_p<2, 1>(&cfg, a); break;
         case 10: e = launch_gemv_p<2, 2>(&cfg, a); break;
         default: e = launch_gemv_p<2, 3>(&cfg, a); break;
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return KEA_ERR_CUDA;
+    }
+    return KEA_OK;
+}
+
+// The register-operand kernel (warp MMAs, weights expanded in registers): `cn` channels x `rows` activation rows
+// (tokens x parts) per CTA, its 8 warps cut into `ks` K-slices x 8 / ks channel groups of 16 x cg channels.
+struct RegPlan {
+    int cg = 0, rg = 0, ks = 0, cn = 0, rows = 0, tt = 0;
+};
+
+// The instantiated warp tiles (cg channel groups x rg row groups): 16 x cg channels x 8 x rg rows per warp.
+bool reg_tile_ok(int cg, int rg) { return (cg == 1 && rg == 4) || (cg == 2 && (rg == 4 || rg == 2)) || (cg == 4 && rg == 2); }
+
+bool reg_plan(int parts, int cn, int rows, int ks, RegPlan *p) {
+    if (ks != 1 && ks != 2 && ks != 4 && ks != 8) return false;
+    if (cn != 16 && cn != 32 && cn != 64 && cn != 128) return false;   // divides the 128-row panel tile
+    if (rows != 16 && rows != 32) return false;
+    const int cw = kea::kRegWarps / ks;
+    if (cn % (16 * cw)) return false;
+    const int cg = cn / (16 * cw), rg = rows / 8;
+    if (!reg_tile_ok(cg, rg) || rows / parts < 1) return false;
+    p->cg = cg;
+    p->rg = rg;
+    p->ks = ks;
+    p->cn = cn;
+    p->rows = rows;
+    p->tt = rows / parts;
+    return true;
+}
+
+template <int W, int P>
+cudaError_t launch_reg_p(cudaLaunchConfig_t *cfg, const kea::RegArgs &a, const RegPlan &p) {
+    if (p.cg == 1) return cudaLaunchKernelEx(cfg, kea::lowbit_gemm_reg_kernel<W, P, 1, 4, 2>, a);
+    if (p.cg == 4) return cudaLaunchKernelEx(cfg, kea::lowbit_gemm_reg_kernel<W, P, 4, 2, 2>, a);
+    if (p.rg == 2) return cudaLaunchKernelEx(cfg, kea::lowbit_gemm_reg_kernel<W, P, 2, 2, 3>, a);
+    return cudaLaunchKernelEx(cfg, kea::lowbit_gemm_reg_kernel<W, P, 2, 4, 2>, a);
+}
+
+int launch_reg(const KeaGemmDesc *d, const RegPlan &p, void *stream) {
+    kea::RegArgs a{};
+    a.q = d->q;
+    a.q_stride = d->parts > 1 ? d->q_part_stride : 0;
+    a.ldq = d->ldq;
+    a.qs = d->qs;
+    a.qs_stride = d->qs_part_stride;
+    a.panels = d->panels;
+    a.alpha = d->alpha;
+    a.bias = d->bias;
+    a.y = d->y;
+    a.ldy = d->ldy;
+    a.y_f16 = d->y_dtype == KEA_OUT_F16;
+    a.acc = d->acc;
+    a.ld_acc = d->ld_acc;
+    a.acc_stride = d->acc_part_stride;
+    a.res = d->residual;
+    a.ld_res = d->ld_residual;
+    a.res_scale = d->residual_scale;
+    a.M = d->m;
+    a.N = d->n;
+    a.K = d->k;
+    a.kb_total = ceil_div(d->k, kea::kBK);
+    a.ks = p.ks;
+    a.tt = p.tt;
+    a.flags = d->flags & (KEA_FLAG_SILU | KEA_FLAG_ORDER1);
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ceil_div(d->n, p.cn), (unsigned)ceil_div(d->m, p.tt), 1);
+    cfg.blockDim = dim3(kea::kRegThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)kea::reg_smem_bytes(p.ks, p.rows, p.cn);
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    if (d->flags & KEA_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e;
+    switch (d->wbits * 4 + d->parts) {
+        case 5: e = launch_reg_p<1, 1>(&cfg, a, p); break;
+        case 6: e = launch_reg_p<1, 2>(&cfg, a, p); break;
+        case 7: e = launch_reg_p<1, 3>(&cfg, a, p); break;
+        case 9: e = launch_reg_p<2, 1>(&cfg, a, p); break;
+        case 10: e = launch_reg_p<2, 2>(&cfg, a, p); break;
+        default: e = launch_reg_p<2, 3>(&cfg, a, p); break;
     }
     if (e != cudaSuccess) {
         cudaGetLastError();
@@ -788,7 +929,8 @@ int validate_gemm(const KeaGemmDesc *d) {
     if (!aligned16(d->q) || d->ldq % 16 || !aligned16(d->panels)) return KEA_ERR_ALIGNMENT;
     if (d->parts > 1 && (d->q_part_stride % 16 || d->q_part_stride < (int64_t)d->m * d->ldq)) return KEA_ERR_ALIGNMENT;
     if (d->flags & ~(KEA_FLAG_SILU | KEA_FLAG_ORDER1 | KEA_FLAG_PDL | KEA_FLAG_NO_PAIR | KEA_FLAG_FORCE_PAIR |
-                     KEA_FLAG_FORCE_SWAP | KEA_FLAG_NO_SWAP | KEA_FLAG_TEST_STALL | KEA_FLAG_NO_RESIDENT_WEIGHTS))
+                     KEA_FLAG_FORCE_SWAP | KEA_FLAG_NO_SWAP | KEA_FLAG_TEST_STALL | KEA_FLAG_NO_RESIDENT_WEIGHTS |
+                     KEA_FLAG_FORCE_REG | KEA_FLAG_NO_REG))
         return KEA_ERR_INVALID_VALUE;
     if ((d->flags & KEA_FLAG_NO_PAIR) && (d->flags & KEA_FLAG_FORCE_PAIR)) return KEA_ERR_INVALID_VALUE;
     // forced swap: tile_m is its token tile (0, or a multiple of 16), tile_n unused
@@ -796,15 +938,27 @@ int validate_gemm(const KeaGemmDesc *d) {
         (d->tile_m % 16 || d->tile_m < 0 || d->tile_n || (d->flags & (KEA_FLAG_NO_SWAP | KEA_FLAG_FORCE_PAIR))))
         return KEA_ERR_INVALID_VALUE;
     if ((d->flags & KEA_FLAG_TEST_STALL) && !(d->flags & KEA_FLAG_FORCE_SWAP)) return KEA_ERR_INVALID_VALUE;
+    // forced register-operand kernel: tile_n channels and tile_m rows per CTA, splits K-slices (0: the table's)
+    if ((d->flags & KEA_FLAG_FORCE_REG) &&
+        (d->stages || (d->flags & (KEA_FLAG_NO_REG | KEA_FLAG_FORCE_SWAP | KEA_FLAG_FORCE_PAIR))))
+        return KEA_ERR_INVALID_VALUE;
     if (d->wait_clocks < 0) return KEA_ERR_INVALID_VALUE;
     return KEA_OK;
 }
 
 // ---- routing: the one decision of which kernel runs a descriptor (the launch, the no-allocation scratch check) ----
-enum Route { kRouteGemv, kRoutePair, kRouteSwap, kRouteTile };
+enum Route { kRouteGemv, kRoutePair, kRouteSwap, kRouteTile, kRouteReg };
 
-int route_gemm(const KeaGemmDesc *d, int sms, Route *route, KeaGemmConfig *c, SwapPlan *sp) {
+int route_gemm(const KeaGemmDesc *d, int sms, Route *route, KeaGemmConfig *c, SwapPlan *sp, RegPlan *rp) {
     const bool forced = d->tile_m || d->tile_n || d->splits || d->stages;
+    if (d->flags & KEA_FLAG_FORCE_REG) {   // channels / rows / K-slices (0: the table's) apply to the register kernel
+        const KeaGemmConfig t = reg_config(d->m, d->n, d->k, d->parts, sms);
+        if (!reg_plan(d->parts, d->tile_n ? d->tile_n : t.tile_n, d->tile_m ? d->tile_m : t.tile_m,
+                      d->splits ? d->splits : t.splits, rp))
+            return KEA_ERR_UNSUPPORTED;
+        *route = kRouteReg;
+        return KEA_OK;
+    }
     if (d->flags & KEA_FLAG_FORCE_SWAP) {   // token tile / splits / stages (0: the table's) apply to the swap kernel
         if (!swap_plan(d->m, d->n, d->k, d->wbits, d->parts, sms, d->splits, d->stages, sp, d->tile_m))
             return KEA_ERR_UNSUPPORTED;
@@ -832,6 +986,13 @@ int route_gemm(const KeaGemmDesc *d, int sms, Route *route, KeaGemmConfig *c, Sw
         *route = kRoutePair;
         return KEA_OK;
     }
+    if (!forced && c->kernel == 4 && !(d->flags & KEA_FLAG_NO_REG) &&
+        reg_plan(d->parts, c->tile_n, c->tile_m, c->splits, rp)) {
+        *route = kRouteReg;
+        return KEA_OK;
+    }
+    if (!forced && c->kernel == 4)   // kept off the register kernel: the tcgen05 table's choice for the shape
+        *c = choose(d->m, d->n, d->k, d->wbits, d->parts, sms, false);
     if (!forced && c->kernel == 3 && !(d->flags & KEA_FLAG_NO_SWAP) &&
         swap_plan(d->m, d->n, d->k, d->wbits, d->parts, sms, 0, 0, sp)) {
         *route = kRouteSwap;
@@ -846,7 +1007,8 @@ size_t routed_scratch_bytes(const KeaGemmDesc *d, int sms) {
     Route r;
     KeaGemmConfig c{};
     SwapPlan sp;
-    if (route_gemm(d, sms, &r, &c, &sp) != KEA_OK || r != kRoutePair) return 0;
+    RegPlan rp;
+    if (route_gemm(d, sms, &r, &c, &sp, &rp) != KEA_OK || r != kRoutePair) return 0;
     return pair_workspace_bytes(d->m, d->n, d->k, d->parts, sms);
 }
 
@@ -1629,9 +1791,11 @@ int kea_lowbit_gemm(const KeaGemmDesc *d, void *stream) {
     Route route;
     KeaGemmConfig c{};
     SwapPlan sp;
-    const int rs = route_gemm(d, g_devices[dev].sms, &route, &c, &sp);
+    RegPlan rp;
+    const int rs = route_gemm(d, g_devices[dev].sms, &route, &c, &sp, &rp);
     if (rs != KEA_OK) return rs;
     if (route == kRouteGemv) return launch_gemv(d, c, stream);
+    if (route == kRouteReg) return launch_reg(d, rp, stream);
     if (route == kRouteSwap) return launch_swap(d, sp, stream);
     if (route == kRoutePair) return launch_pair(d, c, g_devices[dev].sms, stream);
     return launch_tile(d, c, dev, stream, nullptr);
@@ -1667,7 +1831,12 @@ static int project_route(const KeaProjectDesc *p, void *stream, int *fused, KeaG
     Route route;
     KeaGemmConfig c{};
     SwapPlan sp;
-    const int rs = route_gemm(d, g_devices[dev].sms, &route, &c, &sp);
+    RegPlan rp;
+    // the fused form lives in the per-tile tcgen05 kernel: a caller asking for it routes as if the register kernel
+    // were off (unless it forces that kernel)
+    KeaGemmDesc g = *d;
+    if ((p->flags & KEA_PROJECT_FUSE) && !(g.flags & KEA_FLAG_FORCE_REG)) g.flags |= KEA_FLAG_NO_REG;
+    const int rs = route_gemm(&g, g_devices[dev].sms, &route, &c, &sp, &rp);
     if (rs != KEA_OK) return rs;
     if ((p->flags & KEA_PROJECT_FUSE) && route == kRouteTile && quant_unit_rows(x)) {
         const FusedQuant fq{x, p->scratch, p->scratch_bytes, true};

@@ -19,6 +19,7 @@ OK, INVALID_VALUE, ALIGNMENT, UNSUPPORTED, INVALID_CODES, CUDA, NO_DEVICE, DEVIC
 OUT_F32, OUT_F16 = 0, 1
 FLAG_SILU, FLAG_ORDER1, FLAG_PDL, FLAG_NO_PAIR, FLAG_FORCE_PAIR = 1, 2, 4, 8, 16
 FLAG_FORCE_SWAP, FLAG_NO_SWAP, FLAG_TEST_STALL, FLAG_NO_RESIDENT_WEIGHTS = 32, 64, 128, 256
+FLAG_FORCE_REG, FLAG_NO_REG = 512, 1024
 QUANT_INPUT_SILU, QUANT_PDL, QUANT_NARROW_ROWS = 1, 2, 4
 PROJECT_FUSE = 1
 DEVERR_TIMEOUT, DEVERR_TAIL_BITS, DEVERR_TERNARY_11 = 1, 2, 4

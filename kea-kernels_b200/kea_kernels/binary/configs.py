@@ -16,7 +16,7 @@ from kea_kernels import _lib
 SMS = 148
 
 
-PER_TILE, PAIR, GEMV, SWAP = 0, 1, 2, 3
+PER_TILE, PAIR, GEMV, SWAP, REG = 0, 1, 2, 3, 4
 
 
 @dataclasses.dataclass(frozen=True)
@@ -26,8 +26,10 @@ class DotConfig:
     cta_group::2), walked by at most SMS / 2 pairs, two accumulator buffers in tensor memory. kernel == GEMV: the
     CUDA-core kernel for M <= 16, `tile_n` channels per CTA. kernel == SWAP: the small-M kernel with the operands
     swapped (128 weight rows on the MMA's M axis, every part's `tile_m` tokens on its N axis, K split over a cluster
-    of `splits` CTAs). Passing a PER_TILE config forces those tiles; a SWAP config forces the swap kernel with its
-    splits and stages."""
+    of `splits` CTAs). kernel == REG: the small-M register-operand kernel (warp-level MMAs, weights expanded in
+    registers), `tile_n` channels x `tile_m` activation rows (tokens x parts) per CTA, K cut into `splits` slices
+    among its 8 warps. Passing a PER_TILE config forces those tiles; a SWAP config forces the swap kernel with its
+    splits and stages; a REG config the register kernel with its tiles."""
     tile_m: int
     tile_n: int
     splits: int
@@ -45,11 +47,20 @@ class DotConfig:
             return f"gemv_n{self.tile_n}"
         if self.kernel == SWAP:
             return f"swap_t{self.tile_m}_c{self.splits}_s{self.stages}"
+        if self.kernel == REG:
+            return f"reg_r{self.tile_m}_n{self.tile_n}_k{self.splits}"
         return f"m{self.tile_m}_n{self.tile_n}_c{self.splits}_s{self.stages}"
 
     def validate(self, parts: int = 1) -> None:
         if self.kernel == GEMV:
             if not (1 <= self.tile_m <= 16 and self.tile_n in (8, 16, 32)):
+                raise ValueError(f"invalid config {self}")
+            return
+        if self.kernel == REG:
+            cw = 8 // self.splits if self.splits in (1, 2, 4, 8) else 0
+            cg = self.tile_n // (16 * cw) if cw and self.tile_n % (16 * cw) == 0 else 0
+            if not (self.tile_n in (16, 32, 64, 128) and self.tile_m in (16, 32) and self.stages == 0
+                    and (cg, self.tile_m // 8) in ((1, 4), (2, 4), (2, 2), (4, 2)) and self.tile_m // parts >= 1):
                 raise ValueError(f"invalid config {self}")
             return
         if self.kernel == SWAP:
@@ -60,7 +71,7 @@ class DotConfig:
                 and 1 <= self.stages <= 8 and (self.tile_m // 128) * parts * self.tile_n <= 512):
             raise ValueError(f"invalid config {self}")
 
-    def grid(self, m: int, n: int) -> tuple[int, int, int]:
+    def grid(self, m: int, n: int, parts: int = 1) -> tuple[int, int, int]:
         if self.kernel == GEMV:
             return (-(-n // self.tile_n), 1, 1)
         if self.pair:
@@ -68,6 +79,8 @@ class DotConfig:
             return (2 * min(tiles, SMS // 2), 1, 1)
         if self.kernel == SWAP:
             return (-(-n // 128), -(-m // self.tile_m), self.splits)
+        if self.kernel == REG:
+            return (-(-n // self.tile_n), -(-m // (self.tile_m // parts)), 1)
         return (-(-n // self.tile_n), -(-m // self.tile_m), self.splits)
 
 

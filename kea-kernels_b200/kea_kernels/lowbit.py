@@ -103,7 +103,7 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
          config=None, pdl: bool = False, error_word: Tensor | None = None, pair: bool = True,
          force_pair: bool = False, residual: Tensor | None = None, residual_scale: float = 1.0,
          workspace: Tensor | None = None, swap: bool = True, wait_clocks: int = 0, test_stall: bool = False,
-         resident_weights: bool = True) -> None:
+         resident_weights: bool = True, reg: bool = True) -> None:
     """y[:m] (row stride y.stride(0); FP32 or FP16) from q int8 [parts, m, ldq] and qs FP32 [parts, m].
     acc, when given, receives the exact INT32 accumulators as int32 [parts, m, n] (any row / part strides).
     `config` forces the per-tile kernel's tiles, or (tile_m <= 16, m <= 16) the CUDA-core kernel's channels per CTA;
@@ -116,13 +116,15 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
     the table away from the small-M swapped-operand kernel; a SWAP config (kernel == 3) forces it with its splits and
     stages. wait_clocks bounds each wait of the swap kernel (0: the library's default); test_stall (tests only, with a
     forced SWAP config) makes the kernel withhold its activation copies so that a wait runs out. resident_weights=False
-    keeps the pair kernel re-expanding every tile's weights where it would keep them resident (one part, K <= 1024)."""
+    keeps the pair kernel re-expanding every tile's weights where it would keep them resident (one part, K <= 1024).
+    reg=False keeps the table away from the small-M register-operand kernel; a REG config (kernel == 4) forces it
+    with its channels, rows and K-slices per CTA."""
     if m == 0:
         return
     d, keep = _gemm_desc(q, qs, ldq, m, panels, wbits, n, k, alpha, bias, y, parts=parts, silu=silu, order=order,
                          acc=acc, config=config, pdl=pdl, error_word=error_word, pair=pair, force_pair=force_pair,
                          residual=residual, residual_scale=residual_scale, workspace=workspace, swap=swap,
-                         wait_clocks=wait_clocks, test_stall=test_stall, resident_weights=resident_weights)
+                         wait_clocks=wait_clocks, test_stall=test_stall, resident_weights=resident_weights, reg=reg)
     with torch.cuda.device(y.device):
         _lib.check(_lib.lib().kea_lowbit_gemm(ctypes.byref(d), _lib.stream_handle(y.device)), "gemm")
 
@@ -130,7 +132,7 @@ def gemm(q: Tensor, qs: Tensor, ldq: int, m: int, panels: Tensor, wbits: int, n:
 def _gemm_desc(q, qs, ldq, m, panels, wbits, n, k, alpha, bias, y, *, parts, silu=False, order=0, acc=None,
                config=None, pdl=False, error_word=None, pair=True, force_pair=False, residual=None,
                residual_scale=1.0, workspace=None, swap=True, wait_clocks=0, test_stall=False,
-               resident_weights=True):
+               resident_weights=True, reg=True):
     """The C descriptor of gemm()'s arguments (checked), and the workspace tensor it points into (keep it alive
     until the launch)."""
     if parts not in (1, 2, 3):
@@ -177,7 +179,12 @@ def _gemm_desc(q, qs, ldq, m, panels, wbits, n, k, alpha, bias, y, *, parts, sil
         | (0 if swap else _lib.FLAG_NO_SWAP) | (_lib.FLAG_TEST_STALL if test_stall else 0) \
         | (0 if resident_weights else _lib.FLAG_NO_RESIDENT_WEIGHTS)
     kernel = getattr(config, "kernel", 0) if config is not None else None
-    if kernel == 3:   # the swap kernel with this config's token tile, split and stages (0: the table's)
+    if not reg and kernel != 4:
+        d.flags |= _lib.FLAG_NO_REG
+    if kernel == 4:   # the register kernel with this config's channels, rows and K-slices per CTA (0: the table's)
+        d.flags |= _lib.FLAG_FORCE_REG
+        d.tile_m, d.tile_n, d.splits = config.tile_m, config.tile_n, config.splits
+    elif kernel == 3:   # the swap kernel with this config's token tile, split and stages (0: the table's)
         d.flags |= _lib.FLAG_FORCE_SWAP
         d.tile_m, d.splits, d.stages = config.tile_m, config.splits, config.stages
     elif config is not None and kernel != 1:   # a pair config from the table forces nothing

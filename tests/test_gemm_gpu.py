@@ -52,7 +52,7 @@ def _channel(n: int, seed: int, bias: bool):
 
 
 def _run(codes, wbits, n, k, q, qs, alpha, bias, *, flags=0, out=torch.float32, config=None, pdl=False, pair=True,
-         pair_only=False, swap=True):
+         pair_only=False, swap=True, reg=False):
     parts, m, ldq = q.shape
     panels = lowbit.prepare_panels(torch.from_numpy(codes).to(DEV), wbits, n, k)
     qd, qsd = torch.from_numpy(q).to(DEV), torch.from_numpy(qs).to(DEV)
@@ -61,7 +61,8 @@ def _run(codes, wbits, n, k, q, qs, alpha, bias, *, flags=0, out=torch.float32, 
     y = torch.full((m, n), float("nan"), device=DEV, dtype=out)
     acc = torch.full((parts, m, n), -7, device=DEV, dtype=torch.int32)
     lowbit.gemm(qd, qsd, ldq, m, panels, wbits, n, k, ad, bd, y, parts=parts, silu=bool(flags & 1),
-                order=(flags >> 1) & 1, acc=acc, config=config, pdl=pdl, pair=pair, force_pair=pair_only, swap=swap)
+                order=(flags >> 1) & 1, acc=acc, config=config, pdl=pdl, pair=pair, force_pair=pair_only, swap=swap,
+                reg=reg)
     torch.cuda.synchronize()
     assert _lib.read_device_error() == 0
     return y.cpu(), acc.cpu().numpy()
@@ -662,17 +663,18 @@ def test_graph_capture_replays_bitwise():
 @pytest.mark.parametrize("n,k,m,parts,kernel", [(1024, 1024, 2, 1, configs.GEMV), (4096, 1024, 125, 1, configs.PER_TILE),
                                                 (1024, 4096, 38, 1, configs.PER_TILE),
                                                 (1024, 1024, 40, 3, configs.PER_TILE),
-                                                (300, 200, 77, 2, configs.PER_TILE), (4096, 1024, 16, 1, configs.SWAP),
-                                                (1024, 4096, 16, 1, configs.SWAP), (1024, 4096, 256, 3, configs.SWAP),
+                                                (300, 200, 77, 2, configs.PER_TILE), (4096, 1024, 16, 1, configs.REG),
+                                                (1024, 4096, 16, 1, configs.REG), (1024, 1024, 125, 1, configs.REG),
+                                                (1024, 4096, 256, 3, configs.SWAP),
                                                 (2048, 1024, 256, 2, configs.SWAP), (1024, 1024, 200, 1, configs.SWAP), (4096, 1024, 2048, 1, configs.PAIR),
                                                 (4096, 1024, 8192, 2, configs.PAIR)])
 @pytest.mark.parametrize("scale", [1.0, 0.5])
 def test_residual_epilogue_equals_unfused(wbits, n, k, m, parts, kernel, scale):
-    """The skip connection in the epilogue (CUDA-core, swap with and without split-K, per-tile with and without
-    split-K and stacked parts, pair with one and two parts): bit for bit PyTorch's `residual + scale * y`, also
-    written in place over the residual."""
-    swap = kernel != configs.PER_TILE
-    if swap:
+    """The skip connection in the epilogue (CUDA-core, register-operand, swap with and without split-K, per-tile
+    with and without split-K and stacked parts, pair with one and two parts): bit for bit PyTorch's
+    `residual + scale * y`, also written in place over the residual."""
+    swap, reg = kernel not in (configs.PER_TILE, configs.REG), kernel == configs.REG
+    if kernel != configs.PER_TILE:
         assert configs.choose(m, n, k, wbits, parts).kernel == kernel
     seed = wbits * 7 + n + k + m + parts
     codes, _ = _codes(wbits, n, k, seed)
@@ -683,14 +685,14 @@ def test_residual_epilogue_equals_unfused(wbits, n, k, m, parts, kernel, scale):
     ad, bd = torch.from_numpy(alpha).to(DEV), torch.from_numpy(bias).to(DEV)
     res = torch.randn(m, n, generator=torch.Generator().manual_seed(seed)).to(DEV)
     y = torch.empty(m, n, device=DEV)
-    lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, y, parts=parts, swap=swap)
+    lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, y, parts=parts, swap=swap, reg=reg)
     want = res + scale * y
     fused = torch.empty(m, n, device=DEV)
     lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, fused, parts=parts, residual=res,
-                residual_scale=scale, swap=swap)
+                residual_scale=scale, swap=swap, reg=reg)
     inplace = res.clone()
     lowbit.gemm(qd, qsd, q.shape[2], m, panels, wbits, n, k, ad, bd, inplace, parts=parts, residual=inplace,
-                residual_scale=scale, swap=swap)
+                residual_scale=scale, swap=swap, reg=reg)
     torch.cuda.synchronize()
     assert _lib.read_device_error() == 0
     assert torch.equal(fused.view(torch.int32), want.view(torch.int32))

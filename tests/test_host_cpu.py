@@ -22,7 +22,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.kea_lowbit_version() == 4
+    assert lib.kea_lowbit_version() == 5
     assert lib.kea_lowbit_status_string(0) == b"success"
     assert lib.kea_lowbit_status_string(4) == b"invalid packed codes"
 
@@ -52,6 +52,16 @@ def test_every_shape_has_a_valid_config(n, k, wbits, parts):
             cfg = configs.choose(m, n, k, wbits, parts)
             cfg.validate(parts)
             assert cfg.grid(m, n)[0] * cfg.tile_n >= n
+            continue
+        rows = m * parts   # the register kernel: up to 160 K output rows x channels, or narrow long-K layers
+        reg = (rows <= 256 and rows * n <= 160 * 1024) or (n <= 1024 and k >= 4096 and (rows <= 128 or (parts == 3 and rows <= 400)))
+        assert (c.kernel == configs.REG) == reg
+        if c.kernel == configs.REG:   # tile_m activation rows x tile_n channels per CTA, K-slices among 8 warps
+            cfg = configs.choose(m, n, k, wbits, parts)
+            cfg.validate(parts)
+            gx, gy, _ = cfg.grid(m, n, parts)
+            assert gx * cfg.tile_n >= n and gy * (cfg.tile_m // parts) >= m
+            assert 0 < c.smem_bytes <= 48 * 1024
             continue
         if c.kernel == configs.PAIR:   # 256 x 256 pair tiles, one 256-column accumulator per part
             assert c.tile_m == 256 and c.tile_n == 256 and parts <= 2 and c.splits == 1
@@ -85,12 +95,14 @@ def test_every_shape_has_a_valid_config(n, k, wbits, parts):
 def test_small_m_splits_k_and_large_m_does_not():
     c = _lib.choose_config(125, 4096, 1024, 1, 1)       # 32-channel tiles already give 128 CTAs
     assert (c.kernel, c.tile_m, c.tile_n, c.splits) == (configs.PER_TILE, 128, 32, 1)
-    c = _lib.choose_config(125, 1024, 4096, 1, 1)       # 32 channel tiles: K split over a cluster
-    assert c.kernel == configs.PER_TILE and c.splits > 1
-    c = _lib.choose_config(16, 4096, 1024, 1, 1)        # swap: 32 channel tiles x 4 K slices = 128 CTAs
-    assert (c.kernel, c.tile_m, c.tile_n, c.splits) == (configs.SWAP, 16, 128, 4)
-    c = _lib.choose_config(16, 1024, 4096, 1, 1)        # swap: 8 channel tiles, K over a cluster of 8
-    assert (c.kernel, c.splits) == (configs.SWAP, 8)
+    c = _lib.choose_config(125, 1024, 4096, 1, 1)       # register kernel: 32 channels x 16 tokens, 256 CTAs
+    assert (c.kernel, c.tile_m, c.tile_n, c.splits) == (configs.REG, 16, 32, 8)
+    c = _lib.choose_config(16, 4096, 1024, 1, 1)        # 16 channels x 32 rows: 256 CTAs
+    assert (c.kernel, c.tile_m, c.tile_n, c.splits) == (configs.REG, 32, 16, 8)
+    c = _lib.choose_config(378, 1024, 4096, 1, 1)       # one part past 128 rows: the tcgen05 table
+    assert c.kernel != configs.REG
+    c = _lib.choose_config(126, 1024, 4096, 1, 3)       # 378 rows of three parts: 32 rows x 32 channels
+    assert (c.kernel, c.tile_m, c.tile_n, c.splits) == (configs.REG, 32, 32, 8)
     c = _lib.choose_config(256, 4096, 1024, 1, 3)       # three parts stacked along the MMA's N: 3 x 128 tokens x 2
     assert (c.kernel, c.tile_m, c.splits) == (configs.SWAP, 128, 1)
     c = _lib.choose_config(8192, 4096, 1024, 1, 1)
@@ -121,7 +133,11 @@ def test_c_abi_argument_errors_are_reported_before_any_device_work():
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(q=24)), None) == _lib.ALIGNMENT
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(ldq=1000)), None) == _lib.INVALID_VALUE   # ldq < k
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(ldq=1032, k=1030)), None) == _lib.ALIGNMENT  # ldq % 16
-    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=512)), None) == _lib.INVALID_VALUE
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=2048)), None) == _lib.INVALID_VALUE
+    # the register kernel takes no stages and no contradictory kernel flags
+    assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_FORCE_REG, stages=2)), None) == _lib.INVALID_VALUE
+    for other in (_lib.FLAG_NO_REG, _lib.FLAG_FORCE_SWAP, _lib.FLAG_FORCE_PAIR):
+        assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_FORCE_REG | other)), None) == _lib.INVALID_VALUE
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_TEST_STALL)), None) == _lib.INVALID_VALUE
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_FORCE_SWAP, tile_m=100)), None) == _lib.INVALID_VALUE
     assert lib.kea_lowbit_gemm(ctypes.byref(_desc(flags=_lib.FLAG_FORCE_SWAP, tile_n=32)), None) == _lib.INVALID_VALUE
@@ -250,6 +266,15 @@ def test_dot_config_validation():
     with pytest.raises(ValueError):
         configs.DotConfig(128, 128, 17, 1).validate(1)
     assert configs.DotConfig(128, 128, 4, 2).label() == "m128_n128_c4_s2"
+    # register kernel: channels x rows x K-slices must name an instantiated warp tile
+    for rows, cn, ks in ((32, 32, 8), (16, 64, 4), (32, 16, 8), (32, 128, 1)):
+        configs.DotConfig(rows, cn, ks, 0, configs.REG).validate(3)
+    for rows, cn, ks, parts in ((24, 32, 8, 1), (32, 48, 8, 1), (32, 32, 3, 1), (16, 16, 8, 1), (32, 256, 8, 1),
+                                (32, 64, 8, 1), (16, 128, 8, 1)):
+        with pytest.raises(ValueError):
+            configs.DotConfig(rows, cn, ks, 0, configs.REG).validate(parts)
+    assert configs.DotConfig(32, 64, 4, 0, configs.REG).label() == "reg_r32_n64_k4"
+    assert configs.DotConfig(30, 64, 4, 0, configs.REG).grid(125, 1000, 3) == (16, 13, 1)
 
 
 def test_part_count_overrides_components_and_forwards_writes():
