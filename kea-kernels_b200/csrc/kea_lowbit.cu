@@ -547,13 +547,13 @@ KeaGemmConfig reg_config(int m, int n, int k, int parts, int sms) {
     return c;
 }
 
-// Where the table takes the register kernel (activation rows = tokens x parts, above the CUDA-core kernel's 4). Measured
-// against the tcgen05 table's choice (graph-timed, with and without programmatic dependent launch): faster while
-// rows x N <= 160 K at up to 256 rows (e.g. N 1024, K 1024, M 125: 4.3 / 3.2 us against 6.7 / 4.6; N 4096, K 1024, M 16: 3.8 / 2.8
-// against 6.6 / 4.9; three parts, N 1024, K 1024, M 38: 3.9 / 2.8 against 6.2 / 4.0) and on narrow layers with long K
-// (N 1024, K 4096, M 125: 6.9 / 5.8 against 7.8 / 6.7; three parts at M 126: 12.9 / 12.0 against 14.2 / 13.0) up to
-// 128 rows, or 400 rows of three parts. Wider layers at M 125 (N 2048-4096, 6.7 / 4.6-5.5 us on the tcgen05 kernels)
-// stay there: their activation rows are re-read by N / 32 CTAs.
+// Where the table takes the register kernel (activation rows = tokens x parts, above the CUDA-core kernel's 4).
+// Measured against the tcgen05 table's choice (graph-timed, without / with programmatic dependent launch): faster
+// while rows x N <= 160 K at up to 256 rows (N 1024, K 1024, M 125: 4.3 / 3.2 us against 6.7 / 4.6; N 4096,
+// K 1024, M 16: 3.8 / 2.8 against 6.6 / 4.9; three parts, N 1024, K 1024, M 38: 3.9 / 2.8 against 6.2 / 4.0) and on
+// narrow layers with long K (N 1024, K 4096, M 125: 6.9 / 5.8 against 7.8 / 6.7; three parts at M 126: 12.9 / 12.0
+// against 14.2 / 13.0) up to 128 rows, or 400 rows of three parts. Wider layers at M 125 (N 2048-4096, 6.7 /
+// 4.6-5.5 us on the tcgen05 kernels) stay there: their activation rows are re-read by N / 32 CTAs.
 bool reg_shape(int m, int n, int k, int parts) {
     const long long rows = (long long)m * parts;
     if (rows <= 256 && rows * n <= 160LL * 1024) return true;
