@@ -525,8 +525,9 @@ KeaGemmConfig narrow_mid_config(int m, int n, int k, int wbits, int sms) {
 // The register-operand kernel's tiles for a shape: tile_n channels x tile_m activation rows (tokens x parts) per CTA,
 // splits K-slices among its 8 warps. Measured (B200, graph-timed, 4 rotating weight sets): about 256 CTAs is best,
 // and of two tiles with the same count the one with more channels (fewer re-reads of the activation rows); 16 rows x
-// 32 channels is the base tile, 32 x 32 where it would exceed ~320 CTAs, 32 x 16 for 16 rows or fewer where it
-// would give fewer than ~160.
+// 32 channels is the base tile; where it would exceed ~320 CTAs, 16 x 64 on N >= 2048 (N 2048, M 125 in the clip:
+// 3.012 against 3.023 ms for 32 x 32) and 32 x 32 below; 32 x 16 for 16 rows or fewer where the base tile would give
+// fewer than ~160.
 KeaGemmConfig reg_config(int m, int n, int k, int parts, int sms) {
     (void)k;
     (void)sms;
@@ -538,8 +539,10 @@ KeaGemmConfig reg_config(int m, int n, int k, int parts, int sms) {
     c.stages = 0;
     const long long rows = (long long)m * parts;
     const long long ctas = (long long)ceil_div(n, 32) * ceil_div(m, 16 / parts);
-    if (ctas > 320) c.tile_m = 32;
-    else if (ctas < 160 && rows <= 16) {
+    if (ctas > 320) {
+        if (n >= 2048) c.tile_n = 64;
+        else c.tile_m = 32;
+    } else if (ctas < 160 && rows <= 16) {
         c.tile_m = 32;
         c.tile_n = 16;
     }
@@ -552,11 +555,15 @@ KeaGemmConfig reg_config(int m, int n, int k, int parts, int sms) {
 // while rows x N <= 160 K at up to 256 rows (N 1024, K 1024, M 125: 4.3 / 3.2 us against 6.7 / 4.6; N 4096,
 // K 1024, M 16: 3.8 / 2.8 against 6.6 / 4.9; three parts, N 1024, K 1024, M 38: 3.9 / 2.8 against 6.2 / 4.0) and on
 // narrow layers with long K (N 1024, K 4096, M 125: 6.9 / 5.8 against 7.8 / 6.7; three parts at M 126: 12.9 / 12.0
-// against 14.2 / 13.0) up to 128 rows, or 400 rows of three parts. Wider layers at M 125 (N 2048-4096, 6.7 /
-// 4.6-5.5 us on the tcgen05 kernels) stay there: their activation rows are re-read by N / 32 CTAs.
+// against 14.2 / 13.0) up to 128 rows, or 400 rows of three parts. N 2048, K 1024, M 125 (rows x N = 256 K) is
+// about even in a GEMM chain (5.9 / 4.9 us against 6.7 / 4.6) but faster in the config-2 clip, where the GEMM follows
+// its quantizer (whole clip 3.061 -> 3.012 ms), so rows x N <= 256 K is taken on N >= 2048, K <= 1024 too. Wider
+// layers at M 125 (N 3072-4096) stay on the tcgen05 kernels (the clip with them here: 3.108 ms): their activation
+// rows are re-read by N / 64 CTAs.
 bool reg_shape(int m, int n, int k, int parts) {
     const long long rows = (long long)m * parts;
     if (rows <= 256 && rows * n <= 160LL * 1024) return true;
+    if (n >= 2048 && k <= 1024 && rows * n <= 256LL * 1024) return true;
     return n <= 1024 && k >= 4096 && (rows <= 128 || (parts == 3 && rows <= 400));
 }
 

@@ -54,7 +54,7 @@ def test_every_shape_has_a_valid_config(n, k, wbits, parts):
             assert cfg.grid(m, n)[0] * cfg.tile_n >= n
             continue
         rows = m * parts   # the register kernel: up to 160 K output rows x channels, or narrow long-K layers
-        reg = (rows <= 256 and rows * n <= 160 * 1024) or (n <= 1024 and k >= 4096 and (rows <= 128 or (parts == 3 and rows <= 400)))
+        reg = (rows <= 256 and rows * n <= 160 * 1024) or (n >= 2048 and k <= 1024 and rows * n <= 256 * 1024) or (n <= 1024 and k >= 4096 and (rows <= 128 or (parts == 3 and rows <= 400)))
         assert (c.kernel == configs.REG) == reg
         if c.kernel == configs.REG:   # tile_m activation rows x tile_n channels per CTA, K-slices among 8 warps
             cfg = configs.choose(m, n, k, wbits, parts)
@@ -99,6 +99,10 @@ def test_small_m_splits_k_and_large_m_does_not():
     assert (c.kernel, c.tile_m, c.tile_n, c.splits) == (configs.REG, 16, 32, 8)
     c = _lib.choose_config(16, 4096, 1024, 1, 1)        # 16 channels x 32 rows: 256 CTAs
     assert (c.kernel, c.tile_m, c.tile_n, c.splits) == (configs.REG, 32, 16, 8)
+    c = _lib.choose_config(125, 2048, 1024, 1, 1)       # 64 channels x 16 tokens: 256 CTAs
+    assert (c.kernel, c.tile_m, c.tile_n, c.splits) == (configs.REG, 16, 64, 8)
+    c = _lib.choose_config(125, 3072, 1024, 1, 1)       # wider: the tcgen05 per-tile kernel
+    assert c.kernel == configs.PER_TILE
     c = _lib.choose_config(378, 1024, 4096, 1, 1)       # one part past 128 rows: the tcgen05 table
     assert c.kernel != configs.REG
     c = _lib.choose_config(126, 1024, 4096, 1, 3)       # 378 rows of three parts: 32 rows x 32 channels
