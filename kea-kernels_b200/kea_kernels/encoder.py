@@ -47,6 +47,7 @@ class LowBitLinear(nn.Module):
         super().__init__()
         n = codes.shape[0]
         self.in_features, self.out_features, self.wbits, self.parts, self.pdl = in_features, n, wbits, parts, pdl
+        self.quant_pdl = False   # launch this projection's quantizer with programmatic dependent launch
         self.panels = lowbit.prepare_panels(codes.to(device), wbits, n, in_features)
         self.scale = scale.to(device=device, dtype=torch.float32).contiguous()
         self.bias = None if bias is None else bias.to(device=device, dtype=torch.float32).contiguous()
@@ -65,14 +66,17 @@ class LowBitLinear(nn.Module):
         if m == 0:
             return y
         # one call: the library runs the quantizer inside the GEMM kernel where the shape allows, else the two
-        # kernels back to back (the quantizer launched plainly: with programmatic dependent launch its CTAs would
-        # sit on the SMs while the previous GEMM drains, measured slower on the clip; the GEMM after it does use it)
+        # kernels back to back. The quantizer is launched plainly unless `quant_pdl` is set: with programmatic
+        # dependent launch its CTAs sit on the SMs while the previous kernel drains, which measured slower on the
+        # clip after most kernels (3.234 -> 3.371 ms per clip with every quantizer so launched) but faster after the
+        # FF up projections' one-CTA-per-SM GEMMs (3.234 -> 3.209 ms with the FF down quantizers alone); the GEMM
+        # after a quantizer always uses it
         res = None if residual is None else residual.reshape(m, self.out_features)
         lowbit.project(x, (x.stride(0), x.stride(1), x.stride(2), t), m, k, self.panels, self.wbits,
                        self.out_features, self.scale, self.bias, y.view(m, self.out_features), parts=self.parts,
                        norm=norm, input_silu=input_silu, pre_norm=pre_norm,
                        normed=None if normed is None else normed.view(m, k), silu=silu, pdl=self.pdl, residual=res,
-                       residual_scale=residual_scale)
+                       residual_scale=residual_scale, quant_pdl=self.pdl and self.quant_pdl)
         return y
 
     def from_quantized(self, q: Tensor, qs: Tensor, ldq: int, b: int, t: int, *, silu: bool = False,
@@ -179,6 +183,8 @@ class ConformerLayer(nn.Module):
             bias = rnd(n) * 0.02 if name != "linear_pos" else None
             self.weights[name] = (w, bias)
             self.lin[name] = LowBitLinear(w.codes, wbits, w.scale, bias, k, parts=parts, device=device, pdl=pdl)
+        for name in ("ff1_down", "ff2_down"):   # their quantizers follow the FF up GEMMs: launched early (forward)
+            self.lin[name].quant_pdl = True
         self.norms = nn.ModuleDict({n: nn.LayerNorm(d) for n in ("ff1", "att", "conv", "ff2", "out")}).to(device)
         with torch.no_grad():
             for norm in self.norms.values():
