@@ -130,9 +130,9 @@ typedef struct KeaGemmDesc {
                                  (same bits). kea_lowbit_workspace_bytes says how much a shape uses; with less (or
                                  NULL) the GEMM runs unsplit. Calls sharing a workspace must not overlap on the GPU. */
     int64_t workspace_bytes;
-    int64_t wait_clocks;      /* 0: the library's bound on a kernel's wait (4e9 SM clocks, about 2 s); else the SM clocks
-                                 one wait of the small-M kernel may last before it gives up, reports KEA_DEVERR_TIMEOUT
-                                 in the error word and returns (the context stays usable) */
+    int64_t wait_clocks;      /* 0: the library's bound on a kernel's wait (4e9 SM clocks, about 2 s); else the SM
+                                 clocks one wait of the swapped-operand kernel may last before it gives up, reports
+                                 KEA_DEVERR_TIMEOUT in the error word and returns (the context stays usable) */
 } KeaGemmDesc;
 
 /* Tile configuration picked for a shape (the M-bucketed split-K dispatch table). */
