@@ -4,30 +4,33 @@
 // With a few dozen to a hundred tokens a launch is latency-bound, and the tcgen05 kernels' fixed costs dominate it:
 // tensor-memory allocation, mbarrier set-up, a TMA round trip for a whole 128-row activation block per CTA, the
 // weight tile expanded into shared memory behind an async-proxy fence, and a chain of issue-paced MMAs from one
-// thread. Here nothing is staged: every warp loads its operands straight from global memory into registers, several
-// k-steps ahead, and issues its own MMAs.
+// thread. Here nothing is staged: every warp loads its operands straight from global memory into registers, a few
+// double steps ahead, and issues its own MMAs.
 //
 // Operands. The weights are the MMA's A operand (16 channels x 32 k), the tokens its B operand (32 k x 8 rows). An
 // integer dot product does not depend on the order of its K terms as long as both operands use the same order, so
-// the 32 columns of a k-step are ordered to suit the panels: lane (g, t) (g = lane / 4, t = lane % 4) holds codes
-// 8t .. 8t+3 of its channel's k-step in its first A register of that row and codes 8t+4 .. 8t+7 in its second, and
-// bytes 8t .. 8t+7 of its token row in its two B registers (one 8-byte load). With the PTX fragment layout
+// k is walked in double steps of 64 (two MMAs) ordered to suit the panels and 16-byte loads: lane (g, t) (g = lane /
+// 4, t = lane % 4) holds codes 16t .. 16t+15 of its channel's double step and bytes 16t .. 16t+15 of its token row
+// (one 16-byte load); MMA h (0, 1) of the double step takes codes / bytes 16t + 8h .. 16t + 8h + 7, the first four in
+// its first A register of that row and first B register, the next four in the second. With the PTX fragment layout
 // (A: registers 0 / 2 = row g at logical columns 4t .. 4t+3 / 16+4t .. 16+4t+3, registers 1 / 3 = row g + 8;
-// B: registers 0 / 1 = logical rows 4t .. 4t+3 / 16+4t .. 16+4t+3 of column g) logical column 4t + i is k-step
-// column 8t + i and 16 + 4t + i is 8t + 4 + i, for both operands. In the panels, 1-bit word s of a channel row holds
-// the k-step's 32 codes with code c at bit 4 (c % 8) + c / 8, so codes 8t .. 8t+7 are the nibbles of
-// (word >> t) & 0x11111111; a 2-bit k-step spans words 2s (codes 0-15) and 2s + 1 (16-31) with field i at bits
-// 4 (i % 8) + 2 (i / 8), so codes 8t .. 8t+7 are the nibbles of (word_{2s + t/2} >> 2 (t % 2)) & 0x33333333. Either
-// way two byte-permute lookups expand them (the tcgen05 expanders' tables).
+// B: registers 0 / 1 = logical rows 4t .. 4t+3 / 16+4t .. 16+4t+3 of column g) logical column 4t + i of MMA h is
+// k = 16t + 8h + i of the double step and 16 + 4t + i is 16t + 8h + 4 + i, for both operands. In the panels, 1-bit
+// word w of a channel row holds codes 32w .. 32w+31 with code c at bit 4 (c % 8) + c / 8 (c within the word), so
+// this lane's codes of double step s lie in word 2s + t/2 and those of MMA h are the nibbles of
+// (word >> (2 (t % 2) + h)) & 0x11111111; a 2-bit word holds 16 codes with field f at bits 4 (f % 8) + 2 (f / 8), so
+// the lane's codes are word 4s + t and those of MMA h the nibbles of (word >> 2h) & 0x33333333. Either way two
+// byte-permute lookups per register pair expand them (the tcgen05 expanders' tables).
 //
 // Work split. A CTA owns CN consecutive channels x TT tokens (all parts of those tokens: rows r = p * TT + token,
 // R = 8 * RG rows). Its 8 warps are KS K-slices x (8 / KS) channel groups: a warp computes 16 * CG channels x all R
-// rows over its slice of the k-steps, CG x RG MMA tiles per k-step with INT32 accumulators in registers. Its loads
-// run D k-steps ahead of its MMAs (a ring of D register sets; a slot is refilled right after its k-step is used).
-// The weights do not depend on the previous kernel of the stream, so the ring's first weight loads are issued before
-// griddepcontrol.wait (programmatic dependent launch overlaps them with that kernel's tail). The K-slices' partial
-// sums meet in shared memory ([slice][row][channel], rows padded by 4 words so the fragment stores do not collide)
-// and every thread sums them in slice order (exact INT32: the order cannot change the result) and finishes
+// rows over its slice of the double steps, 2 x CG x RG MMAs per double step with INT32 accumulators in registers.
+// Its loads run D double steps ahead of its MMAs (a ring of D register sets; a slot is refilled right after its double
+// step is used). The weights do not depend on the previous kernel of the stream, so the ring's first weight loads are
+// issued before griddepcontrol.wait (programmatic dependent launch overlaps them with that kernel's tail); the
+// activations, which that kernel may still be writing, are read with ordinary loads after the wait. The K-slices'
+// partial sums meet in shared memory ([slice][row][channel], rows padded by 4 words so the fragment stores do not
+// collide) and every thread sums them in slice order (exact INT32: the order cannot change the result) and finishes
 // (token, channel) outputs with the tensor-core kernels' finish_value, so the outputs equal theirs bit for bit.
 #pragma once
 
