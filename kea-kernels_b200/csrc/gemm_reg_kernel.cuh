@@ -140,7 +140,8 @@ __global__ void __launch_bounds__(kRegThreads, 2) lowbit_gemm_reg_kernel(const R
         const bool live = s < s1 && 64 * s + 16 * t < a.K;
 #pragma unroll
         for (int rg = 0; rg < RG; ++rg)
-            br[d][rg] = (live && qrow[rg]) ? *reinterpret_cast<const uint4 *>(qrow[rg] + 64 * s) : make_uint4(0u, 0u, 0u, 0u);
+            br[d][rg] = (live && qrow[rg]) ? *reinterpret_cast<const uint4 *>(qrow[rg] + 64 * s)
+                                           : make_uint4(0u, 0u, 0u, 0u);
     }
 
     int acc[CG][RG][4];
