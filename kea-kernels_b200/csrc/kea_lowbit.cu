@@ -693,7 +693,7 @@ struct RegPlan {
 // The instantiated warp tiles (cg channel groups x rg row groups): 16 x cg channels x 8 x rg rows per warp.
 bool reg_tile_ok(int cg, int rg) { return (cg == 1 && rg == 4) || (cg == 2 && (rg == 4 || rg == 2)) || (cg == 4 && rg == 2); }
 
-bool reg_plan(int parts, int cn, int rows, int ks, RegPlan *p) {
+bool reg_plan(int m, int parts, int cn, int rows, int ks, RegPlan *p) {
     if (ks != 1 && ks != 2 && ks != 4 && ks != 8) return false;
     if (cn != 16 && cn != 32 && cn != 64 && cn != 128) return false;   // divides the 128-row panel tile
     if (rows != 16 && rows != 32) return false;
@@ -701,6 +701,7 @@ bool reg_plan(int parts, int cn, int rows, int ks, RegPlan *p) {
     if (cn % (16 * cw)) return false;
     const int cg = cn / (16 * cw), rg = rows / 8;
     if (!reg_tile_ok(cg, rg) || rows / parts < 1) return false;
+    if (ceil_div(m, rows / parts) > 65535) return false;   // token tiles are the grid's y dimension
     p->cg = cg;
     p->rg = rg;
     p->ks = ks;
@@ -960,7 +961,7 @@ int route_gemm(const KeaGemmDesc *d, int sms, Route *route, KeaGemmConfig *c, Sw
     const bool forced = d->tile_m || d->tile_n || d->splits || d->stages;
     if (d->flags & KEA_FLAG_FORCE_REG) {   // channels / rows / K-slices (0: the table's) apply to the register kernel
         const KeaGemmConfig t = reg_config(d->m, d->n, d->k, d->parts, sms);
-        if (!reg_plan(d->parts, d->tile_n ? d->tile_n : t.tile_n, d->tile_m ? d->tile_m : t.tile_m,
+        if (!reg_plan(d->m, d->parts, d->tile_n ? d->tile_n : t.tile_n, d->tile_m ? d->tile_m : t.tile_m,
                       d->splits ? d->splits : t.splits, rp))
             return KEA_ERR_UNSUPPORTED;
         *route = kRouteReg;
@@ -994,7 +995,7 @@ int route_gemm(const KeaGemmDesc *d, int sms, Route *route, KeaGemmConfig *c, Sw
         return KEA_OK;
     }
     if (!forced && c->kernel == 4 && !(d->flags & KEA_FLAG_NO_REG) &&
-        reg_plan(d->parts, c->tile_n, c->tile_m, c->splits, rp)) {
+        reg_plan(d->m, d->parts, c->tile_n, c->tile_m, c->splits, rp)) {
         *route = kRouteReg;
         return KEA_OK;
     }

@@ -142,4 +142,13 @@ def test_forced_config_errors():
     for bad in [(32, 48, 8), (24, 32, 8), (32, 32, 3), (32, 256, 8), (16, 16, 8), (32, 64, 8), (16, 128, 8)]:
         with pytest.raises((ValueError, RuntimeError)):
             _run(codes, wbits, n, k, q, qs, alpha, None, config=_reg(*bad))
+    # more token tiles than a grid's y dimension holds (65535 x 16 tokens)
+    m = 65535 * 16 + 1
+    qd = torch.zeros(1, m, k, dtype=torch.int8, device=DEV)
+    qsd = torch.ones(1, m, device=DEV)
+    panels = lowbit.prepare_panels(torch.from_numpy(codes).to(DEV), wbits, n, k)
+    y = torch.empty(m, n, device=DEV)
+    with pytest.raises((ValueError, RuntimeError)):
+        lowbit.gemm(qd, qsd, k, m, panels, wbits, n, k, torch.from_numpy(alpha).to(DEV), None, y, parts=1,
+                    config=_reg(16, 32, 8))
     assert _lib.read_device_error() == 0
