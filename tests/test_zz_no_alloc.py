@@ -5,7 +5,7 @@ static 16 MiB device buffer instead of a caller's workspace.
 
 Called through the C ABI and checked against kea_lowbit_gemm (the existing entry point, with a workspace it is
 given) on two calls in a row - bit for bit, the tolerance of the other GEMM parity tests without SiLU - at a shape
-that splits K through the scratch and at one that does not; two split calls back to back on one stream (programmatic
+that splits K through the scratch and at two that do not (a tcgen05 and a register-operand route); two split calls back to back on one stream (programmatic
 dependent launch, FP32 output with a residual) against the unsplit GEMM and the oracle; and a shape whose split would
 need more than the buffer is refused. This file is collected last, so a run that stops at the first failure has run every other test first.
 """
@@ -50,7 +50,7 @@ def _noalloc(panels, q, qs, alpha, bias, n, k, m, parts, y, acc, flags=0, residu
         return _lib.lib().kea_lowbit_gemm_noalloc(ctypes.byref(d), _lib.stream_handle(y.device))
 
 
-@pytest.mark.parametrize("n,k,m", [(2048, 4096, 384), (4096, 1024, 125)])
+@pytest.mark.parametrize("n,k,m", [(2048, 4096, 384), (4096, 1024, 125), (1024, 1024, 125)])
 def test_noalloc_gemm_equals_gemm_on_two_calls(n, k, m):
     splits = _lib.workspace_bytes(m, n, k, 1, 1) > 0
     assert splits == (m == 384)                        # the first shape goes through the static scratch
